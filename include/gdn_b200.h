@@ -1,0 +1,113 @@
+/*
+ * gdn_b200.h -- C ABI of the B200 (sm_100a) Gated DeltaNet kernel pair for the
+ * fixed geometry qk4_v8_d128_k_last:
+ *   4 q/k heads, 8 v heads (v-head h reads q/k head h/2), head dim 128,
+ *   recurrent state k-last fp32 [N, 8, 128 (v), 128 (k)].
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream (cudaStream_t passed as void*, NULL = legacy default stream).  Calls
+ * are asynchronous on that stream, never synchronise the host, never
+ * allocate, and return a gdn_status_t.  Tensors are dense row-major
+ * (contiguous); bf16 tensors are passed as raw 16-bit storage.
+ *
+ * The library is built from track-c-gdn_b200/csrc/ by __graft_entry__.build()
+ * into track-c-gdn_b200/libgdn_b200.so.
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  GDN_OK = 0,
+  GDN_ERR_NULL_POINTER = 1,   /* a required pointer is NULL */
+  GDN_ERR_BAD_SIZE = 2,       /* negative / inconsistent sizes */
+  GDN_ERR_MISALIGNED = 3,     /* a pointer violates the documented alignment */
+  GDN_ERR_WORKSPACE = 4,      /* workspace missing or smaller than required */
+  GDN_ERR_LAUNCH = 5,         /* the CUDA launch itself failed */
+  GDN_ERR_DEVICE = 6,         /* no sm_100 device / wrong device */
+  GDN_ERR_ALIASING = 7        /* outputs overlap inputs where not allowed */
+} gdn_status_t;
+
+/* ABI version of this header (bumped on any signature change). */
+int gdn_b200_abi_version(void);
+
+/* Human-readable text for a gdn_status_t. */
+const char *gdn_b200_status_string(int status);
+
+/*
+ * Device-side status word.  Kernels never trap: when one meets an
+ * inconsistency it cannot report synchronously (cu_seqlens that do not match
+ * total_tokens, a bounded wait that ran out) it records a nonzero code in a
+ * per-device word and skips the work.  This call copies the word for the
+ * current device into *code (stream-ordered, then synchronises `stream`) and
+ * clears it.  Codes: 0 none, 1 bad cu_seqlens, 2 wait timeout.
+ */
+int gdn_b200_read_device_status(int *code, void *stream);
+
+/*
+ * Decode step.  Replaces the reference entry point
+ *   run(q, k, v, state, A_log, a, dt_bias, b, scale)
+ *   gdn_decode_qk4_v8_d128_k_last/solution/triton/kernel.py:100-146
+ * q, k      [B,1,4,128] bf16 (8-byte aligned)
+ * v         [B,1,8,128] bf16 (8-byte aligned)
+ * state     [B,8,128,128] fp32 (16-byte aligned) or NULL for a zero state
+ *           (kernel.py:86-94)
+ * A_log     [8] fp32;  dt_bias [8] fp32
+ * a, b      [B,1,8] bf16
+ * scale     0.0f selects 1/sqrt(128) (kernel.py:112-115)
+ * out       [B,1,8,128] bf16 (8-byte aligned)
+ * new_state [B,8,128,128] fp32 (16-byte aligned).  May equal `state` (update
+ *           in place); must not partially overlap it.
+ * Per (request, v-head) it computes g = exp(-exp(A_log) softplus(a+dt_bias))
+ * (softplus threshold 20), beta = sigmoid(b), S <- g S,
+ * S <- S + beta (v - S k) k^T, out = S (scale q)   (kernel.py:26-79).
+ */
+int gdn_decode_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                  const float *state, const float *A_log,
+                                  const void *a, const float *dt_bias,
+                                  const void *b, float scale, int64_t batch,
+                                  void *out, float *new_state, void *stream);
+
+/*
+ * Workspace (bytes) the prefill needs for `total_tokens` tokens packed into
+ * `num_seqs` sequences.  Independent of the sequence lengths.
+ */
+size_t gdn_prefill_workspace_bytes(int64_t total_tokens, int64_t num_seqs);
+
+/*
+ * Chunked (64-token) prefill over ragged sequences.  Replaces the reference
+ * entry point
+ *   run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+ *   solution/triton/kernel.py:1762-1802
+ * q, k        [T,4,128] bf16 (16-byte aligned)
+ * v           [T,8,128] bf16 (16-byte aligned)
+ * state       [N,8,128,128] fp32 initial states, or NULL for zeros
+ * A_log, dt_bias [8] fp32;  a, b [T,8] bf16
+ * cu_seqlens  [N+1] int64 on the device, cu_seqlens[0] = 0,
+ *             non-decreasing, cu_seqlens[N] = T (checked on the device; a
+ *             violation sets device status 1 and leaves outputs unwritten)
+ * scale       0.0f selects 1/sqrt(128)
+ * out         [T,8,128] bf16 (16-byte aligned)
+ * final_state [N,8,128,128] fp32; may equal `state` (in place)
+ * workspace   >= gdn_prefill_workspace_bytes(T, N) bytes, 1024-byte aligned
+ * No host synchronisation: unlike the reference (kernel.py:1665, :181-184)
+ * the chunk metadata is built on the device.
+ */
+int gdn_prefill_qk4_v8_d128_k_last(
+    const void *q, const void *k, const void *v, const float *state,
+    const float *A_log, const void *a, const float *dt_bias, const void *b,
+    const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+    float scale, void *out, float *final_state, void *workspace,
+    size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

@@ -1,0 +1,88 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, and rejects bad arguments before touching the device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "gdn_b200.h"
+
+
+def header_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gdn_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_expected_entry_points():
+    names = header_functions()
+    for n in ("gdn_decode_qk4_v8_d128_k_last", "gdn_prefill_qk4_v8_d128_k_last",
+              "gdn_prefill_workspace_bytes", "gdn_b200_status_string",
+              "gdn_b200_abi_version", "gdn_b200_read_device_status"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(gdn):
+    lib = ctypes.CDLL(str(gdn._native.LIB_PATH))
+    for name in header_functions():
+        assert hasattr(lib, name), f"libgdn_b200.so does not export {name}"
+    # and the Python binding covers each of them
+    assert set(header_functions()) == set(gdn._native.SIGNATURES)
+
+
+def test_status_strings(gdn):
+    lib = gdn._native.lib
+    assert lib.gdn_b200_abi_version() == 1
+    for code in range(8):
+        assert lib.gdn_b200_status_string(code)
+    assert lib.gdn_b200_status_string(0) == b"ok"
+
+
+def test_workspace_size_monotone(gdn):
+    ws = gdn.prefill.workspace_bytes
+    assert ws(0, 1) > 0
+    assert ws(4096, 1) < ws(8192, 1) < ws(8192, 32)
+    # 16 KiB [PA;Ainv] image per (chunk, v-head) dominates: ~2 KiB per token
+    assert 2048 * 4096 < ws(4096, 1) < 2048 * 4096 * 1.2
+
+
+def test_argument_validation_without_device(gdn):
+    lib = gdn._native.lib
+    P = ctypes.c_void_p
+    ok = P(0x10000)
+    # decode: NULL pointers, negative batch, misalignment
+    assert lib.gdn_decode_qk4_v8_d128_k_last(None, ok, ok, None, ok, ok, ok, ok, 0.0, 4, ok, ok, None) == 1
+    assert lib.gdn_decode_qk4_v8_d128_k_last(ok, ok, ok, None, ok, ok, ok, ok, 0.0, -1, ok, ok, None) == 2
+    assert lib.gdn_decode_qk4_v8_d128_k_last(ok, ok, ok, None, ok, ok, ok, ok, 0.0, 0, ok, ok, None) == 0
+    assert lib.gdn_decode_qk4_v8_d128_k_last(P(0x10004), ok, ok, None, ok, ok, ok, ok, 0.0, 4, ok, ok, None) == 3
+    # decode: new_state partially overlapping state
+    assert lib.gdn_decode_qk4_v8_d128_k_last(ok, ok, ok, P(0x100000), ok, ok, ok, ok, 0.0, 4, ok,
+                                             P(0x100000 + 4096), None) == 7
+    # prefill: workspace too small / misaligned, NULL cu_seqlens
+    args = [ok, ok, ok, None, ok, ok, ok, ok, ok, 2, 128, 0.0, ok, ok]
+    assert lib.gdn_prefill_qk4_v8_d128_k_last(*args, ok, 16, None) == 4
+    assert lib.gdn_prefill_qk4_v8_d128_k_last(*args, P(0x10010), 1 << 30, None) == 4
+    bad = list(args)
+    bad[8] = None
+    assert lib.gdn_prefill_qk4_v8_d128_k_last(*bad, ok, 1 << 30, None) == 1
+    assert lib.gdn_prefill_qk4_v8_d128_k_last(*args[:9], -1, 128, *args[11:], ok, 1 << 30, None) == 2
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
+def test_no_device_is_reported_not_crashed(gdn):
+    lib = gdn._native.lib
+    ok = ctypes.c_void_p(0x10000)
+    st = lib.gdn_decode_qk4_v8_d128_k_last(ok, ok, ok, None, ok, ok, ok, ok, 0.0, 4, ok,
+                                           ctypes.c_void_p(0x20000000), None)
+    assert st == 6  # GDN_ERR_DEVICE
+
+
+def test_reference_signatures_preserved(gdn):
+    import inspect
+    assert list(inspect.signature(gdn.decode.run).parameters) == [
+        "q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "scale"]
+    assert list(inspect.signature(gdn.prefill.run).parameters) == [
+        "q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens", "scale"]

@@ -1,0 +1,110 @@
+"""Decode parity on the GPU: the sm_100a kernel (through the C ABI) against the
+reference's golden vectors and the CPU oracle.
+
+Tolerances (stated per the BASELINE contract): outputs are bf16, compared
+after rounding with |d| <= 2e-3 + 1e-2 |ref| (and within one bf16 ulp of the
+reference's own output); the fp32 state must agree with the fp32 oracle to
+<= 1e-5 relative Frobenius (both are fp32 evaluations of the same step).
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import golden_io
+import oracle
+from gpu_util import decode_args, out_err, rel_fro
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _clean_status(gdn):
+    gdn._native.read_device_status()
+    yield
+    assert gdn._native.read_device_status() == 0
+
+
+@pytest.mark.parametrize("name", golden_io.names("decode"))
+def test_decode_matches_reference_golden(gdn, name):
+    kind, inp, scale, z = golden_io.load(name)
+    o, s = gdn.decode.run(*decode_args(inp), scale)
+    torch.cuda.synchronize()
+    e_out, omax, e_proj, e_sl = golden_io.compare(z, o.float().cpu().numpy(), s.cpu().numpy())
+    assert e_out <= max(omax, 1e-3) * 2.0 ** -7, (e_out, omax)
+    assert e_proj < 1e-5 and e_sl < 1e-5, (e_proj, e_sl)
+
+
+@pytest.mark.parametrize("B", [1, 8, 64, 256])
+def test_decode_matches_oracle(gdn, B):
+    inp = cases.decode_inputs(seed=100 + B, B=B)
+    o, s = gdn.decode.run(*decode_args(inp), None)
+    ro, rs = oracle.decode(inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"],
+                           inp["dt_bias"], inp["b"])
+    assert out_err(o, ro) <= 1.0
+    assert rel_fro(s.cpu().numpy(), rs) < 1e-5
+
+
+def test_decode_inplace_equals_out_of_place(gdn):
+    inp = cases.decode_inputs(seed=7, B=33)
+    args = decode_args(inp)
+    o1, s1 = gdn.decode.run(*args, 0.3)
+    st = args[3].clone()
+    o2 = gdn.decode.run_inplace(args[0], args[1], args[2], st, *args[4:], 0.3)
+    assert torch.equal(o1, o2)
+    assert torch.equal(s1, st)
+    # the value-returning form leaves its input state untouched
+    assert torch.equal(args[3], decode_args(inp)[3])
+
+
+def test_decode_none_state_equals_zero_state(gdn):
+    inp = cases.decode_inputs(seed=8, B=5)
+    args = list(decode_args(inp))
+    zero = torch.zeros_like(args[3])
+    o1, s1 = gdn.decode.run(*args[:3], None, *args[4:], None)
+    o2, s2 = gdn.decode.run(*args[:3], zero, *args[4:], None)
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+
+
+def test_decode_batch_1024_consistency(gdn):
+    """Full sweep size (B=1024): in-place == out-of-place bit for bit, and a
+    sample of requests matches the oracle."""
+    inp = cases.decode_inputs(seed=9, B=1024)
+    args = decode_args(inp)
+    o1, s1 = gdn.decode.run(*args, None)
+    st = args[3].clone()
+    o2 = gdn.decode.run_inplace(args[0], args[1], args[2], st, *args[4:], None)
+    assert torch.equal(o1, o2) and torch.equal(s1, st)
+    idx = np.array([0, 1, 511, 777, 1023])
+    sub = {k: (v[idx] if (v is not None and k not in ("A_log", "dt_bias")) else v)
+           for k, v in inp.items()}
+    ro, rs = oracle.decode(sub["q"], sub["k"], sub["v"], sub["state"], sub["A_log"], sub["a"],
+                           sub["dt_bias"], sub["b"])
+    assert out_err(o1[idx], ro) <= 1.0
+    assert rel_fro(s1[idx].cpu().numpy(), rs) < 1e-5
+
+
+def test_decode_repeated_steps_track_oracle(gdn):
+    """Eight consecutive in-place steps stay on the oracle's trajectory."""
+    B = 4
+    inp = cases.decode_inputs(seed=10, B=B)
+    st_dev = decode_args(inp)[3].clone()
+    st_ref = inp["state"].copy()
+    for step in range(8):
+        step_inp = cases.decode_inputs(seed=1000 + step, B=B)
+        step_inp["A_log"], step_inp["dt_bias"] = inp["A_log"], inp["dt_bias"]
+        args = decode_args(step_inp)
+        o = gdn.decode.run_inplace(args[0], args[1], args[2], st_dev, *args[4:], None)
+        ro, st_ref = oracle.decode(step_inp["q"], step_inp["k"], step_inp["v"], st_ref,
+                                   step_inp["A_log"], step_inp["a"], step_inp["dt_bias"],
+                                   step_inp["b"])
+        assert out_err(o, ro) <= 1.0
+    assert rel_fro(st_dev.cpu().numpy(), st_ref) < 1e-5
+
+
+def test_decode_rejects_wrong_dtype(gdn):
+    inp = cases.decode_inputs(seed=11, B=2)
+    args = list(decode_args(inp))
+    args[0] = args[0].float()
+    with pytest.raises(TypeError):
+        gdn.decode.run(*args, None)

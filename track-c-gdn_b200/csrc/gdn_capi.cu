@@ -1,0 +1,151 @@
+// gdn_capi.cu -- extern "C" entry points declared in include/gdn_b200.h.
+//
+// Host-side checks mirror the reference's own asserts (decode kernel.py:117-120,
+// prefill kernel.py:1635-1667) as far as they can be made without touching
+// device memory; the one check that needs device data (cu_seqlens[-1] == T,
+// kernel.py:1665) runs on the device (device status 1) so no call ever
+// synchronises the host.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+
+#include "../../include/gdn_b200.h"
+#include "gdn_common.cuh"
+
+namespace gdn {
+cudaError_t launch_decode(const void *q, const void *k, const void *v, const float *state,
+                          const float *A_log, const void *a, const float *dt_bias,
+                          const void *b, float scale, int64_t batch, void *out,
+                          float *new_state, cudaStream_t stream);
+size_t prefill_workspace_bytes(int64_t T, int64_t N);
+cudaError_t launch_prefill(const void *q, const void *k, const void *v, const float *state,
+                           const float *A_log, const void *a, const float *dt_bias, const void *b,
+                           const int64_t *cu_seqlens, int64_t N, int64_t T, float scale,
+                           void *out, float *final_state, void *workspace, int num_sms,
+                           cudaStream_t stream);
+}  // namespace gdn
+
+namespace {
+
+constexpr float kDefaultScale = 0.08838834764831845f;  // 1/sqrt(128)
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+bool overlap(const void *a, size_t na, const void *b, size_t nb) {
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + nb && y < x + na;
+}
+
+// Current device must be sm_100 (B200 family); cached per device ordinal.
+int check_device(int *num_sms) {
+  static int cached_dev = -1, cached_ok = 0, cached_sms = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_DEVICE;
+  if (dev != cached_dev) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return GDN_ERR_DEVICE;
+    cached_ok = prop.major == 10 && prop.minor == 0;
+    cached_sms = prop.multiProcessorCount;
+    cached_dev = dev;
+  }
+  if (num_sms) *num_sms = cached_sms;
+  return cached_ok ? GDN_OK : GDN_ERR_DEVICE;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn_b200_abi_version(void) { return 1; }
+
+const char *gdn_b200_status_string(int status) {
+  switch (status) {
+    case GDN_OK: return "ok";
+    case GDN_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case GDN_ERR_BAD_SIZE: return "negative or inconsistent sizes";
+    case GDN_ERR_MISALIGNED: return "a pointer violates the documented alignment";
+    case GDN_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case GDN_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case GDN_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    case GDN_ERR_ALIASING: return "an output partially overlaps an input";
+    default: return "unknown status";
+  }
+}
+
+int gdn_b200_read_device_status(int *code, void *stream) {
+  if (code == nullptr) return GDN_ERR_NULL_POINTER;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int zero = 0;
+  if (cudaMemcpyFromSymbolAsync(code, gdn::g_device_status, sizeof(int), 0,
+                                cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return GDN_ERR_LAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return GDN_ERR_LAUNCH;
+  if (cudaMemcpyToSymbolAsync(gdn::g_device_status, &zero, sizeof(int), 0,
+                              cudaMemcpyHostToDevice, s) != cudaSuccess)
+    return GDN_ERR_LAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return GDN_ERR_LAUNCH;
+  return GDN_OK;
+}
+
+int gdn_decode_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                  const float *state, const float *A_log, const void *a,
+                                  const float *dt_bias, const void *b, float scale,
+                                  int64_t batch, void *out, float *new_state, void *stream) {
+  if (batch < 0 || batch > (int64_t{1} << 26)) return GDN_ERR_BAD_SIZE;
+  if (batch == 0) return GDN_OK;
+  if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !out || !new_state)
+    return GDN_ERR_NULL_POINTER;
+  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(v, 8) || !aligned(out, 8) ||
+      !aligned(new_state, 16) || (state && !aligned(state, 16)) || !aligned(a, 2) ||
+      !aligned(b, 2) || !aligned(A_log, 4) || !aligned(dt_bias, 4))
+    return GDN_ERR_MISALIGNED;
+  const size_t state_bytes = static_cast<size_t>(batch) * gdn::kHV * gdn::kD * gdn::kD * 4;
+  if (state && state != new_state && overlap(state, state_bytes, new_state, state_bytes))
+    return GDN_ERR_ALIASING;
+  int sms = 0;
+  if (int st = check_device(&sms)) return st;
+  if (scale == 0.0f) scale = kDefaultScale;
+  cudaError_t err = gdn::launch_decode(q, k, v, state, A_log, a, dt_bias, b, scale, batch, out,
+                                       new_state, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+size_t gdn_prefill_workspace_bytes(int64_t total_tokens, int64_t num_seqs) {
+  if (total_tokens < 0 || num_seqs < 0) return 0;
+  return gdn::prefill_workspace_bytes(total_tokens, num_seqs);
+}
+
+int gdn_prefill_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                   const float *state, const float *A_log, const void *a,
+                                   const float *dt_bias, const void *b,
+                                   const int64_t *cu_seqlens, int64_t num_seqs,
+                                   int64_t total_tokens, float scale, void *out,
+                                   float *final_state, void *workspace, size_t workspace_bytes,
+                                   void *stream) {
+  if (num_seqs < 0 || total_tokens < 0 || total_tokens > (int64_t{1} << 31) ||
+      num_seqs > (int64_t{1} << 24))
+    return GDN_ERR_BAD_SIZE;
+  if (num_seqs == 0) return total_tokens == 0 ? GDN_OK : GDN_ERR_BAD_SIZE;
+  if (!cu_seqlens || !A_log || !dt_bias || !final_state || !workspace) return GDN_ERR_NULL_POINTER;
+  if (total_tokens > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL_POINTER;
+  if ((q && !aligned(q, 16)) || (k && !aligned(k, 16)) || (v && !aligned(v, 16)) ||
+      (out && !aligned(out, 16)) || !aligned(final_state, 4) || (state && !aligned(state, 4)) ||
+      !aligned(cu_seqlens, 8))
+    return GDN_ERR_MISALIGNED;
+  if (!aligned(workspace, 1024) ||
+      workspace_bytes < gdn::prefill_workspace_bytes(total_tokens, num_seqs))
+    return GDN_ERR_WORKSPACE;
+  const size_t state_bytes = static_cast<size_t>(num_seqs) * gdn::kHV * gdn::kD * gdn::kD * 4;
+  if (state && state != final_state && overlap(state, state_bytes, final_state, state_bytes))
+    return GDN_ERR_ALIASING;
+  int sms = 0;
+  if (int st = check_device(&sms)) return st;
+  if (scale == 0.0f) scale = kDefaultScale;
+  cudaError_t err = gdn::launch_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
+                                        total_tokens, scale, out, final_state, workspace, sms,
+                                        static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+}  // extern "C"

@@ -1,0 +1,93 @@
+"""GDN decode (qk4_v8_d128_k_last): drop-in for the reference decode solution.
+
+`run` keeps the reference signature, argument meaning, defaults and error
+behaviour of `run` in gdn_decode_qk4_v8_d128_k_last/solution/triton/kernel.py
+(lines 100-146 of the reference project): value-returning, a fresh
+`new_state` buffer (the input state is not modified), `scale` None or 0 ->
+1/sqrt(128), `state` None -> zero state, shape asserts on q/k/v.  The work is
+one launch of the sm_100a kernel in libgdn_b200.so on the current stream.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _native
+
+HQ = 4
+HV = 8
+D = 128
+
+
+def _scale(scale) -> float:
+    # kernel.py:112-115
+    if scale is None or float(scale) == 0.0:
+        return 1.0 / math.sqrt(D)
+    return float(scale)
+
+
+def _check_inputs(q, k, v, a, b):
+    # kernel.py:117-120
+    assert q.shape[1:] == (1, HQ, D)
+    assert k.shape[1:] == (1, HQ, D)
+    assert v.shape[1:] == (1, HV, D)
+    assert q.shape[0] == v.shape[0]
+    B = q.shape[0]
+    for name, t in (("q", q), ("k", k), ("v", v), ("a", a), ("b", b)):
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"GDN decode expects bf16 {name}, got {t.dtype}")
+        if not t.is_cuda:
+            raise ValueError(f"GDN decode expects CUDA tensors ({name} is on {t.device})")
+    assert a.numel() == B * HV and b.numel() == B * HV, "a, b must be [B,1,8]"
+
+
+def _f32(x: torch.Tensor) -> torch.Tensor:
+    return x.float().contiguous()
+
+
+def decode_into(q, k, v, state, A_log, a, dt_bias, b, scale, out, new_state,
+                stream: Optional[int] = None) -> None:
+    """Destination-passing form: writes `out` [B,1,8,128] bf16 and
+    `new_state` [B,8,128,128] fp32 (may be `state` itself for an in-place
+    update).  All tensors must be contiguous CUDA tensors."""
+    B = q.shape[0]
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+    st = _native.lib.gdn_decode_qk4_v8_d128_k_last(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(),
+        None if state is None else state.data_ptr(),
+        A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
+        _scale(scale), B, out.data_ptr(), new_state.data_ptr(), stream)
+    _native.check(st, "gdn_decode_qk4_v8_d128_k_last")
+
+
+@torch.no_grad()
+def run(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[torch.Tensor],
+        A_log: torch.Tensor, a: torch.Tensor, dt_bias: torch.Tensor, b: torch.Tensor,
+        scale: Optional[float]):
+    """Returns (output [B,1,8,128] bf16, new_state [B,8,128,128] fp32)."""
+    _check_inputs(q, k, v, a, b)
+    B = q.shape[0]
+    if state is not None:
+        assert state.shape == (B, HV, D, D) and state.dtype == torch.float32
+        state = state.contiguous()
+    output = torch.empty(B, 1, HV, D, dtype=q.dtype, device=q.device)
+    new_state = torch.empty(B, HV, D, D, dtype=torch.float32, device=q.device)
+    decode_into(q.contiguous(), k.contiguous(), v.contiguous(), state, _f32(A_log),
+                a.contiguous(), _f32(dt_bias), b.contiguous(), scale, output, new_state)
+    return output, new_state
+
+
+@torch.no_grad()
+def run_inplace(q, k, v, state, A_log, a, dt_bias, b, scale):
+    """Same step with the state updated in place (serving form: the state
+    pool stays resident and is not copied).  Returns output [B,1,8,128]."""
+    _check_inputs(q, k, v, a, b)
+    B = q.shape[0]
+    assert state.shape == (B, HV, D, D) and state.dtype == torch.float32 and state.is_contiguous()
+    output = torch.empty(B, 1, HV, D, dtype=q.dtype, device=q.device)
+    decode_into(q.contiguous(), k.contiguous(), v.contiguous(), state, _f32(A_log),
+                a.contiguous(), _f32(dt_bias), b.contiguous(), scale, output, state)
+    return output

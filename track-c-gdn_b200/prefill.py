@@ -1,0 +1,108 @@
+"""GDN prefill (qk4_v8_d128_k_last): drop-in for the reference prefill solution.
+
+`run` keeps the signature, argument meaning, defaults and error behaviour of
+`run` in solution/triton/kernel.py (lines 1762-1802 of the reference project):
+value-returning (output [T,8,128] bf16, final_state [N,8,128,128] fp32),
+`scale` None or 0 -> 1/sqrt(128), `state` None -> zero initial state, and the
+input checks of `_validate_inputs` (kernel.py:1635-1667), including the
+`cu_seqlens[-1] == T` assert, which reads one value back from the device as
+the reference does.  `prefill_into` is the destination-passing form with no
+host synchronisation at all (the same check then runs on the device).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _native
+
+NUM_Q_HEADS = 4
+NUM_K_HEADS = 4
+NUM_V_HEADS = 8
+HEAD_SIZE = 128
+CHUNK_SIZE = 64
+
+
+def _validate_inputs(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, check_total=True):
+    # kernel.py:1635-1667
+    assert q.is_cuda and k.is_cuda and v.is_cuda
+    assert A_log.is_cuda and a.is_cuda and dt_bias.is_cuda and b.is_cuda and cu_seqlens.is_cuda
+    assert q.dtype == torch.bfloat16
+    assert k.dtype == torch.bfloat16
+    assert v.dtype == torch.bfloat16
+    assert A_log.dtype == torch.float32
+    assert dt_bias.dtype == torch.float32
+    assert a.dtype == torch.bfloat16
+    assert b.dtype == torch.bfloat16
+    if state is not None:
+        assert state.is_cuda and state.dtype == torch.float32
+    assert q.shape[1:] == (NUM_Q_HEADS, HEAD_SIZE)
+    assert k.shape[1:] == (NUM_K_HEADS, HEAD_SIZE)
+    assert v.shape[1:] == (NUM_V_HEADS, HEAD_SIZE)
+    assert A_log.shape == (NUM_V_HEADS,)
+    assert dt_bias.shape == (NUM_V_HEADS,)
+    assert a.shape == (q.shape[0], NUM_V_HEADS)
+    assert b.shape == (q.shape[0], NUM_V_HEADS)
+    assert cu_seqlens.dtype == torch.int64
+    if check_total:
+        assert int(cu_seqlens[-1].item()) == q.shape[0]
+    if state is not None:
+        assert state.shape == (cu_seqlens.numel() - 1, NUM_V_HEADS, HEAD_SIZE, HEAD_SIZE)
+
+
+def workspace_bytes(total_tokens: int, num_seqs: int) -> int:
+    return int(_native.lib.gdn_prefill_workspace_bytes(total_tokens, num_seqs))
+
+
+def alloc_workspace(total_tokens: int, num_seqs: int, device) -> torch.Tensor:
+    """A workspace buffer for `prefill_into` (1024-byte aligned: the caching
+    allocator returns 512-byte aligned blocks, so 1 KiB of slack is added and
+    `workspace_view` picks the aligned start)."""
+    return torch.empty(workspace_bytes(total_tokens, num_seqs) + 1024, dtype=torch.uint8,
+                       device=device)
+
+
+def _aligned_ptr(ws: torch.Tensor):
+    p = ws.data_ptr()
+    off = (-p) % 1024
+    return p + off, ws.numel() - off
+
+
+def prefill_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, out, final_state,
+                 workspace: torch.Tensor, stream: Optional[int] = None) -> None:
+    """Destination-passing prefill: writes `out` [T,8,128] bf16 and
+    `final_state` [N,8,128,128] fp32 (which may be `state`).  No host sync."""
+    T = q.shape[0]
+    N = cu_seqlens.numel() - 1
+    if scale is None or scale == 0.0:
+        scale = 1.0 / math.sqrt(HEAD_SIZE)
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+    wptr, wbytes = _aligned_ptr(workspace)
+    st = _native.lib.gdn_prefill_qk4_v8_d128_k_last(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(),
+        None if state is None else state.data_ptr(),
+        A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
+        cu_seqlens.data_ptr(), N, T, float(scale), out.data_ptr(), final_state.data_ptr(),
+        wptr, wbytes, stream)
+    _native.check(st, "gdn_prefill_qk4_v8_d128_k_last")
+
+
+@torch.no_grad()
+def run(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[torch.Tensor],
+        A_log: torch.Tensor, a: torch.Tensor, dt_bias: torch.Tensor, b: torch.Tensor,
+        cu_seqlens: torch.Tensor, scale: Optional[float]):
+    _validate_inputs(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
+    T = q.shape[0]
+    N = cu_seqlens.numel() - 1
+    out = torch.empty(T, NUM_V_HEADS, HEAD_SIZE, dtype=torch.bfloat16, device=q.device)
+    final_state = torch.empty(N, NUM_V_HEADS, HEAD_SIZE, HEAD_SIZE, dtype=torch.float32,
+                              device=q.device)
+    ws = alloc_workspace(T, N, q.device)
+    prefill_into(q.contiguous(), k.contiguous(), v.contiguous(),
+                 None if state is None else state.contiguous(), A_log.contiguous(),
+                 a.contiguous(), dt_bias.contiguous(), b.contiguous(), cu_seqlens.contiguous(),
+                 scale, out, final_state, ws)
+    return out, final_state
