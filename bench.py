@@ -1,0 +1,583 @@
+"""Benchmark of the B200 GDN kernel pair (qk4_v8_d128_k_last).
+
+Default workload ("mixed serving load"): one serving step
+= a decode step for 4096 requests (state updated in place, resident in HBM)
+plus a ragged prefill of 256 new sequences with lengths ~U{512..8192}
+(~1.1M tokens, zero initial state), followed, when N > 1, by the NCCL gather
+to rank 0 of the decode outputs and prefill final states.  The work is a
+fixed total sharded across the N ranks (decode: request blocks; prefill: LPT
+bin packing by sequence), so scaling is "strong".  All inputs are seeded
+synthetic tensors with the BASELINE value distributions.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload c4|c2|c3|decode]
+
+Prints one JSON line (rank 0).  `value` is whole-job tokens/s (decode tokens
++ prefill tokens) over the device time of K steps (max over ranks);
+`e2e` is the same metric through the public entry points with pinned host
+inputs and outputs copied inside the timed region.  `--impl reference` times
+the CPU oracle (the reference recurrence restated in C, all host threads) on
+bounded samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HQK, HV, D = 4, 8, 128
+DECODE_STATE_BYTES = HV * D * D * 4 * 2           # fp32 state read + written per request
+DECODE_VEC_BYTES = 2 * HQK * D * 2 + 2 * HV * D * 2 + 2 * HV * 2  # q,k,v,out,a,b
+PREFILL_FLOP_PER_TOKEN = 1_441_792                # 8 v-heads x 180,224
+PREFILL_BYTES_PER_TOKEN = 6176
+STATE_BYTES = HV * D * D * 4
+
+WORKLOADS = {
+    "c4": dict(desc="C4 mixed serving: decode B=4096 (in place) + ragged prefill of 256 "
+                    "sequences, lengths U{512..8192}, zero initial state",
+               decode_batch=4096, prefill="c4"),
+    "c2": dict(desc="C2 prefill: one packed sequence T=4096, zero initial state",
+               decode_batch=0, prefill="c2"),
+    "c3": dict(desc="C3 ragged prefill: 32 sequences U{17..3000}, initial states randn*0.02",
+               decode_batch=0, prefill="c3"),
+    "decode": dict(desc="C1 decode sweep point: batch 1024, state updated in place",
+                   decode_batch=1024, prefill=None),
+}
+
+
+def prefill_lengths(kind: str) -> np.ndarray:
+    if kind == "c4":
+        return np.random.default_rng(4).integers(512, 8193, size=256)
+    if kind == "c3":
+        return np.random.default_rng(3).integers(17, 3001, size=32)
+    if kind == "c2":
+        return np.array([4096])
+    raise ValueError(kind)
+
+
+# ---------------------------------------------------------------------------
+# measured peaks
+# ---------------------------------------------------------------------------
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(hbm_gbs=d["hbm_gbs"], bf16_tflops=d["bf16_tflops"],
+                    bf16_tflops_sustained=d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                    source="measured")
+    return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0, source="fallback")
+
+
+def load_traffic(workload: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return {}
+    return json.loads(p.read_text()).get(workload, {})
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, enabled: bool):
+        self.proc = None
+        self.path = None
+        if not enabled:
+            return
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"gdn_clocks_{os.getpid()}.csv"
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self, gpu_indices):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if gpu_indices is not None and idx not in gpu_indices:
+                continue
+            rows.append(parts)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return None
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        smax = max((num(r[2]) for r in rows if num(r[2]) is not None), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def make_prefill_inputs(torch, lengths, with_state, seed, dev):
+    import torch.nn.functional as F
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    T = int(lengths.sum())
+    N = len(lengths)
+    cu = np.zeros(N + 1, np.int64)
+    cu[1:] = np.cumsum(lengths)
+    q = F.normalize(torch.randn(T, HQK, D, generator=g, device=dev), dim=-1).bfloat16()
+    k = F.normalize(torch.randn(T, HQK, D, generator=g, device=dev), dim=-1).bfloat16()
+    v = torch.randn(T, HV, D, generator=g, device=dev).bfloat16()
+    a = torch.randn(T, HV, generator=g, device=dev).bfloat16()
+    b = torch.randn(T, HV, generator=g, device=dev).bfloat16()
+    h0 = (torch.randn(N, HV, D, D, generator=g, device=dev) * 0.02) if with_state else None
+    return dict(q=q, k=k, v=v, a=a, b=b, h0=h0, cu=torch.from_numpy(cu).to(dev), T=T, N=N)
+
+
+def make_decode_inputs(torch, B, seed, dev):
+    import torch.nn.functional as F
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    q = F.normalize(torch.randn(B, 1, HQK, D, generator=g, device=dev), dim=-1).bfloat16()
+    k = F.normalize(torch.randn(B, 1, HQK, D, generator=g, device=dev), dim=-1).bfloat16()
+    v = torch.randn(B, 1, HV, D, generator=g, device=dev).bfloat16()
+    a = torch.randn(B, 1, HV, generator=g, device=dev).bfloat16()
+    b = torch.randn(B, 1, HV, generator=g, device=dev).bfloat16()
+    state = torch.randn(B, HV, D, D, generator=g, device=dev) * 0.02
+    return dict(q=q, k=k, v=v, a=a, b=b, state=state, B=B)
+
+
+def gpu_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    gdn = importlib.import_module("track-c-gdn_b200")
+    from importlib import import_module
+    shard = import_module("track-c-gdn_b200.shard")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=dev)
+    wl = WORKLOADS[args.workload]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    A_log = (torch.rand(HV, generator=gen, device=dev) * 2.7).float()
+    dt_bias = (torch.randn(HV, generator=gen, device=dev) * 0.1).float()
+    if world > 1:  # same gate parameters on every rank (one model)
+        dist.broadcast(A_log, 0)
+        dist.broadcast(dt_bias, 0)
+
+    # ---- this rank's shard of the workload ----
+    B_total = wl["decode_batch"]
+    dec_slice = shard.block_partition(B_total, world, rank)
+    B = dec_slice.stop - dec_slice.start
+    dec = make_decode_inputs(torch, B, 100 + rank, dev) if B > 0 else None
+    pre = None
+    total_prefill_tokens = 0
+    seq_counts = [0] * world
+    if wl["prefill"]:
+        lengths = prefill_lengths(wl["prefill"])
+        total_prefill_tokens = int(lengths.sum())
+        parts = shard.lpt_partition(lengths.tolist(), world)
+        seq_counts = [len(p) for p in parts]
+        my_lengths = lengths[parts[rank]]
+        pre = make_prefill_inputs(torch, my_lengths, wl["prefill"] == "c3", 200 + rank, dev)
+        pre["out"] = torch.empty(pre["T"], HV, D, dtype=torch.bfloat16, device=dev)
+        pre["final"] = torch.empty(pre["N"], HV, D, D, dtype=torch.float32, device=dev)
+        pre["ws"] = gdn.prefill.alloc_workspace(pre["T"], pre["N"], dev)
+    dec_out = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=dev) if B > 0 else None
+    max_seqs = max(seq_counts) if seq_counts else 0
+    max_dec = math.ceil(B_total / world) if B_total else 0
+    total_tokens = B_total + total_prefill_tokens
+    stream = torch.cuda.current_stream(dev)
+
+    ev = {k: [] for k in ("s", "d", "p", "g")}
+
+    def step(record):
+        if record:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            ev["s"].append(e)
+        if dec is not None:
+            gdn.decode.decode_into(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
+                                   dt_bias, dec["b"], None, dec_out, dec["state"])
+        if record:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            ev["d"].append(e)
+        if pre is not None and pre["N"] > 0:
+            gdn.prefill.prefill_into(pre["q"], pre["k"], pre["v"], pre["h0"], A_log, pre["a"],
+                                     dt_bias, pre["b"], pre["cu"], None, pre["out"],
+                                     pre["final"], pre["ws"])
+        if record:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            ev["p"].append(e)
+        if world > 1:
+            if dec_out is not None or max_dec:
+                t = dec_out if dec_out is not None else torch.empty(0, 1, HV, D, dtype=torch.bfloat16, device=dev)
+                shard.gather_padded(t, max_dec)
+            if max_seqs:
+                t = pre["final"] if pre is not None else torch.empty(0, HV, D, D, device=dev)
+                shard.gather_padded(t, max_seqs)
+        if record:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            ev["g"].append(e)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step(False)
+    barrier()
+    sampler = ClockSampler(rank == 0)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop(None)
+    elapsed_ms = max_over_ranks(t0.elapsed_time(t1))
+    ms_step = elapsed_ms / args.steps
+    d_ms = np.mean([a.elapsed_time(b) for a, b in zip(ev["s"], ev["d"])])
+    p_ms = np.mean([a.elapsed_time(b) for a, b in zip(ev["d"], ev["p"])])
+    g_ms = np.mean([a.elapsed_time(b) for a, b in zip(ev["p"], ev["g"])])
+    d_ms_max, p_ms_max, g_ms_max = (max_over_ranks(float(x)) for x in (d_ms, p_ms, g_ms))
+    status = gdn._native.read_device_status()
+    if status:
+        raise SystemExit(f"device status {status} after the timed region")
+
+    peaks = load_peaks()
+    result = {
+        "metric": "GDN serving throughput (decode + prefill tokens/s, max-over-ranks device time)",
+        "value": total_tokens / (ms_step / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE value distributions)",
+        "config": {
+            "workload": wl["desc"],
+            "decode_batch": B_total,
+            "prefill_sequences": int(sum(seq_counts)) if wl["prefill"] else 0,
+            "prefill_tokens": total_prefill_tokens,
+            "l2": "inputs larger than L2 (no flush needed)" if total_tokens > 20000 else
+                  "inputs smaller than L2 (no flush)",
+            "parallelism": f"shard{world}: decode request blocks, prefill LPT by sequence; "
+                           + ("NCCL gather of decode outputs + prefill final states to rank 0"
+                              if world > 1 else "no collective"),
+        },
+        "gpu_launches": args.steps * ((1 if dec is not None else 0) +
+                                      (gdn._native.PREFILL_KERNELS_PER_CALL if pre else 0)),
+        "phases_ms": {"decode": d_ms_max, "prefill": p_ms_max, "gather": g_ms_max},
+        "clocks": clocks,
+    }
+    if dec is not None:
+        gbs = B * (DECODE_STATE_BYTES + DECODE_VEC_BYTES) / (d_ms / 1e3) / 1e9
+        result["decode"] = {"us_per_step": d_ms_max * 1e3, "state_gbs_rank0": gbs,
+                            "batch_per_rank": B}
+        result["roofline_decode"] = {
+            "bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": gbs / peaks["hbm_gbs"],
+            "traffic": load_traffic(args.workload).get("decode_bytes_per_launch"),
+            "peak_source": peaks["source"] + " hbm copy"}
+    if pre is not None:
+        flops = pre["T"] * PREFILL_FLOP_PER_TOKEN
+        tflops = flops / (p_ms / 1e3) / 1e12
+        result["prefill"] = {"tokens_per_s": total_prefill_tokens / (p_ms_max / 1e3),
+                             "tflops_rank0": tflops, "tokens_rank0": pre["T"]}
+        result["roofline"] = {
+            "kernel": "prefill (meta + prep + scan launches of one prefill call)",
+            "bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops_sustained"],
+            "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops_sustained"],
+            "traffic": load_traffic(args.workload).get("prefill_bytes_per_launch"),
+            "algorithmic_bytes": pre["T"] * PREFILL_BYTES_PER_TOKEN + 2 * pre["N"] * STATE_BYTES,
+            "peak_source": peaks["source"] + " bf16 sustained"}
+    elif dec is not None:
+        result["roofline"] = result.pop("roofline_decode")
+
+    # ---- end to end through the public entry points with host buffers ----
+    result["e2e"] = e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world,
+                            max_over_ranks, barrier, total_tokens)
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_seconds)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world, max_over_ranks, barrier,
+            total_tokens):
+    """Same step through decode.run_inplace / prefill.run with pinned host
+    inputs copied in and outputs copied out inside the timed region."""
+    steps = max(1, min(args.steps, args.e2e_steps))
+    stream = torch.cuda.current_stream(dev)
+    host = {}
+    h2d = d2h = 0
+    if dec is not None:
+        for key in ("q", "k", "v", "a", "b"):
+            host["d" + key] = dec[key].cpu().pin_memory()
+            h2d += dec[key].numel() * dec[key].element_size()
+        host["dout"] = torch.empty(dec["B"], 1, HV, D, dtype=torch.bfloat16).pin_memory()
+        d2h += host["dout"].numel() * 2
+    if pre is not None:
+        for key in ("q", "k", "v", "a", "b", "cu"):
+            host["p" + key] = pre[key].cpu().pin_memory()
+            h2d += pre[key].numel() * pre[key].element_size()
+        if pre["h0"] is not None:
+            host["ph0"] = pre["h0"].cpu().pin_memory()
+            h2d += pre["h0"].numel() * 4
+        host["pout"] = torch.empty(pre["T"], HV, D, dtype=torch.bfloat16).pin_memory()
+        host["pfin"] = torch.empty(pre["N"], HV, D, D, dtype=torch.float32).pin_memory()
+        d2h += host["pout"].numel() * 2 + host["pfin"].numel() * 4
+
+    def one():
+        if dec is not None:
+            t = {k: host["d" + k].to(dev, non_blocking=True) for k in ("q", "k", "v", "a", "b")}
+            o = gdn.decode.run_inplace(t["q"], t["k"], t["v"], dec["state"], A_log, t["a"],
+                                       dt_bias, t["b"], None)
+            host["dout"].copy_(o, non_blocking=True)
+        if pre is not None and pre["N"] > 0:
+            t = {k: host["p" + k].to(dev, non_blocking=True) for k in ("q", "k", "v", "a", "b", "cu")}
+            h0 = host["ph0"].to(dev, non_blocking=True) if "ph0" in host else None
+            o, fs = gdn.prefill.run(t["q"], t["k"], t["v"], h0, A_log, t["a"], dt_bias, t["b"],
+                                    t["cu"], None)
+            host["pout"].copy_(o, non_blocking=True)
+            host["pfin"].copy_(fs, non_blocking=True)
+
+    one()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        one()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = max_over_ranks(t0.elapsed_time(t1)) / steps
+    return {"value": total_tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "steps": steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "decode.run_inplace + prefill.run (reference-compatible entry points)",
+            "bytes_per_step_note": "per rank" if world > 1 else "single GPU"}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle (reported baseline and the reference arm)
+# ---------------------------------------------------------------------------
+def _bf16_bits(x: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def _cpu_decode_inputs(rng, B):
+    def nrm(s):
+        x = rng.standard_normal(s, dtype=np.float32)
+        return x / np.linalg.norm(x, axis=-1, keepdims=True)
+    return dict(q=_bf16_bits(nrm((B, 1, HQK, D))), k=_bf16_bits(nrm((B, 1, HQK, D))),
+                v=_bf16_bits(rng.standard_normal((B, 1, HV, D), dtype=np.float32)),
+                a=_bf16_bits(rng.standard_normal((B, 1, HV), dtype=np.float32)),
+                b=_bf16_bits(rng.standard_normal((B, 1, HV), dtype=np.float32)),
+                state=(rng.standard_normal((B, HV, D, D), dtype=np.float32) * 0.02))
+
+
+def _cpu_prefill_inputs(rng, lengths, with_state):
+    T = int(np.sum(lengths))
+    cu = np.zeros(len(lengths) + 1, np.int64)
+    cu[1:] = np.cumsum(lengths)
+
+    def nrm(s):
+        x = rng.standard_normal(s, dtype=np.float32)
+        return x / np.linalg.norm(x, axis=-1, keepdims=True)
+    return dict(q=_bf16_bits(nrm((T, HQK, D))), k=_bf16_bits(nrm((T, HQK, D))),
+                v=_bf16_bits(rng.standard_normal((T, HV, D), dtype=np.float32)),
+                a=_bf16_bits(rng.standard_normal((T, HV), dtype=np.float32)),
+                b=_bf16_bits(rng.standard_normal((T, HV), dtype=np.float32)),
+                state=(rng.standard_normal((len(lengths), HV, D, D), dtype=np.float32) * 0.02)
+                if with_state else None, cu=cu, T=T)
+
+
+class CpuOracleTimer:
+    """Times the oracle on samples of a workload; extrapolates the time of one
+    full step as decode_time_per_request * B + prefill_time_per_token * T."""
+
+    def __init__(self, workload: str):
+        import oracle
+        self.oracle = oracle
+        self.threads = oracle.default_threads()
+        self.wl = WORKLOADS[workload]
+        self.lengths = prefill_lengths(self.wl["prefill"]) if self.wl["prefill"] else None
+        self.rng = np.random.default_rng(77)
+        self.A_log = (self.rng.random(HV, dtype=np.float32) * 2.7).astype(np.float32)
+        self.dt = (self.rng.standard_normal(HV, dtype=np.float32) * 0.1).astype(np.float32)
+        self.dec_s = self.dec_n = self.pre_s = self.pre_n = 0.0
+        self.next_seq = 0
+        self.dec_sample = 64
+
+    def sample(self):
+        if self.wl["decode_batch"]:
+            inp = _cpu_decode_inputs(self.rng, self.dec_sample)
+            t = time.perf_counter()
+            self.oracle.decode(inp["q"], inp["k"], inp["v"], inp["state"], self.A_log, inp["a"],
+                               self.dt, inp["b"], nthreads=self.threads)
+            self.dec_s += time.perf_counter() - t
+            self.dec_n += self.dec_sample
+        if self.lengths is not None:
+            L = [int(self.lengths[self.next_seq % len(self.lengths)])]
+            self.next_seq += 1
+            inp = _cpu_prefill_inputs(self.rng, L, self.wl["prefill"] == "c3")
+            t = time.perf_counter()
+            self.oracle.prefill(inp["q"], inp["k"], inp["v"], inp["state"], self.A_log, inp["a"],
+                                self.dt, inp["b"], inp["cu"], nthreads=self.threads)
+            self.pre_s += time.perf_counter() - t
+            self.pre_n += inp["T"]
+
+    def full_step_seconds(self):
+        t = 0.0
+        if self.wl["decode_batch"]:
+            t += self.dec_s / self.dec_n * self.wl["decode_batch"]
+        if self.lengths is not None:
+            t += self.pre_s / self.pre_n * float(self.lengths.sum())
+        return t
+
+    def total_tokens(self):
+        return self.wl["decode_batch"] + (int(self.lengths.sum()) if self.lengths is not None else 0)
+
+    def describe(self):
+        parts = []
+        if self.dec_n:
+            parts.append(f"decode of {int(self.dec_n)} requests")
+        if self.pre_n:
+            parts.append(f"prefill of {int(self.pre_n)} tokens ({self.next_seq} sequences drawn "
+                         f"from the workload's length list)")
+        return ("; ".join(parts) + "; extrapolated per request / per token to the full step")
+
+
+def cpu_baseline(workload: str, budget_s: float = 15.0):
+    timer = CpuOracleTimer(workload)
+    t_start = time.perf_counter()
+    while time.perf_counter() - t_start < budget_s:
+        timer.sample()
+    step_s = timer.full_step_seconds()
+    return {"value": timer.total_tokens() / step_s, "unit": "tokens/s", "cores": timer.threads,
+            "kind": "port", "sample": timer.describe(),
+            "wall_s": round(time.perf_counter() - t_start, 1)}
+
+
+def reference_arm(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    timer = CpuOracleTimer(args.workload)
+    for _ in range(args.warmup):
+        timer.sample()
+    timer.dec_s = timer.dec_n = timer.pre_s = timer.pre_n = 0.0
+    t_start = time.perf_counter()
+    for _ in range(args.steps):
+        timer.sample()
+    step_s = timer.full_step_seconds()
+    value = timer.total_tokens() / step_s
+    wl = WORKLOADS[args.workload]
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "GDN serving throughput (decode + prefill tokens/s, max-over-ranks device time)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": wl["desc"], "decode_batch": wl["decode_batch"],
+                   "prefill_tokens": int(timer.lengths.sum()) if timer.lengths is not None else 0},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": timer.threads,
+                         "kind": "port", "sample": timer.describe() + f"; {args.steps} timed samples",
+                         "wall_s": round(time.perf_counter() - t_start, 1)},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference's path is Python/Triton (GPU only); its CPU implementation "
+                "is the oracle's C restatement of the same recurrence (OpenMP, all host threads)",
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c4")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "b200":
+        args.warmup = 3  # timing rule: at least three warm-up steps
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()
