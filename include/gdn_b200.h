@@ -31,7 +31,8 @@ typedef enum {
   GDN_ERR_WORKSPACE = 4,      /* workspace missing or smaller than required */
   GDN_ERR_LAUNCH = 5,         /* the CUDA launch itself failed */
   GDN_ERR_DEVICE = 6,         /* no sm_100 device / wrong device */
-  GDN_ERR_ALIASING = 7        /* outputs overlap inputs where not allowed */
+  GDN_ERR_ALIASING = 7,       /* outputs overlap inputs where not allowed */
+  GDN_ERR_TOO_LARGE = 8       /* problem exceeds the no-allocation scratch */
 } gdn_status_t;
 
 /* ABI version of this header (bumped on any signature change). */
@@ -105,6 +106,29 @@ int gdn_prefill_qk4_v8_d128_k_last(
     const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
     float scale, void *out, float *final_state, void *workspace,
     size_t workspace_bytes, void *stream);
+
+/*
+ * Prefill that allocates nothing -- no counterpart in the reference.
+ * Same arguments and results as gdn_prefill_qk4_v8_d128_k_last minus the
+ * workspace: for callers that may not allocate device memory while a step
+ * runs (e.g. a plugin whose host framework owns all device memory, or a
+ * serving loop that cannot afford cudaMalloc's implicit synchronisation).
+ * The scratch is a 32 MiB buffer compiled into the library
+ * (GDN_PREFILL_NOALLOC_SCRATCH_BYTES), held on every GPU that loads it until
+ * exit.  Problems whose gdn_prefill_workspace_bytes(T, N) exceeds it are
+ * rejected with GDN_ERR_TOO_LARGE before anything is launched; a problem
+ * always fits when T + 64 N <= 15,872 (e.g. T <= 15,808 for one sequence).
+ * All calls on a device share the buffer: calls whose kernels overlap on
+ * that GPU race and must be serialised by the caller.  The first call on
+ * each device looks up the buffer's device address (cudaGetSymbolAddress,
+ * with that device current); make it before any stream capture begins.
+ */
+#define GDN_PREFILL_NOALLOC_SCRATCH_BYTES (32u << 20)
+int gdn_prefill_qk4_v8_d128_k_last_noalloc(
+    const void *q, const void *k, const void *v, const float *state,
+    const float *A_log, const void *a, const float *dt_bias, const void *b,
+    const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+    float scale, void *out, float *final_state, void *stream);
 
 #ifdef __cplusplus
 }

@@ -4,3 +4,4 @@
 #include "gdn_decode.cu"
 #include "gdn_prefill.cu"
 #include "gdn_capi.cu"
+#include "gdn_prefill_noalloc.cu"

@@ -69,6 +69,7 @@ const char *gdn_b200_status_string(int status) {
     case GDN_ERR_LAUNCH: return "CUDA kernel launch failed";
     case GDN_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
     case GDN_ERR_ALIASING: return "an output partially overlaps an input";
+    case GDN_ERR_TOO_LARGE: return "problem exceeds the no-allocation entry point's built-in scratch";
     default: return "unknown status";
   }
 }
