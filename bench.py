@@ -357,8 +357,9 @@ def gpu_arm(args):
         result["roofline"] = result.pop("roofline_decode")
 
     # ---- end to end through the public entry points with host buffers ----
-    result["e2e"] = e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world,
-                            max_over_ranks, barrier, total_tokens)
+    if not args.no_e2e:
+        result["e2e"] = e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world,
+                                max_over_ranks, barrier, total_tokens)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_seconds)
@@ -570,6 +571,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="device step only (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3  # timing rule: at least three warm-up steps

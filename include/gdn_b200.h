@@ -88,14 +88,15 @@ size_t gdn_prefill_workspace_bytes(int64_t total_tokens, int64_t num_seqs);
  *   solution/triton/kernel.py:1762-1802
  * q, k        [T,4,128] bf16 (16-byte aligned)
  * v           [T,8,128] bf16 (16-byte aligned)
- * state       [N,8,128,128] fp32 initial states, or NULL for zeros
+ * state       [N,8,128,128] fp32 initial states (16-byte aligned), or NULL
+ *             for zeros
  * A_log, dt_bias [8] fp32;  a, b [T,8] bf16
  * cu_seqlens  [N+1] int64 on the device, cu_seqlens[0] = 0,
  *             non-decreasing, cu_seqlens[N] = T (checked on the device; a
  *             violation sets device status 1 and leaves outputs unwritten)
  * scale       0.0f selects 1/sqrt(128)
  * out         [T,8,128] bf16 (16-byte aligned)
- * final_state [N,8,128,128] fp32; may equal `state` (in place)
+ * final_state [N,8,128,128] fp32 (16-byte aligned); may equal `state`
  * workspace   >= gdn_prefill_workspace_bytes(T, N) bytes, 1024-byte aligned
  * No host synchronisation: unlike the reference (kernel.py:1665, :181-184)
  * the chunk metadata is built on the device.

@@ -131,7 +131,7 @@ int gdn_prefill_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
   if (!cu_seqlens || !A_log || !dt_bias || !final_state || !workspace) return GDN_ERR_NULL_POINTER;
   if (total_tokens > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL_POINTER;
   if ((q && !aligned(q, 16)) || (k && !aligned(k, 16)) || (v && !aligned(v, 16)) ||
-      (out && !aligned(out, 16)) || !aligned(final_state, 4) || (state && !aligned(state, 4)) ||
+      (out && !aligned(out, 16)) || !aligned(final_state, 16) || (state && !aligned(state, 16)) ||
       !aligned(cu_seqlens, 8))
     return GDN_ERR_MISALIGNED;
   if (!aligned(workspace, 1024) ||

@@ -29,6 +29,12 @@
 //   3. gdn_prefill_scan_kernel   (one CTA per (sequence, v-head, v-slice))
 //      runs the inter-chunk scan with the fp32 state slice held in registers
 //      and a bf16 copy in shared memory as the MMA operand.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
 #include "gdn_common.cuh"
 #include "sm100.cuh"
 
@@ -100,23 +106,6 @@ __device__ __noinline__ bool wait_phase(uint32_t mbar, uint32_t parity, volatile
       set_device_status(kDevStatusWaitTimeout);
       return false;
     }
-  }
-}
-
-// Copy rows of q (rows 0..63) and k (rows 64..127) of one chunk into the
-// [Q;K] operand tile: two 64-wide d-blocks of 128 rows x 128 bytes each,
-// 128-byte swizzled.  Rows past the chunk's valid length are zero.
-__device__ __forceinline__ void load_qk_tile(uint8_t *qk, const uint16_t *__restrict__ q,
-                                             const uint16_t *__restrict__ k, int64_t t0, int L,
-                                             int hqk, int tid, int nthreads) {
-  for (int idx = tid; idx < 128 * 16; idx += nthreads) {
-    const int r = idx >> 4, ch = idx & 15, tok = r & 63;
-    uint4 val = make_uint4(0u, 0u, 0u, 0u);
-    if (tok < L) {
-      const uint16_t *src = (r < 64 ? q : k) + ((t0 + tok) * kHQK + hqk) * kD + ch * 8;
-      val = __ldg(reinterpret_cast<const uint4 *>(src));
-    }
-    *reinterpret_cast<uint4 *>(qk + (ch >> 3) * 16384 + sw128(r, ch & 7)) = val;
   }
 }
 
@@ -211,22 +200,30 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
 // ---------------------------------------------------------------------------
 // 2. chunk-parallel preparation
 // ---------------------------------------------------------------------------
+// One CTA per (chunk, q/k head), 128 threads, both v-heads j = 0, 1 of the
+// q/k head.  The [Q;K] tile arrives by TMA; D = [Q;K] K^T on the tensor core
+// gives Q K^T (TMEM lanes 0..63) and K K^T (lanes 64..127) at once; each
+// thread turns one row into P_j (bf16 operand) or A_j (fp32, shared memory);
+// thread (j, c) solves column c of (I + A_j)^-1 by fp32 forward substitution;
+// a second MMA forms P_j Ainv_j.  Output per (chunk, v-head): the 16 KiB
+// [P Ainv ; Ainv] image in the scan kernel's shared-memory operand layout.
 constexpr int kPrepThreads = 128;
 // shared memory map (offsets from a 1024-byte aligned base)
-constexpr int kPrepQK = 0;         // [Q;K] tile 32 KB; later the fp32 A matrices
-constexpr int kPrepPP = 32768;     // [P_0 ; P_1] bf16, K-major 128 x 64, 16 KB
-constexpr int kPrepM2 = 49152;     // two [PA ; Ainv] images, 2 x 16 KB
-constexpr int kPrepG = 81920;      // float G[2][64]
-constexpr int kPrepB = 82432;      // float beta[2][64]
-constexpr int kPrepWt = 82944;     // float warp totals[4]
-constexpr int kPrepBar = 82960;    // mbarrier (8 B)
-constexpr int kPrepTmem = 82968;   // TMEM base address (4 B)
-constexpr int kPrepBroken = 82972; // wait-timeout flag
-// + 1024 for aligning the base, + 16 KiB guard after the last operand
-constexpr int kPrepSmem = 83008 + 1024 + 16384;
+constexpr int kPrepQK = 0;          // [Q;K] tile 32 KB; after MMA 1 the fp32 A_0, A_1
+constexpr int kPrepPP = 32768;      // [P_0 ; P_1] bf16, K-major 128 x 64, 16 KB
+constexpr int kPrepAI = 49152;      // Ainv_0, Ainv_1 bf16, 64 x 64 each (2 x 8 KB)
+constexpr int kPrepG = 65536;       // float G[2][64]
+constexpr int kPrepB = kPrepG + 512;    // float beta[2][64]
+constexpr int kPrepWt = kPrepB + 512;   // float warp totals[4]
+constexpr int kPrepBar = kPrepWt + 16;  // mbarriers: mma, tma
+constexpr int kPrepTmem = kPrepBar + 16;
+constexpr int kPrepBroken = kPrepTmem + 4;
+constexpr int kPrepSmem = kPrepBroken + 12 + 1024;  // + base alignment slack
+constexpr uint32_t kPrepTmemCols = 128;
 
 __global__ void __launch_bounds__(kPrepThreads)
-gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
+gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                        const __grid_constant__ CUtensorMap tmap_k,
                         const float *__restrict__ A_log, const uint16_t *__restrict__ a,
                         const float *__restrict__ dt_bias, const uint16_t *__restrict__ b,
                         const int64_t *__restrict__ cu, const int *__restrict__ meta,
@@ -245,23 +242,32 @@ gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
 
   uint8_t *qk = smem + kPrepQK;
   uint8_t *pp = smem + kPrepPP;
-  uint8_t *m2 = smem + kPrepM2;
+  uint8_t *ai = smem + kPrepAI;
   float *Gs = reinterpret_cast<float *>(smem + kPrepG);
   float *Bs = reinterpret_cast<float *>(smem + kPrepB);
   float *wt = reinterpret_cast<float *>(smem + kPrepWt);
   volatile int *broken = reinterpret_cast<volatile int *>(smem + kPrepBroken);
-  const uint32_t bar = smem_u32(smem + kPrepBar);
+  const uint32_t bar = smem_u32(smem + kPrepBar), bar_tma = bar + 8;
 
-  if (warp == 0) tmem_alloc(smem_u32(smem + kPrepTmem), 256);
+  if (warp == 0) tmem_alloc(smem_u32(smem + kPrepTmem), kPrepTmemCols);
   if (tid == 0) {
     *broken = 0;
     mbar_init(bar, 1);
     mbar_init_fence();
+    mbar_init(bar_tma, 1);
+    mbar_init_fence();
+    // [Q;K] tile: Q rows 0..63 and K rows 64..127 of each 64-wide d-block
+    mbar_arrive_expect_tx(bar_tma, 32768);
+    const uint32_t base = smem_u32(qk);
+    for (int blk = 0; blk < 2; ++blk) {
+      tma_load_2d(base + blk * 16384, &tmap_q, hqk * kD + 64 * blk, static_cast<int>(t0), bar_tma);
+      tma_load_2d(base + blk * 16384 + 8192, &tmap_k, hqk * kD + 64 * blk, static_cast<int>(t0),
+                  bar_tma);
+    }
   }
 
-  load_qk_tile(qk, q, k, t0, L, hqk, tid, kPrepThreads);
-
-  // Gates for v-heads 2*hqk + j (j = tid / 64), token t = tid % 64.
+  // Gates for v-heads 2*hqk + j (j = tid / 64), token t = tid % 64, while the
+  // tile is in flight.
   {
     const int j = tid >> 6, t = tid & 63, hv = 2 * hqk + j;
     const bool valid = t < L;
@@ -289,6 +295,15 @@ gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
     }
   }
 
+  wait_phase(bar_tma, 0, broken);
+  if (L < kChunk) {
+    // rows past the sequence end hold the next sequence's tokens: zero them
+    for (int idx = tid; idx < 4 * (kChunk - L) * 8; idx += kPrepThreads) {
+      const int ch = idx & 7, rr = (idx >> 3) % (kChunk - L), blk = (idx >> 3) / (kChunk - L);
+      *reinterpret_cast<uint4 *>(qk + (blk >> 1) * 16384 + (blk & 1) * 8192 + (L + rr) * 128 +
+                                 ch * 16) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -317,6 +332,7 @@ gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
     tmem_ld32(trow + 32, *reinterpret_cast<float(*)[32]>(acc + 32));
     tmem_wait_ld();
     const int i = (warp & 1) * 32 + lane;
+    const bool rv = i < L;
     if (warp >= 2) {
       // A_j rows (fp32) into the retired [Q;K] region, 16-byte chunks
       // swizzled by (row & 15) so the row-per-thread stores do not conflict.
@@ -331,7 +347,7 @@ gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int col = 4 * m + u;
-            vals[u] = col < i ? acc[col] * expf(Gi - Gs[j * 64 + col]) * bi : 0.f;
+            vals[u] = (rv && col < i) ? acc[col] * __expf(Gi - Gs[j * 64 + col]) * bi : 0.f;
           }
           *reinterpret_cast<float4 *>(Arow + 4 * (m ^ (i & 15))) =
               make_float4(vals[0], vals[1], vals[2], vals[3]);
@@ -342,14 +358,13 @@ gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const float Gi = Gs[j * 64 + i];
-        const bool rv = i < L;
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           float vals[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int col = 8 * cc + u;
-            vals[u] = (rv && col <= i) ? acc[col] * expf(Gi - Gs[j * 64 + col]) : 0.f;
+            vals[u] = (rv && col <= i) ? acc[col] * __expf(Gi - Gs[j * 64 + col]) : 0.f;
           }
           uint4 pk;
           pk.x = pack_bf16x2(vals[0], vals[1]);
@@ -361,6 +376,7 @@ gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
       }
     }
   }
+  tc_fence_before();
   __syncthreads();
 
   // Forward substitution: thread (j, c) solves column c of (I + A_j)^-1 in
@@ -387,14 +403,12 @@ gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
       if (r == c) x[r] = 1.f;
       if (r < c) x[r] = 0.f;
     }
-    // Column c of Ainv_j -> rows 64..127 of the j-th [PA ; Ainv] image.
-    uint8_t *img = m2 + j * 16384;
+    // Column c of Ainv_j -> the j-th 64 x 64 bf16 tile (row r, swizzled).
+    uint8_t *img = ai + j * 8192;
 #pragma unroll
-    for (int r = 0; r < 64; ++r) {
-      const uint32_t R = 64 + r;
-      *reinterpret_cast<__nv_bfloat16 *>(img + R * 128 + (((c >> 3) ^ (R & 7)) << 4) +
+    for (int r = 0; r < 64; ++r)
+      *reinterpret_cast<__nv_bfloat16 *>(img + r * 128 + (((c >> 3) ^ (r & 7)) << 4) +
                                          (c & 7) * 2) = __float2bfloat16_rn(x[r]);
-    }
   }
 
   fence_async_smem();
@@ -402,34 +416,40 @@ gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
   __syncthreads();
   tc_fence_after();
 
-  // D_j[128 x 64] = [P_0 ; P_1] Ainv_j  (B = Ainv_j, MN-major: rows = K index).
+  // D_j[128 x 64] = [P_0 ; P_1] Ainv_j  (B = Ainv_j, MN-major: rows = K index),
+  // reusing TMEM columns 64 j .. 64 j + 63.
   if (tid == 0) {
     const uint32_t idesc = umma_idesc_bf16(128, 64, false, true);
     const uint32_t pbase = smem_u32(pp);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const uint32_t bbase = smem_u32(m2 + j * 16384 + 8192);
+      const uint32_t bbase = smem_u32(ai + j * 8192);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        umma_bf16(tmem + 64 + 64 * j, umma_desc_sw128(pbase + ks * 32, 16, 1024),
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + 64 * j, umma_desc_sw128(pbase + ks * 32, 16, 1024),
                   umma_desc_sw128(bbase + ks * 2048, 8192, 1024), idesc, ks > 0);
-      }
     }
     umma_commit(bar);
   }
+  // Ainv halves -> rows 64..127 of the workspace images while the MMA runs.
+  uint8_t *img0 = m2_ws + (static_cast<size_t>(gchunk) * kHV + 2 * hqk) * kM2Bytes;
+  for (int idx = tid; idx < 2 * 512; idx += kPrepThreads) {
+    const int j = idx >> 9, o = idx & 511;
+    reinterpret_cast<uint4 *>(img0 + j * kM2Bytes + 8192)[o] =
+        reinterpret_cast<const uint4 *>(ai + j * 8192)[o];
+  }
   wait_phase(bar, 1, broken);
   tc_fence_after();
-
   {
     // warps 0,1: rows 0..63 of D_0 = P_0 Ainv_0; warps 2,3: rows 64..127 of
-    // D_1 = P_1 Ainv_1.
+    // D_1 = P_1 Ainv_1.  Row i of P_j Ainv_j -> row i of image j.
     const int j = warp >> 1, i = (warp & 1) * 32 + lane;
     float acc[64];
-    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16) + 64 + 64 * j;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16) + 64 * j;
     tmem_ld32(trow, *reinterpret_cast<float(*)[32]>(acc));
     tmem_ld32(trow + 32, *reinterpret_cast<float(*)[32]>(acc + 32));
     tmem_wait_ld();
-    uint8_t *img = m2 + j * 16384;
+    uint8_t *img = img0 + j * kM2Bytes;
 #pragma unroll
     for (int cc = 0; cc < 8; ++cc) {
       uint4 pk;
@@ -442,283 +462,361 @@ gdn_prefill_prep_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
   }
   tc_fence_before();
   __syncthreads();
-
-  // Both images -> workspace (image index = chunk * 8 + v-head).
-  {
-    uint4 *dst = reinterpret_cast<uint4 *>(m2_ws + (static_cast<size_t>(gchunk) * kHV + 2 * hqk) * kM2Bytes);
-    const uint4 *src = reinterpret_cast<const uint4 *>(m2);
-    for (int idx = tid; idx < 2 * 1024; idx += kPrepThreads) dst[idx] = src[idx];
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kPrepTmemCols);
   }
-  if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 // ---------------------------------------------------------------------------
 // 3. sequential inter-chunk scan
 // ---------------------------------------------------------------------------
+// One CTA per (sequence, v-head), 256 threads.  The 128 v-rows of the state
+// sit on the 128 TMEM lanes: thread (quad q = warp % 4, lane l, half h =
+// warp / 4) owns row v = 32 q + l and column half h of every [v x 64] tile
+// (k-half h of the state).
+//   S      fp32 S[v][k] in registers (64 k per thread)
+//   TMEM   cols [0, 64)    bf16(S): A operand of MMA 1 (two bf16 per column)
+//          cols [128, 256) Yq | Yk, then O' | V_new, then dS
+// Per chunk (t = token of the chunk, L valid tokens):
+//   MMA 1   Yq = S Q^T, Yk = S K^T                    M=128, N=64+64, K=128
+//           X[v][t] = beta_t (V[t][v] - e^{G_t} Yk[v][t]),  Yq[v][t] *= e^{G_t}
+//   MMA 2   O' = Yq + X PA^T,  V_new = X Ainv^T       M=128, N=64+64, K=64
+//           out[t][v] = scale O'[v][t];  V_dec[v][t] = e^{G_last - G_t} V_new[v][t]
+//   MMA 3   dS = V_dec K                               M=128, N=128,   K=64
+//           S = e^{G_last} S + dS,  bf16(S) -> TMEM
+// Operands arrive by TMA (Q and K tiles with 128-byte swizzle, V tile plain)
+// and a bulk copy (the [PA;Ainv] image), each on its own mbarrier, issued as
+// soon as its buffer is free: Q after MMA 1, V after X, [PA;Ainv] after
+// MMA 2, K two chunks ahead (double buffered).
 constexpr int kScanThreads = 256;
 
-template <int VS>
 struct ScanSmem {
-  static constexpr int kQK = 0;                       // [Q;K] tile, 32 KB
-  static constexpr int kM2 = 32768;                   // [PA ; Ainv], 16 KB
-  static constexpr int kS = 49152;                    // bf16 S slice, MN-major
-  static constexpr int kSGroup = 16384;               // 128 K-rows x 128 B
-  static constexpr int kX = kS + (VS / 64) * kSGroup; // X / V_dec, MN-major
-  static constexpr int kXGroup = 8192;                // 64 K-rows x 128 B
-  static constexpr int kG = kX + (VS / 64) * kXGroup; // float G[64]
-  static constexpr int kB = kG + 256;                 // float beta[64]
-  static constexpr int kBar = kB + 256;
-  static constexpr int kTmem = kBar + 8;
-  static constexpr int kBroken = kBar + 12;
-  static constexpr int kBytes = kBar + 64 + 1024 + 16384;  // align slack + guard
-  static constexpr uint32_t kTmemCols = 2 * VS;
+  static constexpr int kQ = 0;         // Q tile: 2 d-blocks x 64 t x 128 B, 128-byte swizzle
+  static constexpr int kK0 = 16384;    // K tiles, same layout, double buffered
+  static constexpr int kK1 = 32768;
+  static constexpr int kM2 = 49152;    // [PA ; Ainv] image, 128 rows x 128 B
+  static constexpr int kXV = 65536;    // X, then V_dec: 128 v rows x 64 t, K-major (16 KB)
+  static constexpr int kV = 81920;     // V tile: 64 t rows x 128 v bf16, unswizzled (16 KB)
+  static constexpr int kG = 98304;     // float G[2][64]
+  static constexpr int kB = kG + 512;  // float beta[2][64]
+  static constexpr int kBar = kB + 512;
+  static constexpr int kBarMma = kBar, kBarQ = kBar + 8, kBarV = kBar + 16, kBarM2 = kBar + 24,
+                       kBarK0 = kBar + 32;  // kBarK1 = kBarK0 + 8
+  static constexpr int kTmem = kBar + 48;
+  static constexpr int kBroken = kBar + 52;
+  static constexpr int kBytes = kBar + 64 + 1024;  // + base alignment slack
+  static constexpr uint32_t kTmemCols = 256;
+  static constexpr uint32_t kColSb = 0, kColY = 128;
 };
 
-// Write n8 chunks of 8 bf16 (from fp32 vals) into row `row` of a 128-byte
-// swizzled operand whose 64-column groups are `gstride` bytes apart,
-// starting at column col0 (a multiple of 8).
-template <int NV>
-__device__ __forceinline__ void store_row_bf16(uint8_t *base, int row, int col0, const float *vals,
-                                               int gstride) {
-#pragma unroll
-  for (int i = 0; i < NV / 8; ++i) {
-    const int col = col0 + 8 * i;
-    uint4 pk;
-    pk.x = pack_bf16x2(vals[8 * i + 0], vals[8 * i + 1]);
-    pk.y = pack_bf16x2(vals[8 * i + 2], vals[8 * i + 3]);
-    pk.z = pack_bf16x2(vals[8 * i + 4], vals[8 * i + 5]);
-    pk.w = pack_bf16x2(vals[8 * i + 6], vals[8 * i + 7]);
-    *reinterpret_cast<uint4 *>(base + (col >> 6) * gstride + sw128(row, (col & 63) >> 3)) = pk;
-  }
+// Writes 16 fp32 as bf16 into row `row`, 16-byte chunks c0, c0+1 of a
+// 128-byte swizzled operand.
+__device__ __forceinline__ void store16_bf16(uint8_t *base, int row, int c0, const float *x) {
+  uint4 a, b;
+  a.x = pack_bf16x2(x[0], x[1]);
+  a.y = pack_bf16x2(x[2], x[3]);
+  a.z = pack_bf16x2(x[4], x[5]);
+  a.w = pack_bf16x2(x[6], x[7]);
+  b.x = pack_bf16x2(x[8], x[9]);
+  b.y = pack_bf16x2(x[10], x[11]);
+  b.z = pack_bf16x2(x[12], x[13]);
+  b.w = pack_bf16x2(x[14], x[15]);
+  *reinterpret_cast<uint4 *>(base + sw128(row, c0)) = a;
+  *reinterpret_cast<uint4 *>(base + sw128(row, c0 + 1)) = b;
 }
 
-template <int VS>
-__global__ void __launch_bounds__(kScanThreads, 1)
-gdn_prefill_scan_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
-                        const uint16_t *__restrict__ v, const float *h0,
+__global__ void __launch_bounds__(kScanThreads, 2)
+gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                        const __grid_constant__ CUtensorMap tmap_k,
+                        const __grid_constant__ CUtensorMap tmap_v, const float *h0,
                         const int64_t *__restrict__ cu, const int *__restrict__ meta,
                         const int *__restrict__ chunk_off, const int *__restrict__ seq_order,
                         const float *__restrict__ gcum_ws, const float *__restrict__ beta_ws,
-                        const uint8_t *__restrict__ m2_ws, float scale, uint16_t *__restrict__ out,
-                        float *final_state) {
-  using SM = ScanSmem<VS>;
-  constexpr int NSL = kD / VS;   // v-slices per head
-  constexpr int HALF = VS / 2;   // columns per thread
+                        const uint8_t *__restrict__ m2_ws, float scale,
+                        uint16_t *__restrict__ out, float *final_state) {
+  using SM = ScanSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(align_up(reinterpret_cast<size_t>(smem_raw), 1024));
   if (meta[1] != 0) return;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, hc = warp >> 2;
-  const int rank = blockIdx.x / (kHV * NSL);
-  const int rem = blockIdx.x % (kHV * NSL);
-  const int hv = rem / NSL, slice = rem % NSL;
+  const int vrow = 32 * quad + lane;  // state row (v) owned by this thread
+  const int hv = blockIdx.x % kHV;
   const int hqk = hv >> 1;
-  const int n = seq_order[rank];
+  const int n = seq_order[blockIdx.x / kHV];
   const int64_t bos = cu[n];
   const int64_t len = cu[n + 1] - bos;
   const int nchunks = static_cast<int>((len + kChunk - 1) / kChunk);
   const int gbase = chunk_off[n];
-  const int v0 = slice * VS;
-  const int vcol0 = hc * HALF;          // this thread's first column within the slice
-  const int drow = 32 * quad + lane;    // state k-index owned for dS / S
 
-  uint8_t *qk = smem + SM::kQK;
-  uint8_t *m2 = smem + SM::kM2;
-  uint8_t *sop = smem + SM::kS;
-  uint8_t *xv = smem + SM::kX;
+  uint8_t *xv = smem + SM::kXV;
+  const uint16_t *vt = reinterpret_cast<const uint16_t *>(smem + SM::kV);
   float *Gs = reinterpret_cast<float *>(smem + SM::kG);
   float *Bs = reinterpret_cast<float *>(smem + SM::kB);
   volatile int *broken = reinterpret_cast<volatile int *>(smem + SM::kBroken);
-  const uint32_t bar = smem_u32(smem + SM::kBar);
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t bar_mma = s_base + SM::kBarMma, bar_q = s_base + SM::kBarQ,
+                 bar_v = s_base + SM::kBarV, bar_m2 = s_base + SM::kBarM2,
+                 bar_k0 = s_base + SM::kBarK0;
 
-  if (warp == 0) tmem_alloc(smem_u32(smem + SM::kTmem), SM::kTmemCols);
+  if (warp == 0) tmem_alloc(s_base + SM::kTmem, SM::kTmemCols);
   if (tid == 0) {
     *broken = 0;
-    mbar_init(bar, 1);
+    for (int i = 0; i < 6; ++i) mbar_init(bar_mma + 8 * i, 1);
     mbar_init_fence();
   }
 
-  // fp32 state slice S[v0 + vcol0 + jj][drow] in registers.
-  float s[HALF];
-  const int64_t state_base = ((static_cast<int64_t>(n) * kHV + hv) * kD + v0 + vcol0) * kD + drow;
-#pragma unroll
-  for (int jj = 0; jj < HALF; ++jj) s[jj] = h0 != nullptr ? h0[state_base + jj * kD] : 0.f;
-  store_row_bf16<HALF>(sop, drow, vcol0, s, SM::kSGroup);
-
-  const uint32_t qk_s = smem_u32(qk), m2_s = smem_u32(m2), sop_s = smem_u32(sop),
-                 xv_s = smem_u32(xv);
-  const uint32_t idesc_y = umma_idesc_bf16(128, VS, false, true);
-  const uint32_t idesc_ds = umma_idesc_bf16(128, VS, true, true);
-  uint32_t phase = 0;
-  uint32_t tmem = 0;
-
-  for (int c = 0; c < nchunks; ++c) {
+  // Chunk operand loads, all issued by thread 0.
+  auto issue_qk = [&](bool is_k, int c, uint32_t dst, uint32_t bar) {
+    const int y = static_cast<int>(bos + static_cast<int64_t>(c) * kChunk);
+    mbar_arrive_expect_tx(bar, 16384);
+    const void *tm = is_k ? static_cast<const void *>(&tmap_k) : static_cast<const void *>(&tmap_q);
+    tma_load_2d(dst, tm, hqk * kD, y, bar);
+    tma_load_2d(dst + 8192, tm, hqk * kD + 64, y, bar);
+  };
+  auto issue_v = [&](int c) {
+    mbar_arrive_expect_tx(bar_v, 16384);
+    tma_load_2d(s_base + SM::kV, &tmap_v, hv * kD, static_cast<int>(bos + static_cast<int64_t>(c) * kChunk), bar_v);
+  };
+  auto issue_m2 = [&](int c) {
+    mbar_arrive_expect_tx(bar_m2, static_cast<uint32_t>(kM2Bytes));
+    bulk_load(s_base + SM::kM2, m2_ws + (static_cast<int64_t>(gbase + c) * kHV + hv) * kM2Bytes,
+              static_cast<uint32_t>(kM2Bytes), bar_m2);
+  };
+  auto load_gates = [&](int c, int buf) {  // threads 0..63
     const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
     const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
-    const int64_t gidx = gbase + c;
+    const bool valid = tid < L;
+    Gs[buf * 64 + tid] = gcum_ws[(t0 + (valid ? tid : L - 1)) * kHV + hv];
+    Bs[buf * 64 + tid] = valid ? beta_ws[(t0 + tid) * kHV + hv] : 0.f;
+  };
 
-    // ---- stage this chunk's operands ----
-    load_qk_tile(qk, q, k, t0, L, hqk, tid, kScanThreads);
-    {
-      const uint4 *src = reinterpret_cast<const uint4 *>(m2_ws + (gidx * kHV + hv) * kM2Bytes);
-      uint4 *dst = reinterpret_cast<uint4 *>(m2);
-      for (int idx = tid; idx < 1024; idx += kScanThreads) dst[idx] = __ldg(src + idx);
-    }
-    const float g_last = gcum_ws[(t0 + L - 1) * kHV + hv];
-    if (tid < 64) {
-      const bool valid = tid < L;
-      Gs[tid] = valid ? gcum_ws[(t0 + tid) * kHV + hv] : g_last;
-      Bs[tid] = valid ? beta_ws[(t0 + tid) * kHV + hv] : 0.f;
-    }
-    // V row of this thread's token (quadrants 2,3), kept as packed bf16
-    // pairs until X is formed; the loads overlap MMA 1.
-    uint4 vpk[HALF / 8];
-    const int tok = 32 * (quad & 1) + lane;
-    if (quad >= 2) {
-      const uint4 *src = reinterpret_cast<const uint4 *>(
-          v + ((t0 + tok) * kHV + hv) * kD + v0 + vcol0);
+  // fp32 state row slice S[v][64 hc .. 64 hc + 63].
+  float s[64];
+  const int64_t srow = ((static_cast<int64_t>(n) * kHV + hv) * kD + vrow) * kD + 64 * hc;
+  if (h0 != nullptr) {
 #pragma unroll
-      for (int i = 0; i < HALF / 8; ++i)
-        vpk[i] = tok < L ? __ldg(src + i) : make_uint4(0u, 0u, 0u, 0u);
+    for (int i = 0; i < 16; ++i) {
+      const float4 x = *reinterpret_cast<const float4 *>(h0 + srow + 4 * i);
+      s[4 * i] = x.x;
+      s[4 * i + 1] = x.y;
+      s[4 * i + 2] = x.z;
+      s[4 * i + 3] = x.w;
     }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    tmem = *reinterpret_cast<volatile uint32_t *>(smem + SM::kTmem);
-    const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-
-    // ---- MMA 1: Y[128 x VS] = [Q;K] S^T ----
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) s[i] = 0.f;
+  }
+  __syncthreads();  // barriers initialised, TMEM address published
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + SM::kTmem);
+  const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * quad) << 16);
+  {
+    uint32_t pk[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(s[2 * j], s[2 * j + 1]);
+    tmem_st32(tlane + SM::kColSb + 32 * hc, pk);
+  }
+  if (nchunks > 0) {
     if (tid == 0) {
+      issue_qk(false, 0, s_base + SM::kQ, bar_q);
+      issue_qk(true, 0, s_base + SM::kK0, bar_k0);
+      if (nchunks > 1) issue_qk(true, 1, s_base + SM::kK1, bar_k0 + 8);
+      issue_v(0);
+      issue_m2(0);
+    }
+    if (tid < 64) load_gates(0, 0);
+  }
+  tmem_wait_st();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t idesc_n64 = umma_idesc_bf16(128, 64, false, false);
+  const uint32_t idesc_ds = umma_idesc_bf16(128, 128, false, true);
+  uint32_t ph_mma = 0, ph_q = 0, ph_v = 0, ph_m2 = 0, ph_k = 0;  // ph_k: bit b = parity of K buffer b
+
+  for (int c = 0; c < nchunks; ++c) {
+    const int cb = c & 1;
+    const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
+    const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
+    const float g_last = Gs[cb * 64 + L - 1];
+    const uint32_t kbuf = s_base + (cb ? SM::kK1 : SM::kK0);
+    const uint32_t bar_k = bar_k0 + 8 * cb;
+
+    // Q, K and [PA;Ainv] are read only by the tensor core, so only the MMA
+    // thread waits for them: thread 0 re-arms each barrier for the next chunk
+    // right after the MMA that consumed it, and a thread still polling the
+    // old phase could otherwise see two completions and wait forever.  The
+    // one exception is the tail chunk (always the last, so never re-armed):
+    // every thread must see its tiles landed before zeroing rows.
+    const bool tail = L < kChunk;
+    if (tid == 0 || tail) {
+      wait_phase(bar_q, ph_q, broken);
+      wait_phase(bar_k, (ph_k >> cb) & 1, broken);
+    }
+    ph_q ^= 1;
+    ph_k ^= 1u << cb;
+    if (tail) {
+      // tail chunk: zero the rows past the sequence end (TMA brought in the
+      // next sequence's tokens there)
+      for (int idx = tid; idx < 2 * 2 * (kChunk - L) * 8; idx += kScanThreads) {
+        const int ch = idx & 7, r = L + ((idx >> 3) % (kChunk - L)), blk = (idx >> 3) / (kChunk - L);
+        const int which = blk >> 1, dblk = blk & 1;
+        uint8_t *tile = smem + (which ? (cb ? SM::kK1 : SM::kK0) : SM::kQ);
+        *reinterpret_cast<uint4 *>(tile + dblk * 8192 + r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+      }
+      fence_async_smem();
+      __syncthreads();
+    }
+
+    // ---- MMA 1: Yq = S Q^T, Yk = S K^T ----
+    if (tid == 0) {
+      tc_fence_after();
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
-        umma_bf16(tmem, umma_desc_sw128(qk_s + aoff, 16, 1024),
-                  umma_desc_sw128(sop_s + ks * 2048, SM::kSGroup, 1024), idesc_y, ks > 0);
+        const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
+        umma_bf16_ts(tmem + SM::kColY, tmem + SM::kColSb + 8 * ks,
+                     umma_desc_sw128(s_base + SM::kQ + boff, 16, 1024), idesc_n64, ks > 0);
       }
-      umma_commit(bar);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
+        umma_bf16_ts(tmem + SM::kColY + 64, tmem + SM::kColSb + 8 * ks,
+                     umma_desc_sw128(kbuf + boff, 16, 1024), idesc_n64, ks > 0);
+      }
+      umma_commit(bar_mma);
     }
-    wait_phase(bar, phase, broken);
-    phase ^= 1;
+    wait_phase(bar_mma, ph_mma, broken);
+    ph_mma ^= 1;
     tc_fence_after();
+    if (tid == 0 && c + 1 < nchunks) issue_qk(false, c + 1, s_base + SM::kQ, bar_q);
+    wait_phase(bar_v, ph_v, broken);
+    ph_v ^= 1;
 
-    if (quad >= 2) {
-      // X = beta * (V - e^G * (K S^T)) for token `tok`, 32 columns at a time
-      const float eg = expf(Gs[tok]), bt = Bs[tok];
+    // ---- X = beta (V - e^G Yk) -> smem;  Yq *= e^G in TMEM ----
 #pragma unroll
-      for (int p = 0; p < HALF / 32; ++p) {
-        float y[32];
-        tmem_ld32(tlane + vcol0 + 32 * p, y);
-        tmem_wait_ld();
+    for (int p = 0; p < 2; ++p) {
+      const int tb = 32 * hc + 16 * p;
+      float yk[16], yq[16];
+      tmem_ld16(tlane + SM::kColY + 64 + tb, yk);
+      tmem_ld16(tlane + SM::kColY + tb, yq);
+      tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 w = vpk[4 * p + i];
-          const float vv[8] = {bf16_lo(w.x), bf16_hi(w.x), bf16_lo(w.y), bf16_hi(w.y),
-                               bf16_lo(w.z), bf16_hi(w.z), bf16_lo(w.w), bf16_hi(w.w)};
-#pragma unroll
-          for (int u = 0; u < 8; ++u) y[8 * i + u] = bt * (vv[u] - eg * y[8 * i + u]);
-        }
-        store_row_bf16<32>(xv, tok, vcol0 + 32 * p, y, SM::kXGroup);
+      for (int j = 0; j < 16; ++j) {
+        const int t = tb + j;
+        const float eg = expf(Gs[cb * 64 + t]);
+        const float vv = t < L ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
+        yk[j] = Bs[cb * 64 + t] * (vv - eg * yk[j]);
+        yq[j] *= eg;
       }
+      store16_bf16(xv, vrow, tb >> 3, yk);
+      uint32_t u[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) u[j] = __float_as_uint(yq[j]);
+      tmem_st16(tlane + SM::kColY + tb, u);
+    }
+    tmem_wait_st();
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0 && c + 1 < nchunks) issue_v(c + 1);
+
+    // ---- MMA 2: O' = Yq + X PA^T, V_new = X Ainv^T ----
+    if (tid == 0) {
+      wait_phase(bar_m2, ph_m2, broken);
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + SM::kColY, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
+                  umma_desc_sw128(s_base + SM::kM2 + ks * 32, 16, 1024), idesc_n64, 1);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + SM::kColY + 64, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
+                  umma_desc_sw128(s_base + SM::kM2 + 8192 + ks * 32, 16, 1024), idesc_n64,
+                  ks > 0);
+      umma_commit(bar_mma);
+    }
+    ph_m2 ^= 1;
+    wait_phase(bar_mma, ph_mma, broken);
+    ph_mma ^= 1;
+    tc_fence_after();
+    if (tid == 0 && c + 1 < nchunks) issue_m2(c + 1);
+
+    // ---- outputs and V_dec ----
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int tb = 32 * hc + 16 * p;
+      float zo[16], zv[16];
+      tmem_ld16(tlane + SM::kColY + tb, zo);
+      tmem_ld16(tlane + SM::kColY + 64 + tb, zv);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = tb + j;
+        if (t < L) {
+          out[((t0 + t) * kHV + hv) * kD + vrow] =
+              __bfloat16_as_ushort(__float2bfloat16_rn(scale * zo[j]));
+          zv[j] *= expf(g_last - Gs[cb * 64 + t]);
+        } else {
+          zv[j] = 0.f;
+        }
+      }
+      store16_bf16(xv, vrow, tb >> 3, zv);
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
 
-    // ---- MMA 2: Z[128 x VS] = [PA ; Ainv] X ----
+    // ---- MMA 3: dS = V_dec K ----
     if (tid == 0) {
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        umma_bf16(tmem + VS, umma_desc_sw128(m2_s + ks * 32, 16, 1024),
-                  umma_desc_sw128(xv_s + ks * 2048, SM::kXGroup, 1024), idesc_y, ks > 0);
-      }
-      umma_commit(bar);
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + SM::kColY, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
+                  umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), idesc_ds, ks > 0);
+      umma_commit(bar_mma);
     }
-    wait_phase(bar, phase, broken);
-    phase ^= 1;
+    if (tid < 64 && c + 1 < nchunks) load_gates(c + 1, cb ^ 1);
+    wait_phase(bar_mma, ph_mma, broken);
+    ph_mma ^= 1;
     tc_fence_after();
+    if (tid == 0 && c + 2 < nchunks) issue_qk(true, c + 2, kbuf, bar_k);
 
-    if (quad < 2) {
-      // O = scale * (e^G * (Q S^T) + P Ainv X) for token `tok`
-      const float eg = expf(Gs[tok]);
-      uint4 *dst = reinterpret_cast<uint4 *>(out + ((t0 + tok) * kHV + hv) * kD + v0 + vcol0);
-#pragma unroll
-      for (int p = 0; p < HALF / 32; ++p) {
-        float y[32], z[32];
-        tmem_ld32(tlane + vcol0 + 32 * p, y);
-        tmem_ld32(tlane + VS + vcol0 + 32 * p, z);
-        tmem_wait_ld();
-        if (tok < L) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float o8[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) o8[u] = scale * (eg * y[8 * i + u] + z[8 * i + u]);
-            uint4 pk;
-            pk.x = pack_bf16x2(o8[0], o8[1]);
-            pk.y = pack_bf16x2(o8[2], o8[3]);
-            pk.z = pack_bf16x2(o8[4], o8[5]);
-            pk.w = pack_bf16x2(o8[6], o8[7]);
-            dst[4 * p + i] = pk;
-          }
-        }
-      }
-    } else {
-      // V_dec = e^{G_last - G} * V_new, zero past the chunk's end
-      const float dec = tok < L ? expf(g_last - Gs[tok]) : 0.f;
-#pragma unroll
-      for (int p = 0; p < HALF / 32; ++p) {
-        float z[32];
-        tmem_ld32(tlane + VS + vcol0 + 32 * p, z);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) z[i] *= dec;
-        store_row_bf16<32>(xv, tok, vcol0 + 32 * p, z, SM::kXGroup);
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-
-    // ---- MMA 3: dS^T[128 (k) x VS] = K^T V_dec ----
-    if (tid == 0) {
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        umma_bf16(tmem, umma_desc_sw128(qk_s + 8192 + ks * 2048, 16384, 1024),
-                  umma_desc_sw128(xv_s + ks * 2048, SM::kXGroup, 1024), idesc_ds, ks > 0);
-      }
-      umma_commit(bar);
-    }
-    wait_phase(bar, phase, broken);
-    phase ^= 1;
-    tc_fence_after();
+    // ---- S = e^{G_last} S + dS ;  bf16(S) -> TMEM ----
     {
       const float eg_last = expf(g_last);
 #pragma unroll
-      for (int p = 0; p < HALF / 32; ++p) {
+      for (int p = 0; p < 2; ++p) {
         float ds[32];
-        tmem_ld32(tlane + vcol0 + 32 * p, ds);
+        tmem_ld32(tlane + SM::kColY + 64 * hc + 32 * p, ds);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 * p + i] = eg_last * s[32 * p + i] + ds[i];
-        store_row_bf16<32>(sop, drow, vcol0 + 32 * p, s + 32 * p, SM::kSGroup);
+        for (int j = 0; j < 32; ++j) s[32 * p + j] = eg_last * s[32 * p + j] + ds[j];
       }
+      uint32_t pk[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(s[2 * j], s[2 * j + 1]);
+      tmem_st32(tlane + SM::kColSb + 32 * hc, pk);
     }
+    tmem_wait_st();
     tc_fence_before();
     __syncthreads();
+    tc_fence_after();
   }
 
 #pragma unroll
-  for (int jj = 0; jj < HALF; ++jj) final_state[state_base + jj * kD] = s[jj];
+  for (int i = 0; i < 16; ++i)
+    *reinterpret_cast<float4 *>(final_state + srow + 4 * i) =
+        make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
 
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem = *reinterpret_cast<volatile uint32_t *>(smem + SM::kTmem);
     tmem_dealloc(tmem, SM::kTmemCols);
   }
 }
@@ -728,22 +826,33 @@ gdn_prefill_scan_kernel(const uint16_t *__restrict__ q, const uint16_t *__restri
 // ---------------------------------------------------------------------------
 size_t prefill_workspace_bytes(int64_t T, int64_t N) { return prefill_ws_layout(T, N).total; }
 
-template <int VS>
-static cudaError_t launch_scan(const void *q, const void *k, const void *v, const float *state,
-                               const int64_t *cu, const int *meta, const int *chunk_off,
-                               const int *seq_order, const float *gcum, const float *beta,
-                               const uint8_t *m2, float scale, void *out, float *final_state,
-                               int64_t N, cudaStream_t stream) {
-  using SM = ScanSmem<VS>;
-  cudaError_t err = cudaFuncSetAttribute(gdn_prefill_scan_kernel<VS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SM::kBytes);
-  if (err != cudaSuccess) return err;
-  const int64_t blocks = N * kHV * (kD / VS);
-  gdn_prefill_scan_kernel<VS><<<static_cast<unsigned>(blocks), kScanThreads, SM::kBytes, stream>>>(
-      static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
-      static_cast<const uint16_t *>(v), state, cu, meta, chunk_off, seq_order, gcum, beta, m2,
-      scale, static_cast<uint16_t *>(out), final_state);
-  return cudaGetLastError();
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2D bf16 tensor map over a [rows, row_elems] row-major tensor.
+static bool make_tmap_2d(CUtensorMap *m, const void *base, uint64_t row_elems, uint64_t rows,
+                         uint32_t box_x, uint32_t box_y, bool swizzle128) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {row_elems, rows};
+  const cuuint64_t strides[1] = {row_elems * 2};
+  const cuuint32_t box[2] = {box_x, box_y};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 cudaError_t launch_prefill(const void *q, const void *k, const void *v, const float *state,
@@ -751,6 +860,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
                            const int64_t *cu_seqlens, int64_t N, int64_t T, float scale,
                            void *out, float *final_state, void *workspace, int num_sms,
                            cudaStream_t stream) {
+  (void)num_sms;
   if (N == 0) return cudaSuccess;
   const PrefillWs w = prefill_ws_layout(T, N);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
@@ -761,6 +871,17 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   float *gcum = reinterpret_cast<float *>(ws + w.gcum);
   float *beta = reinterpret_cast<float *>(ws + w.beta);
   uint8_t *m2 = ws + w.m2;
+
+  CUtensorMap tq, tk, tv;
+  memset(&tq, 0, sizeof(tq));
+  memset(&tk, 0, sizeof(tk));
+  memset(&tv, 0, sizeof(tv));
+  if (T > 0) {
+    if (!make_tmap_2d(&tq, q, kHQK * kD, T, 64, 64, true) ||
+        !make_tmap_2d(&tk, k, kHQK * kD, T, 64, 64, true) ||
+        !make_tmap_2d(&tv, v, kHV * kD, T, kD, 64, false))
+      return cudaErrorInvalidValue;
+  }
 
   gdn_prefill_meta_kernel<<<1, kMetaThreads, 0, stream>>>(cu_seqlens, static_cast<int>(N), T,
                                                           w.nt_max, meta, chunk_off, seq_order,
@@ -774,20 +895,19 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   if (w.nt_max > 0) {
     dim3 grid(static_cast<unsigned>(w.nt_max), kHQK);
     gdn_prefill_prep_kernel<<<grid, kPrepThreads, kPrepSmem, stream>>>(
-        static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k), A_log,
-        static_cast<const uint16_t *>(a), dt_bias, static_cast<const uint16_t *>(b), cu_seqlens,
-        meta, chunk_tab, gcum, beta, m2);
+        tq, tk, A_log, static_cast<const uint16_t *>(a), dt_bias,
+        static_cast<const uint16_t *>(b), cu_seqlens, meta, chunk_tab, gcum, beta, m2);
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
   }
-  // Few recurrences: split each head's 128 v-rows over two CTAs for more
-  // parallelism along the sequential scan; otherwise one CTA per head.
-  const bool split = N * kHV * 2 <= static_cast<int64_t>(num_sms);
-  if (split)
-    return launch_scan<64>(q, k, v, state, cu_seqlens, meta, chunk_off, seq_order, gcum, beta,
-                           m2, scale, out, final_state, N, stream);
-  return launch_scan<128>(q, k, v, state, cu_seqlens, meta, chunk_off, seq_order, gcum, beta, m2,
-                          scale, out, final_state, N, stream);
+  err = cudaFuncSetAttribute(gdn_prefill_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             ScanSmem::kBytes);
+  if (err != cudaSuccess) return err;
+  gdn_prefill_scan_kernel<<<static_cast<unsigned>(N * kHV), kScanThreads, ScanSmem::kBytes,
+                            stream>>>(tq, tk, tv, state, cu_seqlens, meta, chunk_off, seq_order,
+                                      gcum, beta, m2, scale, static_cast<uint16_t *>(out),
+                                      final_state);
+  return cudaGetLastError();
 }
 
 }  // namespace gdn

@@ -69,7 +69,7 @@ extern "C" int gdn_prefill_qk4_v8_d128_k_last_noalloc(
   if (!cu_seqlens || !A_log || !dt_bias || !final_state) return GDN_ERR_NULL_POINTER;
   if (total_tokens > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL_POINTER;
   if ((q && !aligned(q, 16)) || (k && !aligned(k, 16)) || (v && !aligned(v, 16)) ||
-      (out && !aligned(out, 16)) || !aligned(final_state, 4) || (state && !aligned(state, 4)) ||
+      (out && !aligned(out, 16)) || !aligned(final_state, 16) || (state && !aligned(state, 16)) ||
       !aligned(cu_seqlens, 8))
     return GDN_ERR_MISALIGNED;
   const size_t state_bytes = static_cast<size_t>(num_seqs) * gdn::kHV * gdn::kD * gdn::kD * 4;
