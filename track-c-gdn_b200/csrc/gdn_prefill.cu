@@ -84,29 +84,32 @@ __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Wait for an mbarrier phase; gives up after ~4 s (or at once when another
-// thread of the CTA already gave up), records device status 2 and returns
-// false.  A CTA that gave up finishes its loop without waiting again and
-// still deallocates its TMEM.
-__device__ __noinline__ bool wait_phase(uint32_t mbar, uint32_t parity, volatile int *broken) {
-  if (*broken) return false;
-  const uint64_t t0 = globaltimer_ns();
+// Slow path of wait_phase: keep polling, give up after 2^33 SM cycles
+// (about 4 s at the B200's top clock, longer at lower clocks) or at once
+// when another thread of the CTA already gave up; records device status 2.
+// A CTA that gave up finishes its loop without waiting again and still
+// deallocates its TMEM.
+__device__ __noinline__ bool wait_phase_slow(uint32_t mbar, uint32_t parity, volatile int *broken) {
+  const long long t0 = clock64();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(mbar, parity)) return true;
     if (*broken) return false;
-    if (globaltimer_ns() - t0 > 4000000000ull) {
+    if (clock64() - t0 > (1ll << 33)) {
       *broken = 1;
       set_device_status(kDevStatusWaitTimeout);
       return false;
     }
   }
+}
+
+// Wait for an mbarrier phase: one try_wait (which itself suspends the warp
+// for a while) covers the common case; only a still-pending phase takes the
+// bounded slow path.
+__device__ __forceinline__ bool wait_phase(uint32_t mbar, uint32_t parity, volatile int *broken) {
+  if (mbar_try_wait(mbar, parity)) return true;
+  if (*broken) return false;
+  return wait_phase_slow(mbar, parity, broken);
 }
 
 // ---------------------------------------------------------------------------
@@ -214,12 +217,93 @@ constexpr int kPrepPP = 32768;      // [P_0 ; P_1] bf16, K-major 128 x 64, 16 KB
 constexpr int kPrepAI = 49152;      // Ainv_0, Ainv_1 bf16, 64 x 64 each (2 x 8 KB)
 constexpr int kPrepG = 65536;       // float G[2][64]
 constexpr int kPrepB = kPrepG + 512;    // float beta[2][64]
-constexpr int kPrepWt = kPrepB + 512;   // float warp totals[4]
+constexpr int kPrepGn = kPrepB + 512;   // float gnext[2][64]: e^{gl_{t+1}} (1 at t = 63)
+constexpr int kPrepWt = kPrepGn + 512;  // float warp totals[4]
 constexpr int kPrepBar = kPrepWt + 16;  // mbarriers: mma, tma
 constexpr int kPrepTmem = kPrepBar + 16;
 constexpr int kPrepBroken = kPrepTmem + 4;
 constexpr int kPrepSmem = kPrepBroken + 12 + 1024;  // + base alignment slack
 constexpr uint32_t kPrepTmemCols = 128;
+
+// Column c of (I + A)^-1 for a strictly lower-triangular 64 x 64 fp32 A given
+// transposed (AT[col * 64 + row]), by blocked forward substitution in fp32:
+// rows in blocks of 16; the earlier blocks' contribution is a loop over
+// their x values (kept in this thread's TMEM lane at columns txs..txs+63,
+// float4 broadcast reads of AT), the 16 x 16 triangle inside the block is
+// unrolled.  The loops keep the code small enough to stay in the
+// instruction cache.  Blocks that lie wholly above this warp's first column
+// (`c_warp`) are zero and skipped.  Writes the column as bf16 into the
+// 64 x 64 tile `img` (128-byte rows, 128-byte swizzle).
+__device__ __forceinline__ void solve_unit_lower_column(const float *AT, int c, int c_warp,
+                                                        uint32_t txs, uint8_t *img) {
+#pragma unroll 1
+  for (int blk = 0; blk < 4; ++blk) {
+    const int r0 = 16 * blk;
+    float xb[16];
+    if (r0 + 16 <= c_warp) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) xb[i] = 0.f;
+    } else {
+      float acc[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+      // the earlier blocks' x values, fetched from TMEM in one round trip
+      float xprev[48];
+      const int pb0 = c_warp >> 4;
+#pragma unroll
+      for (int pb = 0; pb < 3; ++pb)
+        if (pb >= pb0 && pb < blk)
+          tmem_ld16(txs + 16 * pb, *reinterpret_cast<float(*)[16]>(xprev + 16 * pb));
+      tmem_wait_ld();
+#pragma unroll
+      for (int pb = 0; pb < 3; ++pb) {
+        if (pb < pb0 || pb >= blk) continue;
+        const float *xp = xprev + 16 * pb;
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const float4 *col = reinterpret_cast<const float4 *>(AT + (16 * pb + jj) * 64 + r0);
+          const float4 a0 = col[0], a1 = col[1], a2 = col[2], a3 = col[3];
+          const float xj = xp[jj];
+          acc[0] += a0.x * xj;
+          acc[1] += a0.y * xj;
+          acc[2] += a0.z * xj;
+          acc[3] += a0.w * xj;
+          acc[4] += a1.x * xj;
+          acc[5] += a1.y * xj;
+          acc[6] += a1.z * xj;
+          acc[7] += a1.w * xj;
+          acc[8] += a2.x * xj;
+          acc[9] += a2.y * xj;
+          acc[10] += a2.z * xj;
+          acc[11] += a2.w * xj;
+          acc[12] += a3.x * xj;
+          acc[13] += a3.y * xj;
+          acc[14] += a3.z * xj;
+          acc[15] += a3.w * xj;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float s = acc[i];
+#pragma unroll
+        for (int jp = 0; jp < i; ++jp) s += AT[(r0 + jp) * 64 + r0 + i] * xb[jp];
+        const int r = r0 + i;
+        xb[i] = (r == c) ? 1.f : (r < c ? 0.f : -s);
+      }
+    }
+    uint32_t u[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(xb[i]);
+    tmem_st16(txs + 16 * blk, u);
+    tmem_wait_st();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int r = r0 + i;
+      *reinterpret_cast<__nv_bfloat16 *>(img + r * 128 + (((c >> 3) ^ (r & 7)) << 4) +
+                                         (c & 7) * 2) = __float2bfloat16_rn(xb[i]);
+    }
+  }
+}
 
 __global__ void __launch_bounds__(kPrepThreads)
 gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -245,6 +329,7 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   uint8_t *ai = smem + kPrepAI;
   float *Gs = reinterpret_cast<float *>(smem + kPrepG);
   float *Bs = reinterpret_cast<float *>(smem + kPrepB);
+  float *Gn = reinterpret_cast<float *>(smem + kPrepGn);
   float *wt = reinterpret_cast<float *>(smem + kPrepWt);
   volatile int *broken = reinterpret_cast<volatile int *>(smem + kPrepBroken);
   const uint32_t bar = smem_u32(smem + kPrepBar), bar_tma = bar + 8;
@@ -288,6 +373,10 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     if (warp & 1) x += wt[warp - 1];
     Gs[j * 64 + t] = x;
     Bs[j * 64 + t] = bt;
+    // per-token decay e^{gl_t} (1 past the end), stored one slot down so that
+    // gnext[c] = e^{gl_{c+1}}: the factor that extends a row's running decay
+    // product from column c+1 to column c
+    Gn[j * 64 + (t == 0 ? 63 : t - 1)] = t == 0 ? 1.f : expf(gl);
     if (valid) {
       const int64_t idx = (t0 + t) * kHV + hv;
       gcum_ws[idx] = x;
@@ -325,46 +414,49 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   wait_phase(bar, 0, broken);
   tc_fence_after();
 
+  // A_j^T (fp32, into the retired [Q;K] region: AT[j][col][row], so a warp's
+  // stores for one column are 32 consecutive floats) from the K K^T rows
+  // (warps 2,3) and P_j (bf16 operand rows) from the Q K^T rows (warps 0,1),
+  // eight accumulator columns at a time, right to left: the decay factor
+  // e^{G_i - G_c} = prod_{k=c+1..i} e^{gl_k} of row i is a running product
+  // (no per-entry exponential; exact to fp32 rounding, never overflows).
+  float *AT = reinterpret_cast<float *>(smem + kPrepQK);
   {
-    float acc[64];
+    const int i = (warp & 1) * 32 + lane;
+    const bool rv = i < L;
     const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    float acc[64];  // row i of Q K^T (warps 0,1) or K K^T (warps 2,3): one TMEM round trip
     tmem_ld32(trow, *reinterpret_cast<float(*)[32]>(acc));
     tmem_ld32(trow + 32, *reinterpret_cast<float(*)[32]>(acc + 32));
     tmem_wait_ld();
-    const int i = (warp & 1) * 32 + lane;
-    const bool rv = i < L;
-    if (warp >= 2) {
-      // A_j rows (fp32) into the retired [Q;K] region, 16-byte chunks
-      // swizzled by (row & 15) so the row-per-thread stores do not conflict.
-      float *Abuf = reinterpret_cast<float *>(smem + kPrepQK);
+#pragma unroll 1
+    for (int j = 0; j < 2; ++j) {
+      const float bi = Bs[j * 64 + i];
+      float dec = 1.f;  // e^{G_i - G_c} for the current column c (1 for c >= i)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float Gi = Gs[j * 64 + i], bi = Bs[j * 64 + i];
-        float *Arow = Abuf + (j * 64 + i) * 64;
+      for (int cc = 7; cc >= 0; --cc) {
+        const float4 g0 = *reinterpret_cast<const float4 *>(Gn + j * 64 + 8 * cc);
+        const float4 g1 = *reinterpret_cast<const float4 *>(Gn + j * 64 + 8 * cc + 4);
+        const float gn[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        float dc[8];
 #pragma unroll
-        for (int m = 0; m < 16; ++m) {
-          float vals[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int col = 4 * m + u;
-            vals[u] = (rv && col < i) ? acc[col] * __expf(Gi - Gs[j * 64 + col]) * bi : 0.f;
-          }
-          *reinterpret_cast<float4 *>(Arow + 4 * (m ^ (i & 15))) =
-              make_float4(vals[0], vals[1], vals[2], vals[3]);
+        for (int u = 7; u >= 0; --u) {
+          if (8 * cc + u < i) dec *= gn[u];
+          dc[u] = dec;
         }
-      }
-    } else {
-      // P_j rows (bf16) into the [P_0 ; P_1] operand.
+        const float *a8 = acc + 8 * cc;
+        if (warp >= 2) {
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float Gi = Gs[j * 64 + i];
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
+          for (int u = 0; u < 8; ++u) {
+            const int col = 8 * cc + u;
+            AT[(j * 64 + col) * 64 + i] = (rv && col < i) ? a8[u] * dc[u] * bi : 0.f;
+          }
+        } else {
           float vals[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int col = 8 * cc + u;
-            vals[u] = (rv && col <= i) ? acc[col] * __expf(Gi - Gs[j * 64 + col]) : 0.f;
+            vals[u] = (rv && col <= i) ? a8[u] * dc[u] : 0.f;
           }
           uint4 pk;
           pk.x = pack_bf16x2(vals[0], vals[1]);
@@ -378,37 +470,15 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   }
   tc_fence_before();
   __syncthreads();
+  tc_fence_after();
 
-  // Forward substitution: thread (j, c) solves column c of (I + A_j)^-1 in
-  // fp32; the rows of A_j are broadcast reads from shared memory.
+  // Forward substitution: thread (j = tid / 64, c = tid % 64) solves column c
+  // of (I + A_j)^-1; its x values live in its own TMEM lane, columns 64..127
+  // (idle until the P Ainv MMA below).
   {
     const int j = tid >> 6, c = tid & 63;
-    const float *Aj = reinterpret_cast<const float *>(smem + kPrepQK) + j * 64 * 64;
-    float x[64];
-#pragma unroll
-    for (int r = 0; r < 64; ++r) x[r] = 0.f;
-    if (c == 0) x[0] = 1.f;
-#pragma unroll
-    for (int r = 1; r < 64; ++r) {
-      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-      for (int m = 0; m < (r + 3) / 4; ++m) {
-        const float4 av = *reinterpret_cast<const float4 *>(Aj + r * 64 + 4 * (m ^ (r & 15)));
-        s0 += av.x * x[4 * m + 0];
-        s1 += av.y * x[4 * m + 1];
-        s2 += av.z * x[4 * m + 2];
-        s3 += av.w * x[4 * m + 3];
-      }
-      x[r] = -((s0 + s1) + (s2 + s3));
-      if (r == c) x[r] = 1.f;
-      if (r < c) x[r] = 0.f;
-    }
-    // Column c of Ainv_j -> the j-th 64 x 64 bf16 tile (row r, swizzled).
-    uint8_t *img = ai + j * 8192;
-#pragma unroll
-    for (int r = 0; r < 64; ++r)
-      *reinterpret_cast<__nv_bfloat16 *>(img + r * 128 + (((c >> 3) ^ (r & 7)) << 4) +
-                                         (c & 7) * 2) = __float2bfloat16_rn(x[r]);
+    solve_unit_lower_column(AT + j * 4096, c, 32 * (warp & 1),
+                            tmem + (static_cast<uint32_t>(32 * warp) << 16) + 64, ai + j * 8192);
   }
 
   fence_async_smem();
@@ -477,7 +547,8 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // (k-half h of the state).
 //   S      fp32 S[v][k] in registers (64 k per thread)
 //   TMEM   cols [0, 64)    bf16(S): A operand of MMA 1 (two bf16 per column)
-//          cols [128, 256) Yq | Yk, then O' | V_new, then dS
+//          cols [64, 128)  O_intra = X PA^T
+//          cols [128, 256) Yq | Yk, then Yq | V_new, then dS
 // Per chunk (t = token of the chunk, L valid tokens):
 //   MMA 1   Yq = S Q^T, Yk = S K^T                    M=128, N=64+64, K=128
 //           X[v][t] = beta_t (V[t][v] - e^{G_t} Yk[v][t]),  Yq[v][t] *= e^{G_t}
@@ -498,16 +569,20 @@ struct ScanSmem {
   static constexpr int kM2 = 49152;    // [PA ; Ainv] image, 128 rows x 128 B
   static constexpr int kXV = 65536;    // X, then V_dec: 128 v rows x 64 t, K-major (16 KB)
   static constexpr int kV = 81920;     // V tile: 64 t rows x 128 v bf16, unswizzled (16 KB)
-  static constexpr int kG = 98304;     // float G[2][64]
+  // per-token gate factors of the current / next chunk, computed once per
+  // chunk: e^{G_t}, beta_t, e^{G_last - G_t} (0 past the end), e^{G_last}
+  static constexpr int kG = 98304;     // float eG[2][64]
   static constexpr int kB = kG + 512;  // float beta[2][64]
-  static constexpr int kBar = kB + 512;
+  static constexpr int kDec = kB + 512;  // float eDec[2][64]
+  static constexpr int kGl = kDec + 512;  // float eGlast[2]
+  static constexpr int kBar = kGl + 16;
   static constexpr int kBarMma = kBar, kBarQ = kBar + 8, kBarV = kBar + 16, kBarM2 = kBar + 24,
                        kBarK0 = kBar + 32;  // kBarK1 = kBarK0 + 8
   static constexpr int kTmem = kBar + 48;
   static constexpr int kBroken = kBar + 52;
   static constexpr int kBytes = kBar + 64 + 1024;  // + base alignment slack
   static constexpr uint32_t kTmemCols = 256;
-  static constexpr uint32_t kColSb = 0, kColY = 128;
+  static constexpr uint32_t kColSb = 0, kColOi = 64, kColY = 128;
 };
 
 // Writes 16 fp32 as bf16 into row `row`, 16-byte chunks c0, c0+1 of a
@@ -553,8 +628,10 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 
   uint8_t *xv = smem + SM::kXV;
   const uint16_t *vt = reinterpret_cast<const uint16_t *>(smem + SM::kV);
-  float *Gs = reinterpret_cast<float *>(smem + SM::kG);
+  float *Eg = reinterpret_cast<float *>(smem + SM::kG);
   float *Bs = reinterpret_cast<float *>(smem + SM::kB);
+  float *Ed = reinterpret_cast<float *>(smem + SM::kDec);
+  float *Egl = reinterpret_cast<float *>(smem + SM::kGl);
   volatile int *broken = reinterpret_cast<volatile int *>(smem + SM::kBroken);
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar_mma = s_base + SM::kBarMma, bar_q = s_base + SM::kBarQ,
@@ -585,12 +662,27 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     bulk_load(s_base + SM::kM2, m2_ws + (static_cast<int64_t>(gbase + c) * kHV + hv) * kM2Bytes,
               static_cast<uint32_t>(kM2Bytes), bar_m2);
   };
-  auto load_gates = [&](int c, int buf) {  // threads 0..63
+  // Gates of chunk c for token `tid` (threads 0..63): fetched into registers
+  // a chunk ahead, turned into the per-token factors when the buffer is free.
+  struct GateRegs {
+    float g, g_last, beta;
+    bool valid;
+  };
+  auto fetch_gates = [&](int c) {
     const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
     const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
-    const bool valid = tid < L;
-    Gs[buf * 64 + tid] = gcum_ws[(t0 + (valid ? tid : L - 1)) * kHV + hv];
-    Bs[buf * 64 + tid] = valid ? beta_ws[(t0 + tid) * kHV + hv] : 0.f;
+    GateRegs r;
+    r.valid = tid < L;
+    r.g_last = gcum_ws[(t0 + L - 1) * kHV + hv];
+    r.g = r.valid ? gcum_ws[(t0 + tid) * kHV + hv] : r.g_last;
+    r.beta = r.valid ? beta_ws[(t0 + tid) * kHV + hv] : 0.f;
+    return r;
+  };
+  auto store_gates = [&](const GateRegs &r, int buf) {
+    Eg[buf * 64 + tid] = expf(r.g);
+    Bs[buf * 64 + tid] = r.beta;
+    Ed[buf * 64 + tid] = r.valid ? expf(r.g_last - r.g) : 0.f;
+    if (tid == 0) Egl[buf] = expf(r.g_last);
   };
 
   // fp32 state row slice S[v][64 hc .. 64 hc + 63].
@@ -627,7 +719,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       issue_v(0);
       issue_m2(0);
     }
-    if (tid < 64) load_gates(0, 0);
+    if (tid < 64) store_gates(fetch_gates(0), 0);
   }
   tmem_wait_st();
   tc_fence_before();
@@ -642,9 +734,10 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const int cb = c & 1;
     const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
     const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
-    const float g_last = Gs[cb * 64 + L - 1];
     const uint32_t kbuf = s_base + (cb ? SM::kK1 : SM::kK0);
     const uint32_t bar_k = bar_k0 + 8 * cb;
+    GateRegs next_gates;
+    if (tid < 64 && c + 1 < nchunks) next_gates = fetch_gates(c + 1);
 
     // Q, K and [PA;Ainv] are read only by the tensor core, so only the MMA
     // thread waits for them: thread 0 re-arms each barrier for the next chunk
@@ -654,10 +747,9 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // every thread must see its tiles landed before zeroing rows.
     const bool tail = L < kChunk;
     if (tid == 0 || tail) {
-      wait_phase(bar_q, ph_q, broken);
       wait_phase(bar_k, (ph_k >> cb) & 1, broken);
+      if (tail) wait_phase(bar_q, ph_q, broken);
     }
-    ph_q ^= 1;
     ph_k ^= 1u << cb;
     if (tail) {
       // tail chunk: zero the rows past the sequence end (TMA brought in the
@@ -672,15 +764,10 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       __syncthreads();
     }
 
-    // ---- MMA 1: Yq = S Q^T, Yk = S K^T ----
+    // ---- MMA 1: Yk = S K^T (committed first: X needs it), then Yq = S Q^T
+    // (read only after MMA 2, whose commit also covers it) ----
     if (tid == 0) {
       tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
-        umma_bf16_ts(tmem + SM::kColY, tmem + SM::kColSb + 8 * ks,
-                     umma_desc_sw128(s_base + SM::kQ + boff, 16, 1024), idesc_n64, ks > 0);
-      }
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
@@ -688,51 +775,57 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                      umma_desc_sw128(kbuf + boff, 16, 1024), idesc_n64, ks > 0);
       }
       umma_commit(bar_mma);
+      if (!tail) wait_phase(bar_q, ph_q, broken);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
+        umma_bf16_ts(tmem + SM::kColY, tmem + SM::kColSb + 8 * ks,
+                     umma_desc_sw128(s_base + SM::kQ + boff, 16, 1024), idesc_n64, ks > 0);
+      }
     }
+    ph_q ^= 1;
     wait_phase(bar_mma, ph_mma, broken);
     ph_mma ^= 1;
     tc_fence_after();
-    if (tid == 0 && c + 1 < nchunks) issue_qk(false, c + 1, s_base + SM::kQ, bar_q);
     wait_phase(bar_v, ph_v, broken);
     ph_v ^= 1;
 
-    // ---- X = beta (V - e^G Yk) -> smem;  Yq *= e^G in TMEM ----
+    // ---- X = beta (V - e^G Yk) -> smem ----
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const int tb = 32 * hc + 16 * p;
-      float yk[16], yq[16];
+      float yk[16];
       tmem_ld16(tlane + SM::kColY + 64 + tb, yk);
-      tmem_ld16(tlane + SM::kColY + tb, yq);
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = tb + j;
-        const float eg = expf(Gs[cb * 64 + t]);
-        const float vv = t < L ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
-        yk[j] = Bs[cb * 64 + t] * (vv - eg * yk[j]);
-        yq[j] *= eg;
+      for (int g = 0; g < 4; ++g) {
+        const float4 eg4 = *reinterpret_cast<const float4 *>(Eg + cb * 64 + tb + 4 * g);
+        const float4 bt4 = *reinterpret_cast<const float4 *>(Bs + cb * 64 + tb + 4 * g);
+        const float eg[4] = {eg4.x, eg4.y, eg4.z, eg4.w};
+        const float bt[4] = {bt4.x, bt4.y, bt4.z, bt4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = 4 * g + u, t = tb + j;
+          const float vv = t < L ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
+          yk[j] = bt[u] * (vv - eg[u] * yk[j]);
+        }
       }
       store16_bf16(xv, vrow, tb >> 3, yk);
-      uint32_t u[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) u[j] = __float_as_uint(yq[j]);
-      tmem_st16(tlane + SM::kColY + tb, u);
     }
-    tmem_wait_st();
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (tid == 0 && c + 1 < nchunks) issue_v(c + 1);
 
-    // ---- MMA 2: O' = Yq + X PA^T, V_new = X Ainv^T ----
+    // ---- MMA 2: O_intra = X PA^T (free columns 64..127), V_new = X Ainv^T ----
     if (tid == 0) {
       wait_phase(bar_m2, ph_m2, broken);
       tc_fence_after();
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(tmem + SM::kColY, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
-                  umma_desc_sw128(s_base + SM::kM2 + ks * 32, 16, 1024), idesc_n64, 1);
+        umma_bf16(tmem + SM::kColOi, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
+                  umma_desc_sw128(s_base + SM::kM2 + ks * 32, 16, 1024), idesc_n64, ks > 0);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         umma_bf16(tmem + SM::kColY + 64, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
@@ -744,26 +837,40 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     wait_phase(bar_mma, ph_mma, broken);
     ph_mma ^= 1;
     tc_fence_after();
-    if (tid == 0 && c + 1 < nchunks) issue_m2(c + 1);
+    if (tid == 0 && c + 1 < nchunks) {
+      issue_m2(c + 1);
+      issue_qk(false, c + 1, s_base + SM::kQ, bar_q);  // MMA 1's Q reads are done too
+    }
 
-    // ---- outputs and V_dec ----
+    // ---- outputs O = scale (e^G Yq + O_intra) and V_dec ----
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const int tb = 32 * hc + 16 * p;
-      float zo[16], zv[16];
-      tmem_ld16(tlane + SM::kColY + tb, zo);
+      float zq[16], zo[16];
+      tmem_ld16(tlane + SM::kColY + tb, zq);
+      tmem_ld16(tlane + SM::kColOi + tb, zo);
+      tmem_wait_ld();
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const float4 eg4 = *reinterpret_cast<const float4 *>(Eg + cb * 64 + tb + 4 * g);
+        const float eg[4] = {eg4.x, eg4.y, eg4.z, eg4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = 4 * g + u, t = tb + j;
+          if (t < L)
+            out[((t0 + t) * kHV + hv) * kD + vrow] =
+                __bfloat16_as_ushort(__float2bfloat16_rn(scale * (eg[u] * zq[j] + zo[j])));
+        }
+      }
+      float zv[16];
       tmem_ld16(tlane + SM::kColY + 64 + tb, zv);
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = tb + j;
-        if (t < L) {
-          out[((t0 + t) * kHV + hv) * kD + vrow] =
-              __bfloat16_as_ushort(__float2bfloat16_rn(scale * zo[j]));
-          zv[j] *= expf(g_last - Gs[cb * 64 + t]);
-        } else {
-          zv[j] = 0.f;
-        }
+      for (int g = 0; g < 4; ++g) {
+        const float4 ed4 = *reinterpret_cast<const float4 *>(Ed + cb * 64 + tb + 4 * g);
+        const float ed[4] = {ed4.x, ed4.y, ed4.z, ed4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) zv[4 * g + u] *= ed[u];  // e^{G_last - G_t}, 0 past the end
       }
       store16_bf16(xv, vrow, tb >> 3, zv);
     }
@@ -780,7 +887,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                   umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), idesc_ds, ks > 0);
       umma_commit(bar_mma);
     }
-    if (tid < 64 && c + 1 < nchunks) load_gates(c + 1, cb ^ 1);
+    if (tid < 64 && c + 1 < nchunks) store_gates(next_gates, cb ^ 1);
     wait_phase(bar_mma, ph_mma, broken);
     ph_mma ^= 1;
     tc_fence_after();
@@ -788,7 +895,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 
     // ---- S = e^{G_last} S + dS ;  bf16(S) -> TMEM ----
     {
-      const float eg_last = expf(g_last);
+      const float eg_last = Egl[cb];
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         float ds[32];

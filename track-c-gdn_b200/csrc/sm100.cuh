@@ -172,6 +172,15 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Warp-collective: lane l receives 8 consecutive fp32 columns.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&r)[8]) {
+  uint32_t *u = reinterpret_cast<uint32_t *>(r);
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]),
+                 "=r"(u[6]), "=r"(u[7])
+               : "r"(taddr));
+}
+
 // Warp-collective: lane l receives 16 consecutive fp32 columns.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
   uint32_t *u = reinterpret_cast<uint32_t *>(r);
