@@ -91,61 +91,125 @@ def load_traffic(workload: str):
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples this process's GPU SM clock and clock-event reasons during the
+    timed region.  NVML (read-only queries) polled from a thread every 5 ms,
+    so a timed region of ~100 ms still yields ~20 samples; `nvidia-smi -lms`
+    is the fallback when NVML cannot be opened."""
+    REASONS = (("nvmlClocksEventReasonHwSlowdown", "hw_slowdown"),
+               ("nvmlClocksEventReasonHwThermalSlowdown", "hw_thermal_slowdown"),
+               ("nvmlClocksEventReasonSwThermalSlowdown", "sw_thermal_slowdown"),
+               ("nvmlClocksEventReasonSwPowerCap", "sw_power_cap"),
+               ("nvmlClocksEventReasonHwPowerBrakeSlowdown", "hw_power_brake_slowdown"),
+               ("nvmlClocksEventReasonApplicationsClocksSetting", "applications_clocks_setting"))
+    SMI_FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, enabled: bool):
+    def __init__(self, enabled: bool, device_index: int = 0):
+        import threading
+        self.samples = []          # (sm_mhz, frozenset(reasons))
+        self.sm_max = None
+        self.thread = None
         self.proc = None
-        self.path = None
+        self.stop_evt = threading.Event()
         if not enabled:
             return
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            try:
+                nvml_idx = torch.cuda._get_nvml_device_index(device_index)
+            except Exception:  # noqa: BLE001 -- fall back to the CUDA ordinal
+                nvml_idx = device_index
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(nvml_idx)
+            self.sm_max = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.masks = [(getattr(pynvml, a), n) for a, n in self.REASONS if hasattr(pynvml, a)]
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001 -- NVML unavailable: use nvidia-smi
+            self._start_smi(device_index)
+
+    def _poll(self):
+        nv = self.nvml
+        while not self.stop_evt.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((float(sm), frozenset(n for m, n in self.masks if bits & m)))
+            except Exception:  # noqa: BLE001 -- a failed query drops one sample
+                pass
+            self.stop_evt.wait(0.005)
+
+    def _start_smi(self, device_index):
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"gdn_clocks_{os.getpid()}.csv"
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
+                ["nvidia-smi", f"--id={device_index}", f"--query-gpu={self.SMI_FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh,
+                stderr=subprocess.DEVNULL)
+        except OSError:
             self.proc = None
 
-    def stop(self, gpu_indices):
-        if self.proc is None:
-            return None
+    def _stop_smi(self):
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.fh.close()
-        rows = []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.path.read_text().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
             try:
-                idx = int(parts[0])
-            except ValueError:
+                sm, smax = float(parts[0]), float(parts[1])
+            except (ValueError, IndexError):
                 continue
-            if gpu_indices is not None and idx not in gpu_indices:
-                continue
-            rows.append(parts)
+            self.sm_max = smax
+            self.samples.append((sm, frozenset(n for i, n in enumerate(names)
+                                               if len(parts) > 2 + i and parts[2 + i].lower() == "active")))
         self.path.unlink(missing_ok=True)
-        if not rows:
-            return None
 
-        def num(x):
+    def stop(self):
+        if self.thread is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=5)
             try:
-                return float(x)
-            except ValueError:
-                return None
+                self.nvml.nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
+            source = "nvml 5 ms"
+        elif self.proc is not None:
+            self._stop_smi()
+            source = "nvidia-smi 50 ms"
+        else:
+            return None
+        if not self.samples:
+            return None
+        sm = [x for x, _ in self.samples]
+        reasons = sorted(set().union(*[r for _, r in self.samples]))
+        return {"sm_mhz": float(np.median(sm)), "sm_min_mhz": min(sm), "sm_max_mhz": self.sm_max,
+                "reasons": reasons, "samples": len(sm), "source": source}
 
-        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
-        smax = max((num(r[2]) for r in rows if num(r[2]) is not None), default=None)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
-                "reasons": reasons, "samples": len(rows)}
+
+def merge_clocks(dist, world, mine):
+    """Clock summary over all ranks' GPUs (every rank calls this once, in the
+    same place, after the timed region)."""
+    if world == 1:
+        return mine
+    allc = [None] * world
+    dist.all_gather_object(allc, mine)
+    got = [c for c in allc if c]
+    if not got:
+        return None
+    return {"sm_mhz": float(np.median([c["sm_mhz"] for c in got])),
+            "sm_min_mhz": min(c["sm_min_mhz"] for c in got),
+            "sm_max_mhz": max(c["sm_max_mhz"] or 0 for c in got),
+            "reasons": sorted(set().union(*[c["reasons"] for c in got])),
+            "samples": sum(c["samples"] for c in got), "source": got[0]["source"],
+            "per_rank_sm_mhz": [c["sm_mhz"] if c else None for c in allc]}
 
 
 # ---------------------------------------------------------------------------
@@ -197,6 +261,8 @@ def gpu_arm(args):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
+        # NCCL would print its version banner on stdout ahead of the JSON line
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", timeout=timedelta(seconds=180),
                                 device_id=dev)
     wl = WORKLOADS[args.workload]
@@ -281,7 +347,7 @@ def gpu_arm(args):
     for _ in range(args.warmup):
         step(False)
     barrier()
-    sampler = ClockSampler(rank == 0)
+    sampler = ClockSampler(True, local_rank)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     barrier()
@@ -291,7 +357,7 @@ def gpu_arm(args):
     t1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
-    clocks = sampler.stop(None)
+    clocks = merge_clocks(dist, world, sampler.stop())
     elapsed_ms = max_over_ranks(t0.elapsed_time(t1))
     ms_step = elapsed_ms / args.steps
     d_ms = np.mean([a.elapsed_time(b) for a, b in zip(ev["s"], ev["d"])])
