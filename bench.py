@@ -9,7 +9,7 @@ fixed total sharded across the N ranks (decode: request blocks; prefill: LPT
 bin packing by sequence), so scaling is "strong".  All inputs are seeded
 synthetic tensors with the BASELINE value distributions.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference|triton]
                     [--workload c4|c2|c3|decode]
 
 Prints one JSON line (rank 0).  `value` is whole-job tokens/s (decode tokens
@@ -17,7 +17,9 @@ Prints one JSON line (rank 0).  `value` is whole-job tokens/s (decode tokens
 `e2e` is the same metric through the public entry points with pinned host
 inputs and outputs copied inside the timed region.  `--impl reference` times
 the CPU oracle (the reference recurrence restated in C, all host threads) on
-bounded samples of the same workload.
+bounded samples of the same workload.  `--impl triton` times the reference's
+own Triton kernels (staged unmodified under baseline/_ref) on one GPU with
+the same inputs, and reports our outputs' distance from theirs.
 """
 from __future__ import annotations
 
@@ -627,12 +629,146 @@ def reference_arm(args):
     }), flush=True)
 
 
+TRITON_REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def _load_triton_ref(definition: str):
+    """Import the reference's Triton solution `<definition>/solution/triton/
+    kernel.py` from the unmodified copy staged under baseline/_ref (the
+    reference is not pip-installable)."""
+    import importlib.util
+    path = TRITON_REF_DIR / definition / "solution" / "triton" / "kernel.py"
+    if not path.exists():
+        return None
+    spec = importlib.util.spec_from_file_location(f"triton_ref_{definition}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def triton_arm(args):
+    """The reference's own Triton kernels on this GPU, through their `run`
+    entry points, on the same seeded inputs as the b200 arm at N=1 (decode:
+    value-returning run, which allocates new_state as the reference does;
+    prefill: run, including its host-side checks).  Also reports how far our
+    outputs are from the Triton outputs on these inputs."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    wl = WORKLOADS[args.workload]
+    dec_mod = _load_triton_ref("gdn_decode_qk4_v8_d128_k_last") if wl["decode_batch"] else None
+    pre_mod = _load_triton_ref("gdn_prefill_qk4_v8_d128_k_last") if wl["prefill"] else None
+    if (wl["decode_batch"] and dec_mod is None) or (wl["prefill"] and pre_mod is None):
+        print(json.dumps({"impl": "triton-reference",
+                          "unavailable": f"reference Triton solutions not staged under {TRITON_REF_DIR}"}))
+        return
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)  # the b200 arm's rank-0 seeds, so both arms see the same inputs
+    A_log = (torch.rand(HV, generator=g, device=dev) * 2.7).float()
+    dt_bias = (torch.randn(HV, generator=g, device=dev) * 0.1).float()
+    dec = make_decode_inputs(torch, wl["decode_batch"], 100, dev) if wl["decode_batch"] else None
+    pre = None
+    if wl["prefill"]:
+        lengths = prefill_lengths(wl["prefill"])
+        pre = make_prefill_inputs(torch, lengths, wl["prefill"] == "c3", 200, dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = {k: [] for k in ("s", "d", "p")}
+    keep = {}
+
+    def step(record):
+        if record:
+            ev["s"].append(torch.cuda.Event(enable_timing=True))
+            ev["s"][-1].record(stream)
+        if dec is not None:
+            keep["dec"] = dec_mod.run(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
+                                      dt_bias, dec["b"], None)
+        if record:
+            ev["d"].append(torch.cuda.Event(enable_timing=True))
+            ev["d"][-1].record(stream)
+        if pre is not None:
+            keep["pre"] = pre_mod.run(pre["q"], pre["k"], pre["v"], pre["h0"], A_log, pre["a"],
+                                      dt_bias, pre["b"], pre["cu"], None)
+        if record:
+            ev["p"].append(torch.cuda.Event(enable_timing=True))
+            ev["p"][-1].record(stream)
+
+    for _ in range(max(3, args.warmup)):
+        step(False)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(True, 0)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    d_ms = float(np.mean([a.elapsed_time(b) for a, b in zip(ev["s"], ev["d"])]))
+    p_ms = float(np.mean([a.elapsed_time(b) for a, b in zip(ev["d"], ev["p"])]))
+    total = wl["decode_batch"] + (pre["T"] if pre else 0)
+
+    # our kernels on the same inputs (the reference decode left dec["state"] untouched)
+    gdn = importlib.import_module("track-c-gdn_b200")
+
+    def rel(x, y):
+        x, y = x.float(), y.float()
+        return float((x - y).norm() / y.norm().clamp_min(1e-30))
+
+    parity = {}
+    if dec is not None:
+        o, s = gdn.decode.run(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
+                              dt_bias, dec["b"], None)
+        parity["decode_out_rel_fro"] = rel(o, keep["dec"][0])
+        parity["decode_state_rel_fro"] = rel(s, keep["dec"][1])
+    if pre is not None:
+        o, s = gdn.prefill.run(pre["q"], pre["k"], pre["v"], pre["h0"], A_log, pre["a"], dt_bias,
+                               pre["b"], pre["cu"], None)
+        parity["prefill_out_rel_fro"] = rel(o, keep["pre"][0])
+        parity["prefill_state_rel_fro"] = rel(s, keep["pre"][1])
+        # the reference's Triton output stage is not deterministic on B200 (whole 16-token
+        # blocks of a few chunks differ between identical calls), so also give the median
+        # per-token distance, which those blocks do not move
+        tok = ((o.float() - keep["pre"][0].float()).flatten(1).norm(dim=1)
+               / keep["pre"][0].float().flatten(1).norm(dim=1).clamp_min(1e-30))
+        parity["prefill_out_token_rel_median"] = float(tok.median())
+        parity["prefill_out_tokens_over_2pct"] = int((tok > 0.02).sum())
+    result = {
+        "impl": "triton-reference",
+        "metric": "GDN serving throughput (decode + prefill tokens/s, max-over-ranks device time)",
+        "value": total / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic (seeded; same inputs as the b200 arm at N=1)",
+        "config": {"workload": wl["desc"], "decode_batch": wl["decode_batch"],
+                   "prefill_tokens": pre["T"] if pre else 0},
+        "phases_ms": {"decode": d_ms, "prefill": p_ms},
+        "clocks": clocks,
+        "parity_b200_vs_triton": parity,
+        "note": "reference Triton solutions (gdn_decode/gdn_prefill solution/triton/kernel.py, "
+                "unmodified) through their run() entry points; device time with CUDA events",
+    }
+    if pre is not None:
+        result["prefill"] = {"tokens_per_s": pre["T"] / (p_ms / 1e3),
+                             "tflops": pre["T"] * PREFILL_FLOP_PER_TOKEN / (p_ms / 1e3) / 1e12}
+    if dec is not None:
+        result["decode"] = {"us_per_step": d_ms * 1e3,
+                            "state_gbs": dec["B"] * (DECODE_STATE_BYTES + DECODE_VEC_BYTES)
+                            / (d_ms / 1e3) / 1e9}
+    print(json.dumps(result), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--impl", choices=["b200", "reference", "triton"], default="b200",
+                    help="b200: this build; reference: CPU restatement of the reference path; "
+                         "triton: the reference's Triton kernels staged under baseline/_ref (1 GPU)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c4")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -643,6 +779,8 @@ def main():
         args.warmup = 3  # timing rule: at least three warm-up steps
     if args.impl == "reference":
         reference_arm(args)
+    elif args.impl == "triton":
+        triton_arm(args)
     else:
         gpu_arm(args)
 
