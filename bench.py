@@ -396,7 +396,7 @@ def gpu_arm(args):
                               if world > 1 else "no collective"),
         },
         "gpu_launches": args.steps * ((1 if dec is not None else 0) +
-                                      (gdn._native.PREFILL_KERNELS_PER_CALL if pre else 0)),
+                                      (gdn._native.prefill_kernel_launches(pre["T"], pre["N"]) if pre else 0)),
         "phases_ms": {"decode": d_ms_max, "prefill": p_ms_max, "gather": g_ms_max},
         "clocks": clocks,
     }

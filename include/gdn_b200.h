@@ -82,6 +82,14 @@ int gdn_decode_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
 size_t gdn_prefill_workspace_bytes(int64_t total_tokens, int64_t num_seqs);
 
 /*
+ * Number of kernels one gdn_prefill_qk4_v8_d128_k_last call launches for
+ * (total_tokens, num_seqs): 3, or 5 when the call uses the segmented
+ * evaluation (see below); 0 for num_seqs = 0.  For launch accounting; no
+ * counterpart in the reference.
+ */
+int gdn_prefill_kernel_launches(int64_t total_tokens, int64_t num_seqs);
+
+/*
  * Chunked (64-token) prefill over ragged sequences.  Replaces the reference
  * entry point
  *   run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
@@ -100,6 +108,10 @@ size_t gdn_prefill_workspace_bytes(int64_t total_tokens, int64_t num_seqs);
  * workspace   >= gdn_prefill_workspace_bytes(T, N) bytes, 1024-byte aligned
  * No host synchronisation: unlike the reference (kernel.py:1665, :181-184)
  * the chunk metadata is built on the device.
+ * Few long sequences (num_seqs <= 16 averaging >= 12 chunks, decided from T
+ * and N alone) are evaluated in segments run in parallel and then joined
+ * through the segments' affine state maps; results agree with the
+ * single-pass evaluation within the stated tolerances, not bit for bit.
  */
 int gdn_prefill_qk4_v8_d128_k_last(
     const void *q, const void *k, const void *v, const float *state,
@@ -116,7 +128,8 @@ int gdn_prefill_qk4_v8_d128_k_last(
  * serving loop that cannot afford cudaMalloc's implicit synchronisation).
  * The scratch is a 32 MiB buffer compiled into the library
  * (GDN_PREFILL_NOALLOC_SCRATCH_BYTES), held on every GPU that loads it until
- * exit.  Problems whose gdn_prefill_workspace_bytes(T, N) exceeds it are
+ * exit.  When gdn_prefill_workspace_bytes(T, N) exceeds it, the call runs the
+ * single-pass evaluation (smaller workspace) if that fits, and otherwise is
  * rejected with GDN_ERR_TOO_LARGE before anything is launched; a problem
  * always fits when T + 64 N <= 15,872 (e.g. T <= 15,808 for one sequence).
  * All calls on a device share the buffer: calls whose kernels overlap on

@@ -44,9 +44,27 @@ def test_status_strings(gdn):
 def test_workspace_size_monotone(gdn):
     ws = gdn.prefill.workspace_bytes
     assert ws(0, 1) > 0
-    assert ws(4096, 1) < ws(8192, 1) < ws(8192, 32)
-    # 16 KiB [PA;Ainv] image per (chunk, v-head) dominates: ~2 KiB per token
-    assert 2048 * 4096 < ws(4096, 1) < 2048 * 4096 * 1.2
+    # single-pass evaluation (many or short sequences): the 16 KiB [PA;Ainv]
+    # image per (chunk, v-head) dominates, ~2 KiB per token
+    assert ws(4096, 32) < ws(8192, 32) < ws(8192, 64)
+    assert 2048 * 8192 < ws(8192, 16) < 2048 * 8192 * 1.3   # 128 chunks < 12 x 16: single pass
+    # segmented evaluation (few long sequences) adds three fp32 states
+    # (512 KiB each) per segment: T = 4096, N = 1 -> segments of 4 chunks,
+    # at most 1 + ceil(65 / 4) = 18 of them
+    seg_states = 3 * 18 * 8 * 128 * 128 * 4
+    assert 2048 * 4096 + seg_states < ws(4096, 1) < (2048 * 4096 + seg_states) * 1.1
+    assert ws(4096, 1) < ws(8192, 1)
+
+
+def test_prefill_launch_count_follows_segment_policy(gdn):
+    n = gdn._native.prefill_kernel_launches
+    assert n(0, 0) == 0
+    assert n(4096, 1) == 5        # one long sequence: segmented (3 passes + compose)
+    assert n(16384, 4) == 5
+    assert n(269, 1) == 3         # 5 chunks: too short to segment
+    assert n(44450, 32) == 3      # more than 16 sequences: single pass
+    assert n(11 * 64 * 2, 2) == 3  # fewer than 12 chunks per sequence on average
+    assert n(12 * 64 * 2, 2) == 5
 
 
 def test_argument_validation_without_device(gdn):

@@ -88,6 +88,37 @@ def test_prefill_config_c2_t4096(gdn):
     assert rel_fro(s.cpu().numpy(), rs) < STATE_TOL
 
 
+@pytest.mark.parametrize("lens,with_state", [
+    ([4096], True), ([769], True), ([3000, 1500], True), ([0, 2000, 900], True),
+    ([1024, 1024, 1024], False),
+])
+def test_segmented_evaluation_matches_recurrence(gdn, lens, with_state):
+    """Few long sequences take the segmented path (segments in parallel,
+    joined through their affine state maps): same tolerances as one pass.
+    [769] ends in a ragged chunk inside its last segment; [0, ...] mixes in
+    an empty sequence."""
+    assert gdn._native.prefill_kernel_launches(sum(lens), len(lens)) == 5
+    inp = cases.prefill_inputs(seed=sum(lens) + 7, lens=lens, with_state=with_state)
+    o, s = _run(gdn, inp)
+    ro, rs = _oracle(inp)
+    assert out_err(o, ro) <= 1.0
+    assert rel_fro(s.cpu().numpy(), rs) < STATE_TOL
+    if lens[0] == 0 and with_state:
+        np.testing.assert_array_equal(s[0].cpu().numpy(), inp["state"][0])
+
+
+def test_segmented_state_error_not_worse_than_reference(gdn):
+    inp = cases.prefill_inputs(seed=42, lens=[1500], with_state=True)
+    assert gdn._native.prefill_kernel_launches(1500, 1) == 5
+    o, s = _run(gdn, inp)
+    ro, rs = _oracle(inp)
+    f = bits_to_f32
+    _, cs = oracle.prefill_chunked(f(inp["q"]), f(inp["k"]), f(inp["v"]), inp["state"],
+                                   inp["A_log"], f(inp["a"]), inp["dt_bias"], f(inp["b"]),
+                                   inp["cu_seqlens"])
+    assert rel_fro(s.cpu().numpy(), rs) <= 1.5 * rel_fro(cs, rs) + 1e-4
+
+
 def test_state_error_not_worse_than_reference(gdn):
     """The kernel's state error vs the exact recurrence stays within 1.5x of
     the reference algorithm's own (chunked oracle == reference kernel)."""

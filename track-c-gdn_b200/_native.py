@@ -22,6 +22,7 @@ SIGNATURES = {
     "gdn_decode_qk4_v8_d128_k_last": (
         ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _F, _I64, _P, _P, _P]),
     "gdn_prefill_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
+    "gdn_prefill_kernel_launches": (ctypes.c_int, [_I64, _I64]),
     "gdn_prefill_qk4_v8_d128_k_last": (
         ctypes.c_int,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P, _P, ctypes.c_size_t, _P]),
@@ -33,7 +34,6 @@ ABI_VERSION = 1
 
 # Kernels each entry point launches per call (for launch accounting).
 DECODE_KERNELS_PER_CALL = 1
-PREFILL_KERNELS_PER_CALL = 3
 
 
 class GdnError(RuntimeError):
@@ -62,6 +62,12 @@ def check(status: int, what: str) -> None:
     if status != 0:
         msg = lib.gdn_b200_status_string(status).decode()
         raise GdnError(f"{what} failed: status {status} ({msg})")
+
+
+def prefill_kernel_launches(total_tokens: int, num_seqs: int) -> int:
+    """Kernels one prefill call launches for this problem size (3, or 5 when
+    it runs the segmented evaluation)."""
+    return int(lib.gdn_prefill_kernel_launches(int(total_tokens), int(num_seqs)))
 
 
 def read_device_status(stream: int = 0) -> int:

@@ -18,11 +18,12 @@ cudaError_t launch_decode(const void *q, const void *k, const void *v, const flo
                           const float *A_log, const void *a, const float *dt_bias,
                           const void *b, float scale, int64_t batch, void *out,
                           float *new_state, cudaStream_t stream);
-size_t prefill_workspace_bytes(int64_t T, int64_t N);
+size_t prefill_workspace_bytes(int64_t T, int64_t N, bool allow_segments);
+int prefill_kernel_launches(int64_t T, int64_t N, bool allow_segments);
 cudaError_t launch_prefill(const void *q, const void *k, const void *v, const float *state,
                            const float *A_log, const void *a, const float *dt_bias, const void *b,
                            const int64_t *cu_seqlens, int64_t N, int64_t T, float scale,
-                           void *out, float *final_state, void *workspace, int num_sms,
+                           void *out, float *final_state, void *workspace, bool allow_segments,
                            cudaStream_t stream);
 }  // namespace gdn
 
@@ -114,7 +115,12 @@ int gdn_decode_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
 
 size_t gdn_prefill_workspace_bytes(int64_t total_tokens, int64_t num_seqs) {
   if (total_tokens < 0 || num_seqs < 0) return 0;
-  return gdn::prefill_workspace_bytes(total_tokens, num_seqs);
+  return gdn::prefill_workspace_bytes(total_tokens, num_seqs, true);
+}
+
+int gdn_prefill_kernel_launches(int64_t total_tokens, int64_t num_seqs) {
+  if (total_tokens < 0 || num_seqs < 0) return 0;
+  return gdn::prefill_kernel_launches(total_tokens, num_seqs, true);
 }
 
 int gdn_prefill_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
@@ -135,16 +141,15 @@ int gdn_prefill_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
       !aligned(cu_seqlens, 8))
     return GDN_ERR_MISALIGNED;
   if (!aligned(workspace, 1024) ||
-      workspace_bytes < gdn::prefill_workspace_bytes(total_tokens, num_seqs))
+      workspace_bytes < gdn::prefill_workspace_bytes(total_tokens, num_seqs, true))
     return GDN_ERR_WORKSPACE;
   const size_t state_bytes = static_cast<size_t>(num_seqs) * gdn::kHV * gdn::kD * gdn::kD * 4;
   if (state && state != final_state && overlap(state, state_bytes, final_state, state_bytes))
     return GDN_ERR_ALIASING;
-  int sms = 0;
-  if (int st = check_device(&sms)) return st;
+  if (int st = check_device(nullptr)) return st;
   if (scale == 0.0f) scale = kDefaultScale;
   cudaError_t err = gdn::launch_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
-                                        total_tokens, scale, out, final_state, workspace, sms,
+                                        total_tokens, scale, out, final_state, workspace, true,
                                         static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }

@@ -44,18 +44,57 @@ using namespace sm100;
 // ---------------------------------------------------------------------------
 // workspace layout
 // ---------------------------------------------------------------------------
+// Scan work items (int4 {sequence, segment, mode, 0}).  Without segmentation
+// every sequence is one FULL item.  With segmentation (few long sequences),
+// sequence n is cut into P_n segments of `seg_chunks` chunks and evaluated
+// in three passes, using that the state map of a segment is affine:
+//   S_end = S_start Phi + B,
+// Phi = the segment's final state from S = I with v = 0, B = its final state
+// from S = 0.
+//   pass 1 (parallel): HEAD (segment 0 from h0, with outputs; its final state
+//          is S_start of segment 1), ZERO (B of segments 1..P-2), IDENT (Phi of
+//          segments 1..P-2), FULL (sequences with one segment);
+//   compose (sequential per sequence, cheap): S_start(p+1) = S_start(p) Phi(p) + B(p);
+//   pass 3 (parallel): MID / TAIL (segments 1..P-1 from S_start(p), with
+//          outputs; TAIL writes the final state).
+enum ScanItemMode : int { kItemFull = 0, kItemHead, kItemZero, kItemIdent, kItemMid, kItemTail };
+
+// Segmented evaluation is used for at most this many sequences.
+constexpr int kSegMaxSeqs = 16;
+// Scan CTAs that run at once on a B200 (148 SMs x 2 CTAs).
+constexpr int64_t kScanSlots = 296;
+
 struct PrefillWs {
-  size_t meta, chunk_off, seq_order, chunk_tab, gcum, beta, m2, total;
+  size_t meta, chunk_off, seq_order, chunk_tab, gcum, beta, m2, items, seg_off, seg_ss, seg_sb,
+      seg_phi, total;
   int64_t nt_max;
+  int64_t seg_chunks;  // 0: no segmentation
+  int64_t seg_max;     // bound on the number of segments (segmented mode)
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 constexpr size_t kM2Bytes = 128 * 128;  // [PA ; Ainv] 128 rows x 64 bf16
+constexpr size_t kStateBytes = static_cast<size_t>(kHV) * kD * kD * sizeof(float);
 
-inline PrefillWs prefill_ws_layout(int64_t T, int64_t N) {
+// Segment length (chunks) chosen from T and N alone, so that the workspace
+// size is a function of (T, N): segment only when there are fewer scan
+// chains (8 per sequence) than SMs and the sequences average at least 12
+// chunks; make pass 1 (about two CTAs per segment and v-head) fit one wave.
+inline int64_t prefill_segment_chunks(int64_t T, int64_t N) {
+  if (N <= 0 || N > kSegMaxSeqs) return 0;
+  const int64_t nt = (T + kChunk - 1) / kChunk;
+  if (nt < 12 * N) return 0;
+  const int64_t lc = (16 * (nt + N) + kScanSlots - 1) / kScanSlots;
+  return lc < 4 ? 4 : lc;
+}
+
+inline PrefillWs prefill_ws_layout(int64_t T, int64_t N, bool allow_segments = true) {
   PrefillWs w;
   w.nt_max = (T + kChunk - 1) / kChunk + N;
+  w.seg_chunks = allow_segments ? prefill_segment_chunks(T, N) : 0;
+  w.seg_max = w.seg_chunks ? N + (w.nt_max + w.seg_chunks - 1) / w.seg_chunks : 0;
+  const int64_t n_items = w.seg_chunks ? 3 * w.seg_max : N;
   size_t off = 0;
   w.meta = off;
   off = align_up(off + 4 * sizeof(int), 256);
@@ -65,12 +104,22 @@ inline PrefillWs prefill_ws_layout(int64_t T, int64_t N) {
   off = align_up(off + N * sizeof(int), 256);
   w.chunk_tab = off;
   off = align_up(off + w.nt_max * sizeof(int2), 256);
+  w.items = off;
+  off = align_up(off + n_items * sizeof(int4), 256);
+  w.seg_off = off;
+  off = align_up(off + (N + 1) * sizeof(int), 256);
   w.gcum = off;
   off = align_up(off + T * kHV * sizeof(float), 256);
   w.beta = off;
   off = align_up(off + T * kHV * sizeof(float), 1024);
   w.m2 = off;
   off = align_up(off + static_cast<size_t>(w.nt_max) * kHV * kM2Bytes, 1024);
+  w.seg_ss = off;
+  off = align_up(off + static_cast<size_t>(w.seg_max) * kStateBytes, 1024);
+  w.seg_sb = off;
+  off = align_up(off + static_cast<size_t>(w.seg_max) * kStateBytes, 1024);
+  w.seg_phi = off;
+  off = align_up(off + static_cast<size_t>(w.seg_max) * kStateBytes, 1024);
   w.total = off;
   return w;
 }
@@ -120,7 +169,8 @@ constexpr int kLptMaxSeqs = 2048;
 
 __global__ void __launch_bounds__(kMetaThreads)
 gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_t nt_max,
-                        int *meta, int *chunk_off, int *seq_order, int2 *chunk_tab) {
+                        int *meta, int *chunk_off, int *seq_order, int2 *chunk_tab,
+                        int seg_chunks, int seg_max, int4 *items, int *seg_off) {
   __shared__ int s_wtot[32];
   __shared__ int s_carry;
   __shared__ int s_nc[kLptMaxSeqs];
@@ -134,6 +184,7 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
     if (tid == 0) {
       meta[0] = 0;
       meta[1] = 1;
+      meta[2] = meta[3] = 0;
       set_device_status(kDevStatusBadSeqlens);
     }
     return;
@@ -175,6 +226,7 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
     const bool ok = nt <= nt_max;
     meta[0] = ok ? nt : 0;
     meta[1] = ok ? 0 : 1;
+    meta[2] = meta[3] = 0;
     if (!ok) set_device_status(kDevStatusBadSeqlens);
   }
   if (nt > nt_max) return;
@@ -197,6 +249,54 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
     }
   } else {
     for (int i = tid; i < N; i += kMetaThreads) seq_order[i] = i;
+  }
+  __syncthreads();
+
+  // Scan work items (see ScanItemMode).  meta[2] = pass-1 items, meta[3] =
+  // pass-3 items.
+  if (seg_chunks == 0) {
+    for (int i = tid; i < N; i += kMetaThreads) items[i] = make_int4(seq_order[i], 0, kItemFull, 0);
+    if (tid == 0) {
+      meta[2] = N;
+      meta[3] = 0;
+    }
+    return;
+  }
+  // Segmented (N <= kSegMaxSeqs): thread 0 builds the tables, longest
+  // sequences first.  Pass-1 items occupy items[0, 2 seg_max), pass-3 items
+  // items[2 seg_max, 3 seg_max).
+  if (tid == 0) {
+    int so = 0;
+    for (int i = 0; i < N; ++i) {
+      const int nc = chunk_off[i + 1] - chunk_off[i];
+      seg_off[i] = so;
+      so += nc > seg_chunks ? (nc + seg_chunks - 1) / seg_chunks : 1;
+    }
+    seg_off[N] = so;
+    if (so > seg_max) {  // cannot happen for a valid cu_seqlens (bound of the layout)
+      meta[1] = 1;
+      meta[2] = meta[3] = 0;
+      set_device_status(kDevStatusBadSeqlens);
+      return;
+    }
+    int n1 = 0, n3 = 0;
+    int4 *items3 = items + 2 * seg_max;
+    for (int j = 0; j < N; ++j) {
+      const int i = seq_order[j];
+      const int P = seg_off[i + 1] - seg_off[i];
+      if (P == 1) {
+        items[n1++] = make_int4(i, 0, kItemFull, 0);
+        continue;
+      }
+      items[n1++] = make_int4(i, 0, kItemHead, 0);
+      for (int p = 1; p + 1 < P; ++p) {
+        items[n1++] = make_int4(i, p, kItemZero, 0);
+        items[n1++] = make_int4(i, p, kItemIdent, 0);
+      }
+      for (int p = 1; p < P; ++p) items3[n3++] = make_int4(i, p, p + 1 < P ? kItemMid : kItemTail, 0);
+    }
+    meta[2] = n1;
+    meta[3] = n3;
   }
 }
 
@@ -606,25 +706,57 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const float *h0,
                         const int64_t *__restrict__ cu, const int *__restrict__ meta,
-                        const int *__restrict__ chunk_off, const int *__restrict__ seq_order,
+                        const int *__restrict__ chunk_off,
                         const float *__restrict__ gcum_ws, const float *__restrict__ beta_ws,
                         const uint8_t *__restrict__ m2_ws, float scale,
-                        uint16_t *__restrict__ out, float *final_state) {
+                        uint16_t *__restrict__ out, float *final_state,
+                        const int4 *__restrict__ items, int count_slot, int64_t seg_tokens,
+                        const int *__restrict__ seg_off, float *seg_ss, float *seg_sb,
+                        float *seg_phi) {
   using SM = ScanSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(align_up(reinterpret_cast<size_t>(smem_raw), 1024));
   if (meta[1] != 0) return;
+  const int item = blockIdx.x / kHV;
+  if (item >= meta[count_slot]) return;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, hc = warp >> 2;
   const int vrow = 32 * quad + lane;  // state row (v) owned by this thread
   const int hv = blockIdx.x % kHV;
   const int hqk = hv >> 1;
-  const int n = seq_order[blockIdx.x / kHV];
-  const int64_t bos = cu[n];
-  const int64_t len = cu[n + 1] - bos;
+  const int4 it = items[item];
+  const int n = it.x, seg = it.y, mode = it.z;
+  // this item's token range: segment `seg` of sequence n (the whole sequence
+  // when not segmented: seg = 0 and seg_tokens exceeds any length)
+  const int64_t seg_begin = static_cast<int64_t>(seg) * seg_tokens;
+  const int64_t bos = cu[n] + seg_begin;
+  const int64_t len = lmin(cu[n + 1] - bos, seg_tokens);
   const int nchunks = static_cast<int>((len + kChunk - 1) / kChunk);
-  const int gbase = chunk_off[n];
+  const int gbase = chunk_off[n] + static_cast<int>(seg_begin / kChunk);
+  const bool ident = mode == kItemIdent;
+  const bool write_out = mode == kItemFull || mode == kItemHead || mode == kItemMid ||
+                         mode == kItemTail;
+  // where the state starts from and where the final state goes
+  const int64_t srow = static_cast<int64_t>(vrow) * kD + 64 * hc;  // within one (., hv) state
+  const int64_t hv_off = static_cast<int64_t>(hv) * kD * kD;
+  auto seg_state = [&](float *buf, int p) {
+    return buf + (static_cast<int64_t>(seg_off[n] + p) * kHV) * kD * kD + hv_off;
+  };
+  const float *init = nullptr;
+  if (mode == kItemFull || mode == kItemHead)
+    init = h0 != nullptr ? h0 + static_cast<int64_t>(n) * kHV * kD * kD + hv_off : nullptr;
+  else if (mode == kItemMid || mode == kItemTail)
+    init = seg_state(seg_ss, seg);
+  float *fin = nullptr;
+  if (mode == kItemFull || mode == kItemTail)
+    fin = final_state + static_cast<int64_t>(n) * kHV * kD * kD + hv_off;
+  else if (mode == kItemHead)
+    fin = seg_state(seg_ss, 1);
+  else if (mode == kItemZero)
+    fin = seg_state(seg_sb, seg);
+  else if (mode == kItemIdent)
+    fin = seg_state(seg_phi, seg);
 
   uint8_t *xv = smem + SM::kXV;
   const uint16_t *vt = reinterpret_cast<const uint16_t *>(smem + SM::kV);
@@ -687,11 +819,10 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 
   // fp32 state row slice S[v][64 hc .. 64 hc + 63].
   float s[64];
-  const int64_t srow = ((static_cast<int64_t>(n) * kHV + hv) * kD + vrow) * kD + 64 * hc;
-  if (h0 != nullptr) {
+  if (init != nullptr) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float4 x = *reinterpret_cast<const float4 *>(h0 + srow + 4 * i);
+      const float4 x = *reinterpret_cast<const float4 *>(init + srow + 4 * i);
       s[4 * i] = x.x;
       s[4 * i + 1] = x.y;
       s[4 * i + 2] = x.z;
@@ -699,7 +830,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < 64; ++i) s[i] = 0.f;
+    for (int i = 0; i < 64; ++i) s[i] = (ident && vrow == 64 * hc + i) ? 1.f : 0.f;
   }
   __syncthreads();  // barriers initialised, TMEM address published
   tc_fence_after();
@@ -806,7 +937,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int j = 4 * g + u, t = tb + j;
-          const float vv = t < L ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
+          const float vv = (t < L && !ident) ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
           yk[j] = bt[u] * (vv - eg[u] * yk[j]);
         }
       }
@@ -857,7 +988,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int j = 4 * g + u, t = tb + j;
-          if (t < L)
+          if (write_out && t < L)
             out[((t0 + t) * kHV + hv) * kD + vrow] =
                 __bfloat16_as_ushort(__float2bfloat16_rn(scale * (eg[u] * zq[j] + zo[j])));
         }
@@ -915,10 +1046,12 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     tc_fence_after();
   }
 
+  if (fin != nullptr) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    *reinterpret_cast<float4 *>(final_state + srow + 4 * i) =
-        make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+    for (int i = 0; i < 16; ++i)
+      *reinterpret_cast<float4 *>(fin + srow + 4 * i) =
+          make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+  }
 
   tc_fence_before();
   __syncthreads();
@@ -929,9 +1062,113 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 }
 
 // ---------------------------------------------------------------------------
+// 4. segment composition (segmented mode only)
+// ---------------------------------------------------------------------------
+// S_start(p+1) = S_start(p) Phi(p) + B(p) for p = 1 .. P-2, in fp32.  Rows of
+// S are independent, so one CTA per (sequence, v-head, 16-row block); Phi(p)
+// (64 KiB) arrives by one bulk copy, double buffered one segment ahead; the
+// 16 rows of S_start(p) stay in shared memory between steps.  Thread (col,
+// rh) produces S[r0 + 8 rh + i][col] for i < 8.
+constexpr int kComposeThreads = 256;
+constexpr int kComposeRows = 16;
+constexpr int kCmpPhi = 0;                  // 2 x 64 KiB
+constexpr int kCmpX = 2 * 65536;            // 16 x 128 fp32
+constexpr int kCmpBar = kCmpX + kComposeRows * kD * 4;
+constexpr int kCmpBroken = kCmpBar + 16;
+constexpr int kCmpSmem = kCmpBroken + 16 + 128;  // + base alignment slack
+
+__global__ void __launch_bounds__(kComposeThreads, 1)
+gdn_prefill_compose_kernel(const int *__restrict__ meta, const int *__restrict__ seg_off,
+                           float *seg_ss, const float *__restrict__ seg_sb,
+                           const float *__restrict__ seg_phi) {
+  if (meta[1] != 0) return;
+  const int n = blockIdx.x, hv = blockIdx.y, r0 = blockIdx.z * kComposeRows;
+  const int P = seg_off[n + 1] - seg_off[n];
+  if (P < 3) return;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(align_up(reinterpret_cast<size_t>(smem_raw), 128));
+  float *X = reinterpret_cast<float *>(smem + kCmpX);
+  volatile int *broken = reinterpret_cast<volatile int *>(smem + kCmpBroken);
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t bar0 = s_base + kCmpBar;
+  const int tid = threadIdx.x, col = tid & 127, rh = tid >> 7;
+  const int64_t per_seg = static_cast<int64_t>(kHV) * kD * kD;
+  const int64_t base = static_cast<int64_t>(seg_off[n]) * per_seg + static_cast<int64_t>(hv) * kD * kD;
+
+  if (tid == 0) {
+    *broken = 0;
+    mbar_init(bar0, 1);
+    mbar_init(bar0 + 8, 1);
+    mbar_init_fence();
+  }
+  {
+    const float4 *src = reinterpret_cast<const float4 *>(seg_ss + base + per_seg + r0 * kD);
+    float4 *dst = reinterpret_cast<float4 *>(X);
+    for (int i = tid; i < kComposeRows * kD / 4; i += kComposeThreads) dst[i] = src[i];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar0, 65536);
+    bulk_load(s_base + kCmpPhi, seg_phi + base + per_seg, 65536, bar0);
+  }
+  uint32_t ph0 = 0, ph1 = 0;
+  for (int p = 1; p + 1 < P; ++p) {
+    const int b = (p - 1) & 1;
+    // the other buffer was last read in step p-1, which every thread has left
+    if (tid == 0 && p + 2 < P) {
+      mbar_arrive_expect_tx(bar0 + 8 * (b ^ 1), 65536);
+      bulk_load(s_base + kCmpPhi + 65536 * (b ^ 1), seg_phi + base + (p + 1) * per_seg, 65536,
+                bar0 + 8 * (b ^ 1));
+    }
+    if (b == 0) {
+      wait_phase(bar0, ph0, broken);
+      ph0 ^= 1;
+    } else {
+      wait_phase(bar0 + 8, ph1, broken);
+      ph1 ^= 1;
+    }
+    const float *Phi = reinterpret_cast<const float *>(smem + kCmpPhi + 65536 * b);
+    const float *Bp = seg_sb + base + p * per_seg + static_cast<int64_t>(r0 + 8 * rh) * kD + col;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = Bp[i * kD];
+    const float4 *X4 = reinterpret_cast<const float4 *>(X) + (8 * rh) * (kD / 4);
+#pragma unroll 2
+    for (int kk = 0; kk < kD; kk += 4) {
+      const float f0 = Phi[(kk + 0) * kD + col], f1 = Phi[(kk + 1) * kD + col],
+                  f2 = Phi[(kk + 2) * kD + col], f3 = Phi[(kk + 3) * kD + col];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 x = X4[i * (kD / 4) + kk / 4];
+        acc[i] = fmaf(x.x, f0, acc[i]);
+        acc[i] = fmaf(x.y, f1, acc[i]);
+        acc[i] = fmaf(x.z, f2, acc[i]);
+        acc[i] = fmaf(x.w, f3, acc[i]);
+      }
+    }
+    __syncthreads();  // all reads of X and of this Phi buffer are done
+    float *dst = seg_ss + base + (p + 1) * per_seg + static_cast<int64_t>(r0 + 8 * rh) * kD + col;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      X[(8 * rh + i) * kD + col] = acc[i];
+      dst[i * kD] = acc[i];
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host launcher
 // ---------------------------------------------------------------------------
-size_t prefill_workspace_bytes(int64_t T, int64_t N) { return prefill_ws_layout(T, N).total; }
+size_t prefill_workspace_bytes(int64_t T, int64_t N, bool allow_segments) {
+  return prefill_ws_layout(T, N, allow_segments).total;
+}
+
+int prefill_kernel_launches(int64_t T, int64_t N, bool allow_segments) {
+  if (N == 0) return 0;
+  const PrefillWs w = prefill_ws_layout(T, N, allow_segments);
+  return (w.nt_max > 0 ? 3 : 2) + (w.seg_chunks ? 2 : 0);
+}
 
 static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -965,11 +1202,10 @@ static bool make_tmap_2d(CUtensorMap *m, const void *base, uint64_t row_elems, u
 cudaError_t launch_prefill(const void *q, const void *k, const void *v, const float *state,
                            const float *A_log, const void *a, const float *dt_bias, const void *b,
                            const int64_t *cu_seqlens, int64_t N, int64_t T, float scale,
-                           void *out, float *final_state, void *workspace, int num_sms,
+                           void *out, float *final_state, void *workspace, bool allow_segments,
                            cudaStream_t stream) {
-  (void)num_sms;
   if (N == 0) return cudaSuccess;
-  const PrefillWs w = prefill_ws_layout(T, N);
+  const PrefillWs w = prefill_ws_layout(T, N, allow_segments);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   int *meta = reinterpret_cast<int *>(ws + w.meta);
   int *chunk_off = reinterpret_cast<int *>(ws + w.chunk_off);
@@ -978,6 +1214,12 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   float *gcum = reinterpret_cast<float *>(ws + w.gcum);
   float *beta = reinterpret_cast<float *>(ws + w.beta);
   uint8_t *m2 = ws + w.m2;
+  int4 *items = reinterpret_cast<int4 *>(ws + w.items);
+  int *seg_off = reinterpret_cast<int *>(ws + w.seg_off);
+  float *seg_ss = reinterpret_cast<float *>(ws + w.seg_ss);
+  float *seg_sb = reinterpret_cast<float *>(ws + w.seg_sb);
+  float *seg_phi = reinterpret_cast<float *>(ws + w.seg_phi);
+  const int64_t seg_tokens = w.seg_chunks ? w.seg_chunks * kChunk : (int64_t{1} << 40);
 
   CUtensorMap tq, tk, tv;
   memset(&tq, 0, sizeof(tq));
@@ -990,9 +1232,9 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
       return cudaErrorInvalidValue;
   }
 
-  gdn_prefill_meta_kernel<<<1, kMetaThreads, 0, stream>>>(cu_seqlens, static_cast<int>(N), T,
-                                                          w.nt_max, meta, chunk_off, seq_order,
-                                                          chunk_tab);
+  gdn_prefill_meta_kernel<<<1, kMetaThreads, 0, stream>>>(
+      cu_seqlens, static_cast<int>(N), T, w.nt_max, meta, chunk_off, seq_order, chunk_tab,
+      static_cast<int>(w.seg_chunks), static_cast<int>(w.seg_max), items, seg_off);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
 
@@ -1010,10 +1252,29 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   err = cudaFuncSetAttribute(gdn_prefill_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              ScanSmem::kBytes);
   if (err != cudaSuccess) return err;
-  gdn_prefill_scan_kernel<<<static_cast<unsigned>(N * kHV), kScanThreads, ScanSmem::kBytes,
-                            stream>>>(tq, tk, tv, state, cu_seqlens, meta, chunk_off, seq_order,
-                                      gcum, beta, m2, scale, static_cast<uint16_t *>(out),
-                                      final_state);
+  // pass 1 (the only pass without segmentation)
+  const int64_t n1 = w.seg_chunks ? 2 * w.seg_max : N;
+  gdn_prefill_scan_kernel<<<static_cast<unsigned>(n1 * kHV), kScanThreads, ScanSmem::kBytes,
+                            stream>>>(tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta,
+                                      m2, scale, static_cast<uint16_t *>(out), final_state, items,
+                                      2, seg_tokens, seg_off, seg_ss, seg_sb, seg_phi);
+  err = cudaGetLastError();
+  if (err != cudaSuccess || w.seg_chunks == 0) return err;
+
+  err = cudaFuncSetAttribute(gdn_prefill_compose_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kCmpSmem);
+  if (err != cudaSuccess) return err;
+  dim3 cgrid(static_cast<unsigned>(N), kHV, kD / kComposeRows);
+  gdn_prefill_compose_kernel<<<cgrid, kComposeThreads, kCmpSmem, stream>>>(meta, seg_off, seg_ss,
+                                                                           seg_sb, seg_phi);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  // pass 3
+  gdn_prefill_scan_kernel<<<static_cast<unsigned>(w.seg_max * kHV), kScanThreads,
+                            ScanSmem::kBytes, stream>>>(
+      tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale,
+      static_cast<uint16_t *>(out), final_state, items + 2 * w.seg_max, 3, seg_tokens, seg_off,
+      seg_ss, seg_sb, seg_phi);
   return cudaGetLastError();
 }
 

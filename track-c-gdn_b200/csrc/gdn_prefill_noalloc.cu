@@ -64,8 +64,13 @@ extern "C" int gdn_prefill_qk4_v8_d128_k_last_noalloc(
       num_seqs > (int64_t{1} << 24))
     return GDN_ERR_BAD_SIZE;
   if (num_seqs == 0) return total_tokens == 0 ? GDN_OK : GDN_ERR_BAD_SIZE;
-  const size_t need = gdn::prefill_workspace_bytes(total_tokens, num_seqs);
-  if (need > gdn::kNoallocScratchBytes) return GDN_ERR_TOO_LARGE;
+  // the segmented evaluation when its larger workspace fits the scratch,
+  // else the single-pass one
+  const bool segments =
+      gdn::prefill_workspace_bytes(total_tokens, num_seqs, true) <= gdn::kNoallocScratchBytes;
+  if (!segments &&
+      gdn::prefill_workspace_bytes(total_tokens, num_seqs, false) > gdn::kNoallocScratchBytes)
+    return GDN_ERR_TOO_LARGE;
   if (!cu_seqlens || !A_log || !dt_bias || !final_state) return GDN_ERR_NULL_POINTER;
   if (total_tokens > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL_POINTER;
   if ((q && !aligned(q, 16)) || (k && !aligned(k, 16)) || (v && !aligned(v, 16)) ||
@@ -75,15 +80,14 @@ extern "C" int gdn_prefill_qk4_v8_d128_k_last_noalloc(
   const size_t state_bytes = static_cast<size_t>(num_seqs) * gdn::kHV * gdn::kD * gdn::kD * 4;
   if (state && state != final_state && overlap(state, state_bytes, final_state, state_bytes))
     return GDN_ERR_ALIASING;
-  int sms = 0;
-  if (int st = check_device(&sms)) return st;
+  if (int st = check_device(nullptr)) return st;
   void *scratch = nullptr;
   if (int st = gdn::noalloc_scratch_address(&scratch)) return st;
   const uintptr_t base = reinterpret_cast<uintptr_t>(scratch);
   void *ws = reinterpret_cast<void *>((base + 1023) & ~uintptr_t{1023});
   if (scale == 0.0f) scale = kDefaultScale;
   cudaError_t err = gdn::launch_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
-                                        total_tokens, scale, out, final_state, ws, sms,
+                                        total_tokens, scale, out, final_state, ws, segments,
                                         static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
