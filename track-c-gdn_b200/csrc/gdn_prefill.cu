@@ -34,6 +34,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "gdn_common.cuh"
 #include "sm100.cuh"
@@ -770,12 +771,10 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                  bar_v = s_base + SM::kBarV, bar_m2 = s_base + SM::kBarM2,
                  bar_k0 = s_base + SM::kBarK0;
 
-  if (warp == 0) tmem_alloc(s_base + SM::kTmem, SM::kTmemCols);
-  if (tid == 0) {
-    *broken = 0;
-    for (int i = 0; i < 6; ++i) mbar_init(bar_mma + 8 * i, 1);
-    mbar_init_fence();
-  }
+  // Items without outputs (ZERO, IDENT) need neither Q nor the Q-side MMAs;
+  // IDENT treats V as zero and needs no V either.
+  const bool need_q = write_out;
+  const bool need_v = !ident;
 
   // Chunk operand loads, all issued by thread 0.
   auto issue_qk = [&](bool is_k, int c, uint32_t dst, uint32_t bar) {
@@ -817,6 +816,24 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     if (tid == 0) Egl[buf] = expf(r.g_last);
   };
 
+  // Barriers first, then the first chunk's operand loads and gates, so their
+  // latency overlaps the initial-state load below.
+  if (warp == 0) tmem_alloc(s_base + SM::kTmem, SM::kTmemCols);
+  if (tid == 0) {
+    *broken = 0;
+    for (int i = 0; i < 6; ++i) mbar_init(bar_mma + 8 * i, 1);
+    mbar_init_fence();
+    if (nchunks > 0) {
+      if (need_q) issue_qk(false, 0, s_base + SM::kQ, bar_q);
+      issue_qk(true, 0, s_base + SM::kK0, bar_k0);
+      if (nchunks > 1) issue_qk(true, 1, s_base + SM::kK1, bar_k0 + 8);
+      if (need_v) issue_v(0);
+      issue_m2(0);
+    }
+  }
+  GateRegs gates0;
+  if (tid < 64 && nchunks > 0) gates0 = fetch_gates(0);
+
   // fp32 state row slice S[v][64 hc .. 64 hc + 63].
   float s[64];
   if (init != nullptr) {
@@ -842,16 +859,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(s[2 * j], s[2 * j + 1]);
     tmem_st32(tlane + SM::kColSb + 32 * hc, pk);
   }
-  if (nchunks > 0) {
-    if (tid == 0) {
-      issue_qk(false, 0, s_base + SM::kQ, bar_q);
-      issue_qk(true, 0, s_base + SM::kK0, bar_k0);
-      if (nchunks > 1) issue_qk(true, 1, s_base + SM::kK1, bar_k0 + 8);
-      issue_v(0);
-      issue_m2(0);
-    }
-    if (tid < 64) store_gates(fetch_gates(0), 0);
-  }
+  if (tid < 64 && nchunks > 0) store_gates(gates0, 0);
   tmem_wait_st();
   tc_fence_before();
   __syncthreads();
@@ -861,190 +869,208 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const uint32_t idesc_ds = umma_idesc_bf16(128, 128, false, true);
   uint32_t ph_mma = 0, ph_q = 0, ph_v = 0, ph_m2 = 0, ph_k = 0;  // ph_k: bit b = parity of K buffer b
 
-  for (int c = 0; c < nchunks; ++c) {
-    const int cb = c & 1;
-    const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
-    const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
-    const uint32_t kbuf = s_base + (cb ? SM::kK1 : SM::kK0);
-    const uint32_t bar_k = bar_k0 + 8 * cb;
-    GateRegs next_gates;
-    if (tid < 64 && c + 1 < nchunks) next_gates = fetch_gates(c + 1);
+  // The chunk loop, instantiated twice: with outputs (FULL, HEAD, MID, TAIL)
+  // and state only (ZERO, IDENT).  Compile-time flags keep the loop free of
+  // per-chunk mode branches.
+  auto chunk_loop = [&](auto out_tag) {
+    constexpr bool kOut = decltype(out_tag)::value;
+    for (int c = 0; c < nchunks; ++c) {
+      const int cb = c & 1;
+      const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
+      const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
+      const uint32_t kbuf = s_base + (cb ? SM::kK1 : SM::kK0);
+      const uint32_t bar_k = bar_k0 + 8 * cb;
+      GateRegs next_gates;
+      if (tid < 64 && c + 1 < nchunks) next_gates = fetch_gates(c + 1);
 
-    // Q, K and [PA;Ainv] are read only by the tensor core, so only the MMA
-    // thread waits for them: thread 0 re-arms each barrier for the next chunk
-    // right after the MMA that consumed it, and a thread still polling the
-    // old phase could otherwise see two completions and wait forever.  The
-    // one exception is the tail chunk (always the last, so never re-armed):
-    // every thread must see its tiles landed before zeroing rows.
-    const bool tail = L < kChunk;
-    if (tid == 0 || tail) {
-      wait_phase(bar_k, (ph_k >> cb) & 1, broken);
-      if (tail) wait_phase(bar_q, ph_q, broken);
-    }
-    ph_k ^= 1u << cb;
-    if (tail) {
-      // tail chunk: zero the rows past the sequence end (TMA brought in the
-      // next sequence's tokens there)
-      for (int idx = tid; idx < 2 * 2 * (kChunk - L) * 8; idx += kScanThreads) {
-        const int ch = idx & 7, r = L + ((idx >> 3) % (kChunk - L)), blk = (idx >> 3) / (kChunk - L);
-        const int which = blk >> 1, dblk = blk & 1;
-        uint8_t *tile = smem + (which ? (cb ? SM::kK1 : SM::kK0) : SM::kQ);
-        *reinterpret_cast<uint4 *>(tile + dblk * 8192 + r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+      // Q, K and [PA;Ainv] are read only by the tensor core, so only the MMA
+      // thread waits for them: thread 0 re-arms each barrier for the next chunk
+      // right after the MMA that consumed it, and a thread still polling the
+      // old phase could otherwise see two completions and wait forever.  The
+      // one exception is the tail chunk (always the last, so never re-armed):
+      // every thread must see its tiles landed before zeroing rows.
+      const bool tail = L < kChunk;
+      if (tid == 0 || tail) {
+        wait_phase(bar_k, (ph_k >> cb) & 1, broken);
+        if (tail && kOut) wait_phase(bar_q, ph_q, broken);
+      }
+      ph_k ^= 1u << cb;
+      if (tail) {
+        // tail chunk: zero the rows past the sequence end (TMA brought in the
+        // next sequence's tokens there)
+        for (int idx = tid; idx < 2 * 2 * (kChunk - L) * 8; idx += kScanThreads) {
+          const int ch = idx & 7, r = L + ((idx >> 3) % (kChunk - L)), blk = (idx >> 3) / (kChunk - L);
+          const int which = blk >> 1, dblk = blk & 1;
+          uint8_t *tile = smem + (which ? (cb ? SM::kK1 : SM::kK0) : SM::kQ);
+          *reinterpret_cast<uint4 *>(tile + dblk * 8192 + r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+        }
+        fence_async_smem();
+        __syncthreads();
+      }
+
+      // ---- MMA 1: Yk = S K^T (committed first: X needs it), then Yq = S Q^T
+      // (read only after MMA 2, whose commit also covers it) ----
+      if (tid == 0) {
+        tc_fence_after();
+  #pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
+          umma_bf16_ts(tmem + SM::kColY + 64, tmem + SM::kColSb + 8 * ks,
+                       umma_desc_sw128(kbuf + boff, 16, 1024), idesc_n64, ks > 0);
+        }
+        umma_commit(bar_mma);
+        if constexpr (kOut) {
+          if (!tail) wait_phase(bar_q, ph_q, broken);
+  #pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
+            umma_bf16_ts(tmem + SM::kColY, tmem + SM::kColSb + 8 * ks,
+                         umma_desc_sw128(s_base + SM::kQ + boff, 16, 1024), idesc_n64, ks > 0);
+          }
+        }
+      }
+      ph_q ^= 1;
+      wait_phase(bar_mma, ph_mma, broken);
+      ph_mma ^= 1;
+      tc_fence_after();
+      if (kOut || need_v) {
+        wait_phase(bar_v, ph_v, broken);
+        ph_v ^= 1;
+      }
+
+      // ---- X = beta (V - e^G Yk) -> smem ----
+  #pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int tb = 32 * hc + 16 * p;
+        float yk[16];
+        tmem_ld16(tlane + SM::kColY + 64 + tb, yk);
+        tmem_wait_ld();
+  #pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const float4 eg4 = *reinterpret_cast<const float4 *>(Eg + cb * 64 + tb + 4 * g);
+          const float4 bt4 = *reinterpret_cast<const float4 *>(Bs + cb * 64 + tb + 4 * g);
+          const float eg[4] = {eg4.x, eg4.y, eg4.z, eg4.w};
+          const float bt[4] = {bt4.x, bt4.y, bt4.z, bt4.w};
+  #pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int j = 4 * g + u, t = tb + j;
+            const float vv = (t < L && (kOut || !ident)) ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
+            yk[j] = bt[u] * (vv - eg[u] * yk[j]);
+          }
+        }
+        store16_bf16(xv, vrow, tb >> 3, yk);
       }
       fence_async_smem();
+      tc_fence_before();
       __syncthreads();
-    }
-
-    // ---- MMA 1: Yk = S K^T (committed first: X needs it), then Yq = S Q^T
-    // (read only after MMA 2, whose commit also covers it) ----
-    if (tid == 0) {
       tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
-        umma_bf16_ts(tmem + SM::kColY + 64, tmem + SM::kColSb + 8 * ks,
-                     umma_desc_sw128(kbuf + boff, 16, 1024), idesc_n64, ks > 0);
-      }
-      umma_commit(bar_mma);
-      if (!tail) wait_phase(bar_q, ph_q, broken);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
-        umma_bf16_ts(tmem + SM::kColY, tmem + SM::kColSb + 8 * ks,
-                     umma_desc_sw128(s_base + SM::kQ + boff, 16, 1024), idesc_n64, ks > 0);
-      }
-    }
-    ph_q ^= 1;
-    wait_phase(bar_mma, ph_mma, broken);
-    ph_mma ^= 1;
-    tc_fence_after();
-    wait_phase(bar_v, ph_v, broken);
-    ph_v ^= 1;
+      if (tid == 0 && (kOut || need_v) && c + 1 < nchunks) issue_v(c + 1);
 
-    // ---- X = beta (V - e^G Yk) -> smem ----
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const int tb = 32 * hc + 16 * p;
-      float yk[16];
-      tmem_ld16(tlane + SM::kColY + 64 + tb, yk);
-      tmem_wait_ld();
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const float4 eg4 = *reinterpret_cast<const float4 *>(Eg + cb * 64 + tb + 4 * g);
-        const float4 bt4 = *reinterpret_cast<const float4 *>(Bs + cb * 64 + tb + 4 * g);
-        const float eg[4] = {eg4.x, eg4.y, eg4.z, eg4.w};
-        const float bt[4] = {bt4.x, bt4.y, bt4.z, bt4.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = 4 * g + u, t = tb + j;
-          const float vv = (t < L && !ident) ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
-          yk[j] = bt[u] * (vv - eg[u] * yk[j]);
+      // ---- MMA 2: O_intra = X PA^T (free columns 64..127), V_new = X Ainv^T ----
+      if (tid == 0) {
+        wait_phase(bar_m2, ph_m2, broken);
+        tc_fence_after();
+        if constexpr (kOut) {
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16(tmem + SM::kColOi, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
+                      umma_desc_sw128(s_base + SM::kM2 + ks * 32, 16, 1024), idesc_n64, ks > 0);
         }
+  #pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_bf16(tmem + SM::kColY + 64, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
+                    umma_desc_sw128(s_base + SM::kM2 + 8192 + ks * 32, 16, 1024), idesc_n64,
+                    ks > 0);
+        umma_commit(bar_mma);
       }
-      store16_bf16(xv, vrow, tb >> 3, yk);
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0 && c + 1 < nchunks) issue_v(c + 1);
-
-    // ---- MMA 2: O_intra = X PA^T (free columns 64..127), V_new = X Ainv^T ----
-    if (tid == 0) {
-      wait_phase(bar_m2, ph_m2, broken);
+      ph_m2 ^= 1;
+      wait_phase(bar_mma, ph_mma, broken);
+      ph_mma ^= 1;
       tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(tmem + SM::kColOi, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
-                  umma_desc_sw128(s_base + SM::kM2 + ks * 32, 16, 1024), idesc_n64, ks > 0);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(tmem + SM::kColY + 64, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
-                  umma_desc_sw128(s_base + SM::kM2 + 8192 + ks * 32, 16, 1024), idesc_n64,
-                  ks > 0);
-      umma_commit(bar_mma);
-    }
-    ph_m2 ^= 1;
-    wait_phase(bar_mma, ph_mma, broken);
-    ph_mma ^= 1;
-    tc_fence_after();
-    if (tid == 0 && c + 1 < nchunks) {
-      issue_m2(c + 1);
-      issue_qk(false, c + 1, s_base + SM::kQ, bar_q);  // MMA 1's Q reads are done too
-    }
-
-    // ---- outputs O = scale (e^G Yq + O_intra) and V_dec ----
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const int tb = 32 * hc + 16 * p;
-      float zq[16], zo[16];
-      tmem_ld16(tlane + SM::kColY + tb, zq);
-      tmem_ld16(tlane + SM::kColOi + tb, zo);
-      tmem_wait_ld();
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const float4 eg4 = *reinterpret_cast<const float4 *>(Eg + cb * 64 + tb + 4 * g);
-        const float eg[4] = {eg4.x, eg4.y, eg4.z, eg4.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = 4 * g + u, t = tb + j;
-          if (write_out && t < L)
-            out[((t0 + t) * kHV + hv) * kD + vrow] =
-                __bfloat16_as_ushort(__float2bfloat16_rn(scale * (eg[u] * zq[j] + zo[j])));
-        }
+      if (tid == 0 && c + 1 < nchunks) {
+        issue_m2(c + 1);
+        if constexpr (kOut) issue_qk(false, c + 1, s_base + SM::kQ, bar_q);  // MMA 1's Q reads are done too
       }
-      float zv[16];
-      tmem_ld16(tlane + SM::kColY + 64 + tb, zv);
-      tmem_wait_ld();
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const float4 ed4 = *reinterpret_cast<const float4 *>(Ed + cb * 64 + tb + 4 * g);
-        const float ed[4] = {ed4.x, ed4.y, ed4.z, ed4.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) zv[4 * g + u] *= ed[u];  // e^{G_last - G_t}, 0 past the end
-      }
-      store16_bf16(xv, vrow, tb >> 3, zv);
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
 
-    // ---- MMA 3: dS = V_dec K ----
-    if (tid == 0) {
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(tmem + SM::kColY, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
-                  umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), idesc_ds, ks > 0);
-      umma_commit(bar_mma);
-    }
-    if (tid < 64 && c + 1 < nchunks) store_gates(next_gates, cb ^ 1);
-    wait_phase(bar_mma, ph_mma, broken);
-    ph_mma ^= 1;
-    tc_fence_after();
-    if (tid == 0 && c + 2 < nchunks) issue_qk(true, c + 2, kbuf, bar_k);
-
-    // ---- S = e^{G_last} S + dS ;  bf16(S) -> TMEM ----
-    {
-      const float eg_last = Egl[cb];
-#pragma unroll
+      // ---- outputs O = scale (e^G Yq + O_intra) and V_dec ----
+  #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        float ds[32];
-        tmem_ld32(tlane + SM::kColY + 64 * hc + 32 * p, ds);
+        const int tb = 32 * hc + 16 * p;
+        if constexpr (kOut) {
+          float zq[16], zo[16];
+          tmem_ld16(tlane + SM::kColY + tb, zq);
+          tmem_ld16(tlane + SM::kColOi + tb, zo);
+          tmem_wait_ld();
+  #pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const float4 eg4 = *reinterpret_cast<const float4 *>(Eg + cb * 64 + tb + 4 * g);
+            const float eg[4] = {eg4.x, eg4.y, eg4.z, eg4.w};
+  #pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int j = 4 * g + u, t = tb + j;
+              if (t < L)
+                out[((t0 + t) * kHV + hv) * kD + vrow] =
+                    __bfloat16_as_ushort(__float2bfloat16_rn(scale * (eg[u] * zq[j] + zo[j])));
+            }
+          }
+        }
+        float zv[16];
+        tmem_ld16(tlane + SM::kColY + 64 + tb, zv);
         tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) s[32 * p + j] = eg_last * s[32 * p + j] + ds[j];
+  #pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const float4 ed4 = *reinterpret_cast<const float4 *>(Ed + cb * 64 + tb + 4 * g);
+          const float ed[4] = {ed4.x, ed4.y, ed4.z, ed4.w};
+  #pragma unroll
+          for (int u = 0; u < 4; ++u) zv[4 * g + u] *= ed[u];  // e^{G_last - G_t}, 0 past the end
+        }
+        store16_bf16(xv, vrow, tb >> 3, zv);
       }
-      uint32_t pk[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(s[2 * j], s[2 * j + 1]);
-      tmem_st32(tlane + SM::kColSb + 32 * hc, pk);
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+
+      // ---- MMA 3: dS = V_dec K ----
+      if (tid == 0) {
+  #pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_bf16(tmem + SM::kColY, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
+                    umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), idesc_ds, ks > 0);
+        umma_commit(bar_mma);
+      }
+      if (tid < 64 && c + 1 < nchunks) store_gates(next_gates, cb ^ 1);
+      wait_phase(bar_mma, ph_mma, broken);
+      ph_mma ^= 1;
+      tc_fence_after();
+      if (tid == 0 && c + 2 < nchunks) issue_qk(true, c + 2, kbuf, bar_k);
+
+      // ---- S = e^{G_last} S + dS ;  bf16(S) -> TMEM ----
+      {
+        const float eg_last = Egl[cb];
+  #pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          float ds[32];
+          tmem_ld32(tlane + SM::kColY + 64 * hc + 32 * p, ds);
+          tmem_wait_ld();
+  #pragma unroll
+          for (int j = 0; j < 32; ++j) s[32 * p + j] = eg_last * s[32 * p + j] + ds[j];
+        }
+        uint32_t pk[32];
+  #pragma unroll
+        for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(s[2 * j], s[2 * j + 1]);
+        tmem_st32(tlane + SM::kColSb + 32 * hc, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
     }
-    tmem_wait_st();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-  }
+  };
+  if (write_out)
+    chunk_loop(std::true_type{});
+  else
+    chunk_loop(std::false_type{});
 
   if (fin != nullptr) {
 #pragma unroll
@@ -1065,15 +1091,18 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // 4. segment composition (segmented mode only)
 // ---------------------------------------------------------------------------
 // S_start(p+1) = S_start(p) Phi(p) + B(p) for p = 1 .. P-2, in fp32.  Rows of
-// S are independent, so one CTA per (sequence, v-head, 16-row block); Phi(p)
-// (64 KiB) arrives by one bulk copy, double buffered one segment ahead; the
-// 16 rows of S_start(p) stay in shared memory between steps.  Thread (col,
-// rh) produces S[r0 + 8 rh + i][col] for i < 8.
+// S are independent, so one CTA per (sequence, v-head, 8-row block); Phi(p)
+// (64 KiB) arrives by one bulk copy, double buffered one segment ahead, and
+// B(p+1) is read into registers during step p; the 8 rows of S_start(p)
+// stay in shared memory (double buffered) between steps, so a step needs one
+// CTA barrier.  Thread (col, rh) produces S[r0 + 4 rh + i][col] for i < 4;
+// the fully unrolled k loop lets the loads run ahead of the FMAs.
 constexpr int kComposeThreads = 256;
-constexpr int kComposeRows = 16;
-constexpr int kCmpPhi = 0;                  // 2 x 64 KiB
-constexpr int kCmpX = 2 * 65536;            // 16 x 128 fp32
-constexpr int kCmpBar = kCmpX + kComposeRows * kD * 4;
+constexpr int kComposeRows = 8;
+constexpr int kCmpPhi = 0;                                   // 2 x 64 KiB
+constexpr int kCmpX = 2 * 65536;                             // 2 x (8 x 128 fp32)
+constexpr int kCmpXBytes = kComposeRows * kD * 4;
+constexpr int kCmpBar = kCmpX + 2 * kCmpXBytes;
 constexpr int kCmpBroken = kCmpBar + 16;
 constexpr int kCmpSmem = kCmpBroken + 16 + 128;  // + base alignment slack
 
@@ -1087,13 +1116,13 @@ gdn_prefill_compose_kernel(const int *__restrict__ meta, const int *__restrict__
   if (P < 3) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(align_up(reinterpret_cast<size_t>(smem_raw), 128));
-  float *X = reinterpret_cast<float *>(smem + kCmpX);
   volatile int *broken = reinterpret_cast<volatile int *>(smem + kCmpBroken);
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar0 = s_base + kCmpBar;
   const int tid = threadIdx.x, col = tid & 127, rh = tid >> 7;
   const int64_t per_seg = static_cast<int64_t>(kHV) * kD * kD;
   const int64_t base = static_cast<int64_t>(seg_off[n]) * per_seg + static_cast<int64_t>(hv) * kD * kD;
+  const int64_t my_rows = static_cast<int64_t>(r0 + 4 * rh) * kD + col;
 
   if (tid == 0) {
     *broken = 0;
@@ -1103,9 +1132,12 @@ gdn_prefill_compose_kernel(const int *__restrict__ meta, const int *__restrict__
   }
   {
     const float4 *src = reinterpret_cast<const float4 *>(seg_ss + base + per_seg + r0 * kD);
-    float4 *dst = reinterpret_cast<float4 *>(X);
+    float4 *dst = reinterpret_cast<float4 *>(smem + kCmpX);
     for (int i = tid; i < kComposeRows * kD / 4; i += kComposeThreads) dst[i] = src[i];
   }
+  float bnext[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) bnext[i] = seg_sb[base + per_seg + my_rows + i * kD];
   __syncthreads();
   if (tid == 0) {
     mbar_arrive_expect_tx(bar0, 65536);
@@ -1114,11 +1146,18 @@ gdn_prefill_compose_kernel(const int *__restrict__ meta, const int *__restrict__
   uint32_t ph0 = 0, ph1 = 0;
   for (int p = 1; p + 1 < P; ++p) {
     const int b = (p - 1) & 1;
-    // the other buffer was last read in step p-1, which every thread has left
+    // the other Phi buffer was last read in step p-1, which every thread has left
     if (tid == 0 && p + 2 < P) {
       mbar_arrive_expect_tx(bar0 + 8 * (b ^ 1), 65536);
       bulk_load(s_base + kCmpPhi + 65536 * (b ^ 1), seg_phi + base + (p + 1) * per_seg, 65536,
                 bar0 + 8 * (b ^ 1));
+    }
+    float acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = bnext[i];
+    if (p + 2 < P) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) bnext[i] = seg_sb[base + (p + 1) * per_seg + my_rows + i * kD];
     }
     if (b == 0) {
       wait_phase(bar0, ph0, broken);
@@ -1127,18 +1166,15 @@ gdn_prefill_compose_kernel(const int *__restrict__ meta, const int *__restrict__
       wait_phase(bar0 + 8, ph1, broken);
       ph1 ^= 1;
     }
-    const float *Phi = reinterpret_cast<const float *>(smem + kCmpPhi + 65536 * b);
-    const float *Bp = seg_sb + base + p * per_seg + static_cast<int64_t>(r0 + 8 * rh) * kD + col;
-    float acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = Bp[i * kD];
-    const float4 *X4 = reinterpret_cast<const float4 *>(X) + (8 * rh) * (kD / 4);
-#pragma unroll 2
+    const float *Phi = reinterpret_cast<const float *>(smem + kCmpPhi + 65536 * b) + col;
+    const float4 *X4 =
+        reinterpret_cast<const float4 *>(smem + kCmpX + kCmpXBytes * b) + (4 * rh) * (kD / 4);
+#pragma unroll 4
     for (int kk = 0; kk < kD; kk += 4) {
-      const float f0 = Phi[(kk + 0) * kD + col], f1 = Phi[(kk + 1) * kD + col],
-                  f2 = Phi[(kk + 2) * kD + col], f3 = Phi[(kk + 3) * kD + col];
+      const float f0 = Phi[(kk + 0) * kD], f1 = Phi[(kk + 1) * kD], f2 = Phi[(kk + 2) * kD],
+                  f3 = Phi[(kk + 3) * kD];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 4; ++i) {
         const float4 x = X4[i * (kD / 4) + kk / 4];
         acc[i] = fmaf(x.x, f0, acc[i]);
         acc[i] = fmaf(x.y, f1, acc[i]);
@@ -1146,11 +1182,12 @@ gdn_prefill_compose_kernel(const int *__restrict__ meta, const int *__restrict__
         acc[i] = fmaf(x.w, f3, acc[i]);
       }
     }
-    __syncthreads();  // all reads of X and of this Phi buffer are done
-    float *dst = seg_ss + base + (p + 1) * per_seg + static_cast<int64_t>(r0 + 8 * rh) * kD + col;
+    // next step reads the other X buffer, whose last readers (step p-1) are done
+    float *xo = reinterpret_cast<float *>(smem + kCmpX + kCmpXBytes * (b ^ 1)) + (4 * rh) * kD + col;
+    float *dst = seg_ss + base + (p + 1) * per_seg + my_rows;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      X[(8 * rh + i) * kD + col] = acc[i];
+    for (int i = 0; i < 4; ++i) {
+      xo[i * kD] = acc[i];
       dst[i * kD] = acc[i];
     }
     __syncthreads();
