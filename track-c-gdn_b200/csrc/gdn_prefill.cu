@@ -130,6 +130,15 @@ inline PrefillWs prefill_ws_layout(int64_t T, int64_t N, bool allow_segments = t
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int64_t lmin(int64_t x, int64_t y) { return x < y ? x : y; }
 
+// Aligns the dynamic shared-memory base to A bytes by offsetting the
+// __shared__ array itself (not through an integer cast), so the compiler
+// still knows every access through the result is a shared-memory access.
+template <uint32_t A>
+__device__ __forceinline__ uint8_t *smem_align(uint8_t *raw) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(raw));
+  return raw + ((A - (a & (A - 1))) & (A - 1));
+}
+
 __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
@@ -415,7 +424,7 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         const int2 *__restrict__ chunk_tab, float *__restrict__ gcum_ws,
                         float *__restrict__ beta_ws, uint8_t *__restrict__ m2_ws) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(align_up(reinterpret_cast<size_t>(smem_raw), 1024));
+  uint8_t *smem = smem_align<1024>(smem_raw);
   const int gchunk = blockIdx.x, hqk = blockIdx.y;
   if (meta[1] != 0 || gchunk >= meta[0]) return;
 
@@ -716,7 +725,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         float *seg_phi) {
   using SM = ScanSmem;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(align_up(reinterpret_cast<size_t>(smem_raw), 1024));
+  uint8_t *smem = smem_align<1024>(smem_raw);
   if (meta[1] != 0) return;
   const int item = blockIdx.x / kHV;
   if (item >= meta[count_slot]) return;
@@ -1115,7 +1124,7 @@ gdn_prefill_compose_kernel(const int *__restrict__ meta, const int *__restrict__
   const int P = seg_off[n + 1] - seg_off[n];
   if (P < 3) return;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(align_up(reinterpret_cast<size_t>(smem_raw), 128));
+  uint8_t *smem = smem_align<128>(smem_raw);
   volatile int *broken = reinterpret_cast<volatile int *>(smem + kCmpBroken);
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar0 = s_base + kCmpBar;
