@@ -316,16 +316,18 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
 // One CTA per (chunk, q/k head), 128 threads, both v-heads j = 0, 1 of the
 // q/k head.  The [Q;K] tile arrives by TMA; D = [Q;K] K^T on the tensor core
 // gives Q K^T (TMEM lanes 0..63) and K K^T (lanes 64..127) at once; each
-// thread turns one row into P_j (bf16 operand) or A_j (fp32, shared memory);
-// thread (j, c) solves column c of (I + A_j)^-1 by fp32 forward substitution;
-// a second MMA forms P_j Ainv_j.  Output per (chunk, v-head): the 16 KiB
-// [P Ainv ; Ainv] image in the scan kernel's shared-memory operand layout.
+// thread turns one row into P_j (bf16, parked in its own TMEM lane) or A_j
+// (fp32, shared memory); thread (j, c) solves column c of (I + A_j)^-1 by fp32
+// forward substitution; P moves into the retired A region and a second MMA
+// forms P_j Ainv_j.  Output per (chunk, v-head): the 16 KiB [P Ainv ; Ainv]
+// image in the scan kernel's shared-memory operand layout.  About 51 KB of
+// shared memory, 128 TMEM columns and 128 registers per thread: 4 CTAs/SM.
 constexpr int kPrepThreads = 128;
 // shared memory map (offsets from a 1024-byte aligned base)
-constexpr int kPrepQK = 0;          // [Q;K] tile 32 KB; after MMA 1 the fp32 A_0, A_1
-constexpr int kPrepPP = 32768;      // [P_0 ; P_1] bf16, K-major 128 x 64, 16 KB
-constexpr int kPrepAI = 49152;      // Ainv_0, Ainv_1 bf16, 64 x 64 each (2 x 8 KB)
-constexpr int kPrepG = 65536;       // float G[2][64]
+constexpr int kPrepQK = 0;          // [Q;K] tile 32 KB; after MMA 1 the fp32 A_0, A_1;
+                                    // after the solve [P_0 ; P_1] bf16, K-major 128 x 64
+constexpr int kPrepAI = 32768;      // Ainv_0, Ainv_1 bf16, 64 x 64 each (2 x 8 KB)
+constexpr int kPrepG = 49152;       // float G[2][64]
 constexpr int kPrepB = kPrepG + 512;    // float beta[2][64]
 constexpr int kPrepGn = kPrepB + 512;   // float gnext[2][64]: e^{gl_{t+1}} (1 at t = 63)
 constexpr int kPrepWt = kPrepGn + 512;  // float warp totals[4]
@@ -415,7 +417,7 @@ __device__ __forceinline__ void solve_unit_lower_column(const float *AT, int c, 
   }
 }
 
-__global__ void __launch_bounds__(kPrepThreads)
+__global__ void __launch_bounds__(kPrepThreads, 4)
 gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         const __grid_constant__ CUtensorMap tmap_k,
                         const float *__restrict__ A_log, const uint16_t *__restrict__ a,
@@ -435,7 +437,7 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const int L = static_cast<int>(lmin(kChunk, cu[e.x + 1] - t0));
 
   uint8_t *qk = smem + kPrepQK;
-  uint8_t *pp = smem + kPrepPP;
+  uint8_t *pp = smem + kPrepQK;  // P image, written only once A is no longer read
   uint8_t *ai = smem + kPrepAI;
   float *Gs = reinterpret_cast<float *>(smem + kPrepG);
   float *Bs = reinterpret_cast<float *>(smem + kPrepB);
@@ -543,6 +545,7 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     for (int j = 0; j < 2; ++j) {
       const float bi = Bs[j * 64 + i];
       float dec = 1.f;  // e^{G_i - G_c} for the current column c (1 for c >= i)
+      uint32_t prow[32];  // row i of P_j as bf16 pairs (warps 0,1)
 #pragma unroll
       for (int cc = 7; cc >= 0; --cc) {
         const float4 g0 = *reinterpret_cast<const float4 *>(Gn + j * 64 + 8 * cc);
@@ -568,15 +571,16 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
             const int col = 8 * cc + u;
             vals[u] = (rv && col <= i) ? a8[u] * dc[u] : 0.f;
           }
-          uint4 pk;
-          pk.x = pack_bf16x2(vals[0], vals[1]);
-          pk.y = pack_bf16x2(vals[2], vals[3]);
-          pk.z = pack_bf16x2(vals[4], vals[5]);
-          pk.w = pack_bf16x2(vals[6], vals[7]);
-          *reinterpret_cast<uint4 *>(pp + sw128(j * 64 + i, cc)) = pk;
+          prow[4 * cc + 0] = pack_bf16x2(vals[0], vals[1]);
+          prow[4 * cc + 1] = pack_bf16x2(vals[2], vals[3]);
+          prow[4 * cc + 2] = pack_bf16x2(vals[4], vals[5]);
+          prow[4 * cc + 3] = pack_bf16x2(vals[6], vals[7]);
         }
       }
+      // D's columns 0..63 were read above; lanes 0..63 now keep P_0 | P_1
+      if (warp < 2) tmem_st32(trow + 32 * j, prow);
     }
+    tmem_wait_st();
   }
   tc_fence_before();
   __syncthreads();
@@ -591,6 +595,24 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
                             tmem + (static_cast<uint32_t>(32 * warp) << 16) + 64, ai + j * 8192);
   }
 
+  tc_fence_before();
+  __syncthreads();  // every column solved: the A region is free
+  tc_fence_after();
+  if (warp < 2) {
+    const int i = warp * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float prow[32];  // bf16 pairs, as raw 32-bit words
+      tmem_ld32(trow + 32 * j, prow);
+      tmem_wait_ld();
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc)
+        *reinterpret_cast<uint4 *>(pp + sw128(j * 64 + i, cc)) =
+            make_uint4(__float_as_uint(prow[4 * cc]), __float_as_uint(prow[4 * cc + 1]),
+                       __float_as_uint(prow[4 * cc + 2]), __float_as_uint(prow[4 * cc + 3]));
+    }
+  }
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
