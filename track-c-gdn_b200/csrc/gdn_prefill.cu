@@ -830,20 +830,27 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     float g, g_last, beta;
     bool valid;
   };
+  // Only predicated loads here (no use of the loaded values), so the thread
+  // does not wait for them until store_gates, a chunk later.
   auto fetch_gates = [&](int c) {
     const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
     const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
     GateRegs r;
     r.valid = tid < L;
     r.g_last = gcum_ws[(t0 + L - 1) * kHV + hv];
-    r.g = r.valid ? gcum_ws[(t0 + tid) * kHV + hv] : r.g_last;
-    r.beta = r.valid ? beta_ws[(t0 + tid) * kHV + hv] : 0.f;
+    r.g = 0.f;
+    r.beta = 0.f;
+    if (r.valid) {
+      r.g = gcum_ws[(t0 + tid) * kHV + hv];
+      r.beta = beta_ws[(t0 + tid) * kHV + hv];
+    }
     return r;
   };
   auto store_gates = [&](const GateRegs &r, int buf) {
-    Eg[buf * 64 + tid] = expf(r.g);
+    const float g = r.valid ? r.g : r.g_last;
+    Eg[buf * 64 + tid] = expf(g);
     Bs[buf * 64 + tid] = r.beta;
-    Ed[buf * 64 + tid] = r.valid ? expf(r.g_last - r.g) : 0.f;
+    Ed[buf * 64 + tid] = r.valid ? expf(r.g_last - g) : 0.f;
     if (tid == 0) Egl[buf] = expf(r.g_last);
   };
 
