@@ -337,83 +337,79 @@ constexpr int kPrepBroken = kPrepTmem + 4;
 constexpr int kPrepSmem = kPrepBroken + 12 + 1024;  // + base alignment slack
 constexpr uint32_t kPrepTmemCols = 128;
 
-// Column c of (I + A)^-1 for a strictly lower-triangular 64 x 64 fp32 A given
-// transposed (AT[col * 64 + row]), by blocked forward substitution in fp32:
-// rows in blocks of 16; the earlier blocks' contribution is a loop over
-// their x values (kept in this thread's TMEM lane at columns txs..txs+63,
-// float4 broadcast reads of AT), the 16 x 16 triangle inside the block is
-// unrolled.  The loops keep the code small enough to stay in the
-// instruction cache.  Blocks that lie wholly above this warp's first column
-// (`c_warp`) are zero and skipped.  Writes the column as bf16 into the
-// 64 x 64 tile `img` (128-byte rows, 128-byte swizzle).
-__device__ __forceinline__ void solve_unit_lower_column(const float *AT, int c, int c_warp,
+// (I + A)^-1 for a strictly lower-triangular 64 x 64 fp32 A (given transposed,
+// AT[col * 64 + row]) as a 2 x 2 block inverse of 32 x 32 blocks:
+//   [L11 0; L21 L22]^-1 = [X11 0; X21 X22],  X11 = L11^-1, X22 = L22^-1,
+//   X21 = -X22 (L21 X11).
+// Step 1 (this function): thread (h, lane) solves column c = 32 h + lane of
+// its diagonal block X_hh by blocked forward substitution in fp32 (16-row
+// blocks; block 2h's x values wait in the thread's TMEM lane at columns
+// txs + 32 h .. for block 2h+1; A's rows are broadcast from shared memory),
+// and writes them as bf16 into the 64 x 64 Ainv image `img` (128-byte rows,
+// 128-byte swizzle), with the zeros above the diagonal block for h = 1.
+// Steps 2 and 3 (the two products) run in the kernel, split over all four
+// warps.
+__device__ __forceinline__ void img_put(uint8_t *img, int r, int c, float x) {
+  *reinterpret_cast<__nv_bfloat16 *>(img + r * 128 + (((c >> 3) ^ (r & 7)) << 4) + (c & 7) * 2) =
+      __float2bfloat16_rn(x);
+}
+
+__device__ __forceinline__ void solve_diag_block_column(const float *AT, int c, int h,
                                                         uint32_t txs, uint8_t *img) {
+  if (h == 1) {
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r) img_put(img, r, c, 0.f);
+  }
 #pragma unroll 1
-  for (int blk = 0; blk < 4; ++blk) {
-    const int r0 = 16 * blk;
-    float xb[16];
-    if (r0 + 16 <= c_warp) {
+  for (int bb = 0; bb < 2; ++bb) {
+    const int r0 = 32 * h + 16 * bb;
+    float acc[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) xb[i] = 0.f;
-    } else {
-      float acc[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-      // the earlier blocks' x values, fetched from TMEM in one round trip
-      float xprev[48];
-      const int pb0 = c_warp >> 4;
-#pragma unroll
-      for (int pb = 0; pb < 3; ++pb)
-        if (pb >= pb0 && pb < blk)
-          tmem_ld16(txs + 16 * pb, *reinterpret_cast<float(*)[16]>(xprev + 16 * pb));
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+    if (bb == 1) {
+      // contribution of the block above, within the diagonal block
+      float xp[16];
+      tmem_ld16(txs + 32 * h, xp);
       tmem_wait_ld();
 #pragma unroll
-      for (int pb = 0; pb < 3; ++pb) {
-        if (pb < pb0 || pb >= blk) continue;
-        const float *xp = xprev + 16 * pb;
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const float4 *col = reinterpret_cast<const float4 *>(AT + (16 * pb + jj) * 64 + r0);
-          const float4 a0 = col[0], a1 = col[1], a2 = col[2], a3 = col[3];
-          const float xj = xp[jj];
-          acc[0] += a0.x * xj;
-          acc[1] += a0.y * xj;
-          acc[2] += a0.z * xj;
-          acc[3] += a0.w * xj;
-          acc[4] += a1.x * xj;
-          acc[5] += a1.y * xj;
-          acc[6] += a1.z * xj;
-          acc[7] += a1.w * xj;
-          acc[8] += a2.x * xj;
-          acc[9] += a2.y * xj;
-          acc[10] += a2.z * xj;
-          acc[11] += a2.w * xj;
-          acc[12] += a3.x * xj;
-          acc[13] += a3.y * xj;
-          acc[14] += a3.z * xj;
-          acc[15] += a3.w * xj;
-        }
+      for (int jj = 0; jj < 16; ++jj) {
+        const float4 *col = reinterpret_cast<const float4 *>(AT + (32 * h + jj) * 64 + r0);
+        const float4 a0 = col[0], a1 = col[1], a2 = col[2], a3 = col[3];
+        const float xj = xp[jj];
+        acc[0] += a0.x * xj;
+        acc[1] += a0.y * xj;
+        acc[2] += a0.z * xj;
+        acc[3] += a0.w * xj;
+        acc[4] += a1.x * xj;
+        acc[5] += a1.y * xj;
+        acc[6] += a1.z * xj;
+        acc[7] += a1.w * xj;
+        acc[8] += a2.x * xj;
+        acc[9] += a2.y * xj;
+        acc[10] += a2.z * xj;
+        acc[11] += a2.w * xj;
+        acc[12] += a3.x * xj;
+        acc[13] += a3.y * xj;
+        acc[14] += a3.z * xj;
+        acc[15] += a3.w * xj;
       }
+    }
+    float xb[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float s = acc[i];
+    for (int i = 0; i < 16; ++i) {
+      float s = acc[i];
 #pragma unroll
-        for (int jp = 0; jp < i; ++jp) s += AT[(r0 + jp) * 64 + r0 + i] * xb[jp];
-        const int r = r0 + i;
-        xb[i] = (r == c) ? 1.f : (r < c ? 0.f : -s);
-      }
+      for (int jp = 0; jp < i; ++jp) s += AT[(r0 + jp) * 64 + r0 + i] * xb[jp];
+      const int r = r0 + i;
+      xb[i] = (r == c) ? 1.f : (r < c ? 0.f : -s);
     }
     uint32_t u[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(xb[i]);
-    tmem_st16(txs + 16 * blk, u);
+    tmem_st16(txs + 16 * (2 * h + bb), u);
     tmem_wait_st();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int r = r0 + i;
-      *reinterpret_cast<__nv_bfloat16 *>(img + r * 128 + (((c >> 3) ^ (r & 7)) << 4) +
-                                         (c & 7) * 2) = __float2bfloat16_rn(xb[i]);
-    }
+    for (int i = 0; i < 16; ++i) img_put(img, r0 + i, c, xb[i]);
   }
 }
 
@@ -586,13 +582,83 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   __syncthreads();
   tc_fence_after();
 
-  // Forward substitution: thread (j = tid / 64, c = tid % 64) solves column c
-  // of (I + A_j)^-1; its x values live in its own TMEM lane, columns 64..127
-  // (idle until the P Ainv MMA below).
+  // (I + A_j)^-1 as a 2 x 2 block inverse (see solve_diag_block_column).
+  // Thread (j = tid / 64, h = warp & 1, lane) owns column 32 h + lane of v-head j.
   {
-    const int j = tid >> 6, c = tid & 63;
-    solve_unit_lower_column(AT + j * 4096, c, 32 * (warp & 1),
-                            tmem + (static_cast<uint32_t>(32 * warp) << 16) + 64, ai + j * 8192);
+    const int j = tid >> 6, h = warp & 1;
+    float *ATj = AT + j * 4096;
+    uint8_t *img = ai + j * 8192;
+    const uint32_t txs = tmem + (static_cast<uint32_t>(32 * warp) << 16) + 64;
+    // step 1: diagonal blocks X11 (h = 0) and X22 (h = 1), in parallel
+    solve_diag_block_column(ATj, 32 * h + lane, h, txs, img);
+    tc_fence_before();
+    __syncthreads();  // every diagonal block solved: L11 and L22 are no longer read
+    tc_fence_after();
+    // fp32 copies, row-major 32 x 32, into the retired L22 columns of A_j:
+    // X11 at ATj[32*64 ..), X22 at ATj[48*64 ..)
+    float *Xh = ATj + 32 * 64 + 1024 * h;
+    {
+      float x[32];
+      tmem_ld32(txs + 32 * h, x);
+      tmem_wait_ld();
+#pragma unroll
+      for (int k = 0; k < 32; ++k) Xh[k * 32 + lane] = x[k];
+    }
+    __syncthreads();
+    // step 2: T = L21 X11 (rows 16 h .. 16 h + 15 of column `lane`), with
+    // L21[r][k] = ATj[k * 64 + 32 + r]; T goes into the retired L11 area,
+    // row r at ATj[r * 64 + 0 .. 31]
+    {
+      const float *X11 = ATj + 32 * 64;
+      float t[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) t[i] = 0.f;
+#pragma unroll 4
+      for (int k = 0; k < 32; ++k) {
+        const float xk = X11[k * 32 + lane];
+        const float4 *l = reinterpret_cast<const float4 *>(ATj + k * 64 + 32 + 16 * h);
+        const float4 a0 = l[0], a1 = l[1], a2 = l[2], a3 = l[3];
+        t[0] += a0.x * xk;
+        t[1] += a0.y * xk;
+        t[2] += a0.z * xk;
+        t[3] += a0.w * xk;
+        t[4] += a1.x * xk;
+        t[5] += a1.y * xk;
+        t[6] += a1.z * xk;
+        t[7] += a1.w * xk;
+        t[8] += a2.x * xk;
+        t[9] += a2.y * xk;
+        t[10] += a2.z * xk;
+        t[11] += a2.w * xk;
+        t[12] += a3.x * xk;
+        t[13] += a3.y * xk;
+        t[14] += a3.z * xk;
+        t[15] += a3.w * xk;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) ATj[(16 * h + i) * 64 + lane] = t[i];
+    }
+    __syncthreads();
+    // step 3: X21 = -X22 T (rows 16 h .. 16 h + 15 of column `lane`) -> image
+    // rows 32 .. 63, columns 0 .. 31
+    {
+      const float *X22 = ATj + 48 * 64;
+      float tc[32];
+#pragma unroll
+      for (int k = 0; k < 32; ++k) tc[k] = ATj[k * 64 + lane];
+#pragma unroll 2
+      for (int i = 0; i < 16; ++i) {
+        const int r = 16 * h + i;
+        const float4 *xr = reinterpret_cast<const float4 *>(X22 + r * 32);
+        float s = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 a = xr[q];
+          s += a.x * tc[4 * q] + a.y * tc[4 * q + 1] + a.z * tc[4 * q + 2] + a.w * tc[4 * q + 3];
+        }
+        img_put(img, 32 + r, lane, -s);
+      }
+    }
   }
 
   tc_fence_before();
