@@ -394,14 +394,24 @@ __device__ __forceinline__ void solve_diag_block_column(const float *AT, int c, 
         acc[15] += a3.w * xj;
       }
     }
+    // inside the 16-row block, right-looking: x_jp is final once the rows
+    // above have been applied; column jp of A (float4 reads down the column)
+    // then updates the rows below it, so the dependent chain is one FMA per
+    // row rather than a dot product per row
     float xb[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float s = acc[i];
+    for (int jp = 0; jp < 16; ++jp) {
+      const int r = r0 + jp;
+      xb[jp] = (r == c) ? 1.f : (r < c ? 0.f : -acc[jp]);
+      const float *colp = AT + (r0 + jp) * 64 + r0;
 #pragma unroll
-      for (int jp = 0; jp < i; ++jp) s += AT[(r0 + jp) * 64 + r0 + i] * xb[jp];
-      const int r = r0 + i;
-      xb[i] = (r == c) ? 1.f : (r < c ? 0.f : -s);
+      for (int q = (jp + 1) / 4; q < 4; ++q) {
+        const float4 a = *reinterpret_cast<const float4 *>(colp + 4 * q);
+        if (4 * q + 0 > jp) acc[4 * q + 0] += a.x * xb[jp];
+        if (4 * q + 1 > jp) acc[4 * q + 1] += a.y * xb[jp];
+        if (4 * q + 2 > jp) acc[4 * q + 2] += a.z * xb[jp];
+        if (4 * q + 3 > jp) acc[4 * q + 3] += a.w * xb[jp];
+      }
     }
     uint32_t u[16];
 #pragma unroll
