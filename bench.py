@@ -302,14 +302,27 @@ def gpu_arm(args):
 
     ev = {k: [] for k in ("s", "d", "p", "g")}
 
+    # decode and prefill are independent: with overlap on, decode runs on a
+    # side stream next to the prefill (its CTAs fill SMs the prefill leaves
+    # idle) and the step joins both before the gather
+    overlap = args.overlap == "on" and dec is not None and pre is not None and pre["N"] > 0
+    side = torch.cuda.Stream(dev) if overlap else stream
+    ev["dside"] = []
+
+    def decode():
+        with torch.cuda.stream(side):
+            gdn.decode.decode_into(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
+                                   dt_bias, dec["b"], None, dec_out, dec["state"])
+
     def step(record):
         if record:
             e = torch.cuda.Event(enable_timing=True)
             e.record(stream)
             ev["s"].append(e)
-        if dec is not None:
-            gdn.decode.decode_into(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
-                                   dt_bias, dec["b"], None, dec_out, dec["state"])
+        if overlap:
+            side.wait_stream(stream)
+        if dec is not None and not overlap:
+            decode()
         if record:
             e = torch.cuda.Event(enable_timing=True)
             e.record(stream)
@@ -318,6 +331,15 @@ def gpu_arm(args):
             gdn.prefill.prefill_into(pre["q"], pre["k"], pre["v"], pre["h0"], A_log, pre["a"],
                                      dt_bias, pre["b"], pre["cu"], None, pre["out"],
                                      pre["final"], pre["ws"])
+        if overlap:
+            # issued after the prefill, so its CTAs take the SMs the prefill's
+            # kernels leave free (their tails and the gaps between them)
+            decode()
+            if record:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record(side)
+                ev["dside"].append(e)
+            stream.wait_stream(side)
         if record:
             e = torch.cuda.Event(enable_timing=True)
             e.record(stream)
@@ -362,8 +384,10 @@ def gpu_arm(args):
     clocks = merge_clocks(dist, world, sampler.stop())
     elapsed_ms = max_over_ranks(t0.elapsed_time(t1))
     ms_step = elapsed_ms / args.steps
-    d_ms = np.mean([a.elapsed_time(b) for a, b in zip(ev["s"], ev["d"])])
-    p_ms = np.mean([a.elapsed_time(b) for a, b in zip(ev["d"], ev["p"])])
+    # with overlap the decode runs beside the prefill: its phase is from the
+    # step start to its own end, and the prefill's from the step start
+    d_ms = np.mean([a.elapsed_time(b) for a, b in zip(ev["s"], ev["dside" if overlap else "d"])])
+    p_ms = np.mean([a.elapsed_time(b) for a, b in zip(ev["s" if overlap else "d"], ev["p"])])
     g_ms = np.mean([a.elapsed_time(b) for a, b in zip(ev["p"], ev["g"])])
     d_ms_max, p_ms_max, g_ms_max = (max_over_ranks(float(x)) for x in (d_ms, p_ms, g_ms))
     status = gdn._native.read_device_status()
@@ -391,6 +415,8 @@ def gpu_arm(args):
             "prefill_tokens": total_prefill_tokens,
             "l2": "inputs larger than L2 (no flush needed)" if total_tokens > 20000 else
                   "inputs smaller than L2 (no flush)",
+            "streams": ("decode on a side stream next to the prefill, joined each step" if overlap
+                        else "one stream (decode, then prefill)"),
             "parallelism": f"shard{world}: decode request blocks, prefill LPT by sequence; "
                            + ("NCCL gather of decode outputs + prefill final states to rank 0"
                               if world > 1 else "no collective"),
@@ -827,6 +853,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="device step only (profiling runs)")
+    ap.add_argument("--overlap", choices=["on", "off"], default="off",
+                    help="run decode on a side stream next to the prefill (C4)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3  # timing rule: at least three warm-up steps
