@@ -39,6 +39,20 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# The JSON line goes out on the original stdout; everything else that writes
+# to file descriptor 1 (library banners such as NCCL's version line) is sent
+# to stderr once main() has run, so stdout carries exactly one JSON line.
+_JSON_FD = None
+
+
+def emit(obj) -> None:
+    line = (json.dumps(obj) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(line.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, line)
+
 HQK, HV, D = 4, 8, 128
 DECODE_STATE_BYTES = HV * D * D * 4 * 2           # fp32 state read + written per request
 DECODE_VEC_BYTES = 2 * HQK * D * 2 + 2 * HV * D * 2 + 2 * HV * 2  # q,k,v,out,a,b
@@ -461,7 +475,7 @@ def gpu_arm(args):
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(result)
 
 
 def e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world, max_over_ranks, barrier,
@@ -690,7 +704,7 @@ def reference_arm(args):
     step_s = timer.full_step_seconds()
     value = timer.total_tokens() / step_s
     wl = WORKLOADS[args.workload]
-    print(json.dumps({
+    emit({
         "impl": "reference",
         "metric": "GDN serving throughput (decode + prefill tokens/s, max-over-ranks device time)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -705,7 +719,7 @@ def reference_arm(args):
                 "d2h_bytes_per_step": 0},
         "note": "the reference's path is Python/Triton (GPU only); its CPU implementation "
                 "is the oracle's C restatement of the same recurrence (OpenMP, all host threads)",
-    }), flush=True)
+    })
 
 
 TRITON_REF_DIR = ROOT / "baseline" / "_ref"
@@ -738,8 +752,8 @@ def triton_arm(args):
     dec_mod = _load_triton_ref("gdn_decode_qk4_v8_d128_k_last") if wl["decode_batch"] else None
     pre_mod = _load_triton_ref("gdn_prefill_qk4_v8_d128_k_last") if wl["prefill"] else None
     if (wl["decode_batch"] and dec_mod is None) or (wl["prefill"] and pre_mod is None):
-        print(json.dumps({"impl": "triton-reference",
-                          "unavailable": f"reference Triton solutions not staged under {TRITON_REF_DIR}"}))
+        emit({"impl": "triton-reference",
+              "unavailable": f"reference Triton solutions not staged under {TRITON_REF_DIR}"})
         return
     import torch
     dev = torch.device("cuda", 0)
@@ -837,10 +851,14 @@ def triton_arm(args):
         result["decode"] = {"us_per_step": d_ms * 1e3,
                             "state_gbs": dec["B"] * (DECODE_STATE_BYTES + DECODE_VEC_BYTES)
                             / (d_ms / 1e3) / 1e9}
-    print(json.dumps(result), flush=True)
+    emit(result)
 
 
 def main():
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
