@@ -10,7 +10,7 @@ bin packing by sequence), so scaling is "strong".  All inputs are seeded
 synthetic tensors with the BASELINE value distributions.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference|triton]
-                    [--workload c4|c2|c3|decode]
+                    [--workload c4|c2|c3|decode|mtp]
 
 Prints one JSON line (rank 0).  `value` is whole-job tokens/s (decode tokens
 + prefill tokens) over the device time of K steps (max over ranks);
@@ -70,6 +70,9 @@ WORKLOADS = {
                decode_batch=0, prefill="c3"),
     "decode": dict(desc="C1 decode sweep point: batch 1024, state updated in place",
                    decode_batch=1024, prefill=None),
+    "mtp": dict(desc="multi-token decode (speculative verify): batch 1024 x 4 tokens per request, "
+                     "state updated in place",
+                decode_batch=1024, decode_tokens=4, prefill=None),
 }
 
 
@@ -248,17 +251,27 @@ def make_prefill_inputs(torch, lengths, with_state, seed, dev):
     return dict(q=q, k=k, v=v, a=a, b=b, h0=h0, cu=torch.from_numpy(cu).to(dev), T=T, N=N)
 
 
-def make_decode_inputs(torch, B, seed, dev):
+def make_decode_inputs(torch, B, seed, dev, T=1):
     import torch.nn.functional as F
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
-    q = F.normalize(torch.randn(B, 1, HQK, D, generator=g, device=dev), dim=-1).bfloat16()
-    k = F.normalize(torch.randn(B, 1, HQK, D, generator=g, device=dev), dim=-1).bfloat16()
-    v = torch.randn(B, 1, HV, D, generator=g, device=dev).bfloat16()
-    a = torch.randn(B, 1, HV, generator=g, device=dev).bfloat16()
-    b = torch.randn(B, 1, HV, generator=g, device=dev).bfloat16()
+    q = F.normalize(torch.randn(B, T, HQK, D, generator=g, device=dev), dim=-1).bfloat16()
+    k = F.normalize(torch.randn(B, T, HQK, D, generator=g, device=dev), dim=-1).bfloat16()
+    v = torch.randn(B, T, HV, D, generator=g, device=dev).bfloat16()
+    a = torch.randn(B, T, HV, generator=g, device=dev).bfloat16()
+    b = torch.randn(B, T, HV, generator=g, device=dev).bfloat16()
     state = torch.randn(B, HV, D, D, generator=g, device=dev) * 0.02
-    return dict(q=q, k=k, v=v, a=a, b=b, state=state, B=B)
+    return dict(q=q, k=k, v=v, a=a, b=b, state=state, B=B, T=T)
+
+
+def run_decode(gdn, dec, A_log, dt_bias, out):
+    """One decode step of the workload (multi-token when T > 1), state in place."""
+    if dec["T"] == 1:
+        gdn.decode.decode_into(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
+                               dt_bias, dec["b"], None, out, dec["state"])
+    else:
+        gdn.decode.decode_mtp_into(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
+                                   dt_bias, dec["b"], None, out, dec["state"])
 
 
 def gpu_arm(args):
@@ -294,7 +307,8 @@ def gpu_arm(args):
     B_total = wl["decode_batch"]
     dec_slice = shard.block_partition(B_total, world, rank)
     B = dec_slice.stop - dec_slice.start
-    dec = make_decode_inputs(torch, B, 100 + rank, dev) if B > 0 else None
+    Tdec = wl.get("decode_tokens", 1)
+    dec = make_decode_inputs(torch, B, 100 + rank, dev, Tdec) if B > 0 else None
     pre = None
     total_prefill_tokens = 0
     seq_counts = [0] * world
@@ -308,10 +322,10 @@ def gpu_arm(args):
         pre["out"] = torch.empty(pre["T"], HV, D, dtype=torch.bfloat16, device=dev)
         pre["final"] = torch.empty(pre["N"], HV, D, D, dtype=torch.float32, device=dev)
         pre["ws"] = gdn.prefill.alloc_workspace(pre["T"], pre["N"], dev)
-    dec_out = torch.empty(B, 1, HV, D, dtype=torch.bfloat16, device=dev) if B > 0 else None
+    dec_out = torch.empty(B, Tdec, HV, D, dtype=torch.bfloat16, device=dev) if B > 0 else None
     max_seqs = max(seq_counts) if seq_counts else 0
     max_dec = math.ceil(B_total / world) if B_total else 0
-    total_tokens = B_total + total_prefill_tokens
+    total_tokens = B_total * Tdec + total_prefill_tokens
     stream = torch.cuda.current_stream(dev)
 
     ev = {k: [] for k in ("s", "d", "p", "g")}
@@ -325,8 +339,7 @@ def gpu_arm(args):
 
     def decode():
         with torch.cuda.stream(side):
-            gdn.decode.decode_into(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
-                                   dt_bias, dec["b"], None, dec_out, dec["state"])
+            run_decode(gdn, dec, A_log, dt_bias, dec_out)
 
     def step(record):
         if record:
@@ -360,7 +373,7 @@ def gpu_arm(args):
             ev["p"].append(e)
         if world > 1:
             if dec_out is not None or max_dec:
-                t = dec_out if dec_out is not None else torch.empty(0, 1, HV, D, dtype=torch.bfloat16, device=dev)
+                t = dec_out if dec_out is not None else torch.empty(0, Tdec, HV, D, dtype=torch.bfloat16, device=dev)
                 shard.gather_padded(t, max_dec)
             if max_seqs:
                 t = pre["final"] if pre is not None else torch.empty(0, HV, D, D, device=dev)
@@ -425,6 +438,7 @@ def gpu_arm(args):
         "config": {
             "workload": wl["desc"],
             "decode_batch": B_total,
+            "decode_tokens_per_request": Tdec,
             "prefill_sequences": int(sum(seq_counts)) if wl["prefill"] else 0,
             "prefill_tokens": total_prefill_tokens,
             "l2": "inputs larger than L2 (no flush needed)" if total_tokens > 20000 else
@@ -441,7 +455,7 @@ def gpu_arm(args):
         "clocks": clocks,
     }
     if dec is not None:
-        gbs = B * (DECODE_STATE_BYTES + DECODE_VEC_BYTES) / (d_ms / 1e3) / 1e9
+        gbs = B * (DECODE_STATE_BYTES + Tdec * DECODE_VEC_BYTES) / (d_ms / 1e3) / 1e9
         result["decode"] = {"us_per_step": d_ms_max * 1e3, "state_gbs_rank0": gbs,
                             "batch_per_rank": B}
         result["roofline_decode"] = {
@@ -505,9 +519,11 @@ def e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world, max_over_ran
         for sl in range(2):
             for key in dec_keys:
                 dev_in[sl]["d" + key] = torch.empty_like(dec[key])
-            dev_out[sl]["dout"] = torch.empty(dec["B"], 1, HV, D, dtype=torch.bfloat16, device=dev)
-            host_out[sl]["dout"] = torch.empty(dec["B"], 1, HV, D, dtype=torch.bfloat16).pin_memory()
-        d2h += dec["B"] * HV * D * 2
+            dev_out[sl]["dout"] = torch.empty(dec["B"], dec["T"], HV, D, dtype=torch.bfloat16,
+                                              device=dev)
+            host_out[sl]["dout"] = torch.empty(dec["B"], dec["T"], HV, D,
+                                               dtype=torch.bfloat16).pin_memory()
+        d2h += dec["B"] * dec["T"] * HV * D * 2
     if pre is not None and pre["N"] > 0:
         for key in pre_keys:
             host_in["p" + key] = pre[key].cpu().pin_memory()
@@ -525,8 +541,8 @@ def e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world, max_over_ran
     def compute(sl):
         t = dev_in[sl]
         if dec is not None:
-            gdn.decode.decode_into(t["dq"], t["dk"], t["dv"], dec["state"], A_log, t["da"], dt_bias,
-                                   t["db"], None, dev_out[sl]["dout"], dec["state"])
+            d = dict(dec, q=t["dq"], k=t["dk"], v=t["dv"], a=t["da"], b=t["db"])
+            run_decode(gdn, d, A_log, dt_bias, dev_out[sl]["dout"])
         if pre is not None and pre["N"] > 0:
             gdn.prefill.prefill_into(t["pq"], t["pk"], t["pv"], t.get("ph0"), A_log, t["pa"],
                                      dt_bias, t["pb"], t["pcu"], None, dev_out[sl]["pout"],
@@ -595,14 +611,14 @@ def _bf16_bits(x: np.ndarray) -> np.ndarray:
     return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
 
 
-def _cpu_decode_inputs(rng, B):
+def _cpu_decode_inputs(rng, B, T=1):
     def nrm(s):
         x = rng.standard_normal(s, dtype=np.float32)
         return x / np.linalg.norm(x, axis=-1, keepdims=True)
-    return dict(q=_bf16_bits(nrm((B, 1, HQK, D))), k=_bf16_bits(nrm((B, 1, HQK, D))),
-                v=_bf16_bits(rng.standard_normal((B, 1, HV, D), dtype=np.float32)),
-                a=_bf16_bits(rng.standard_normal((B, 1, HV), dtype=np.float32)),
-                b=_bf16_bits(rng.standard_normal((B, 1, HV), dtype=np.float32)),
+    return dict(q=_bf16_bits(nrm((B, T, HQK, D))), k=_bf16_bits(nrm((B, T, HQK, D))),
+                v=_bf16_bits(rng.standard_normal((B, T, HV, D), dtype=np.float32)),
+                a=_bf16_bits(rng.standard_normal((B, T, HV), dtype=np.float32)),
+                b=_bf16_bits(rng.standard_normal((B, T, HV), dtype=np.float32)),
                 state=(rng.standard_normal((B, HV, D, D), dtype=np.float32) * 0.02))
 
 
@@ -638,13 +654,15 @@ class CpuOracleTimer:
         self.dec_s = self.dec_n = self.pre_s = self.pre_n = 0.0
         self.next_seq = 0
         self.dec_sample = 64
+        self.dec_T = self.wl.get("decode_tokens", 1)
 
     def sample(self):
         if self.wl["decode_batch"]:
-            inp = _cpu_decode_inputs(self.rng, self.dec_sample)
+            inp = _cpu_decode_inputs(self.rng, self.dec_sample, self.dec_T)
             t = time.perf_counter()
-            self.oracle.decode(inp["q"], inp["k"], inp["v"], inp["state"], self.A_log, inp["a"],
-                               self.dt, inp["b"], nthreads=self.threads)
+            fn = self.oracle.decode if self.dec_T == 1 else self.oracle.decode_mtp
+            fn(inp["q"], inp["k"], inp["v"], inp["state"], self.A_log, inp["a"], self.dt, inp["b"],
+               nthreads=self.threads)
             self.dec_s += time.perf_counter() - t
             self.dec_n += self.dec_sample
         if self.lengths is not None:
@@ -666,12 +684,13 @@ class CpuOracleTimer:
         return t
 
     def total_tokens(self):
-        return self.wl["decode_batch"] + (int(self.lengths.sum()) if self.lengths is not None else 0)
+        return (self.wl["decode_batch"] * self.dec_T
+                + (int(self.lengths.sum()) if self.lengths is not None else 0))
 
     def describe(self):
         parts = []
         if self.dec_n:
-            parts.append(f"decode of {int(self.dec_n)} requests")
+            parts.append(f"decode of {int(self.dec_n)} requests x {self.dec_T} token(s)")
         if self.pre_n:
             parts.append(f"prefill of {int(self.pre_n)} tokens ({self.next_seq} sequences drawn "
                          f"from the workload's length list)")
@@ -762,7 +781,8 @@ def triton_arm(args):
     g.manual_seed(1234)  # the b200 arm's rank-0 seeds, so both arms see the same inputs
     A_log = (torch.rand(HV, generator=g, device=dev) * 2.7).float()
     dt_bias = (torch.randn(HV, generator=g, device=dev) * 0.1).float()
-    dec = make_decode_inputs(torch, wl["decode_batch"], 100, dev) if wl["decode_batch"] else None
+    Tdec = wl.get("decode_tokens", 1)
+    dec = make_decode_inputs(torch, wl["decode_batch"], 100, dev, Tdec) if wl["decode_batch"] else None
     pre = None
     if wl["prefill"]:
         lengths = prefill_lengths(wl["prefill"])
@@ -776,8 +796,16 @@ def triton_arm(args):
             ev["s"].append(torch.cuda.Event(enable_timing=True))
             ev["s"][-1].record(stream)
         if dec is not None:
-            keep["dec"] = dec_mod.run(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
-                                      dt_bias, dec["b"], None)
+            # the reference decode takes one token per request: T calls, state chained
+            cur, outs = dec["state"], []
+            for t in range(Tdec):
+                sl = slice(t, t + 1)
+                o_t, cur = dec_mod.run(dec["q"][:, sl].contiguous(), dec["k"][:, sl].contiguous(),
+                                       dec["v"][:, sl].contiguous(), cur, A_log,
+                                       dec["a"][:, sl].contiguous(), dt_bias,
+                                       dec["b"][:, sl].contiguous(), None)
+                outs.append(o_t)
+            keep["dec"] = (torch.cat(outs, 1), cur)
         if record:
             ev["d"].append(torch.cuda.Event(enable_timing=True))
             ev["d"][-1].record(stream)
@@ -803,7 +831,7 @@ def triton_arm(args):
     ms = t0.elapsed_time(t1) / args.steps
     d_ms = float(np.mean([a.elapsed_time(b) for a, b in zip(ev["s"], ev["d"])]))
     p_ms = float(np.mean([a.elapsed_time(b) for a, b in zip(ev["d"], ev["p"])]))
-    total = wl["decode_batch"] + (pre["T"] if pre else 0)
+    total = wl["decode_batch"] * Tdec + (pre["T"] if pre else 0)
 
     # our kernels on the same inputs (the reference decode left dec["state"] untouched)
     gdn = importlib.import_module("track-c-gdn_b200")
@@ -814,8 +842,9 @@ def triton_arm(args):
 
     parity = {}
     if dec is not None:
-        o, s = gdn.decode.run(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
-                              dt_bias, dec["b"], None)
+        fn = gdn.decode.run if Tdec == 1 else gdn.decode.run_mtp
+        o, s = fn(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"], dt_bias, dec["b"],
+                  None)
         parity["decode_out_rel_fro"] = rel(o, keep["dec"][0])
         parity["decode_state_rel_fro"] = rel(s, keep["dec"][1])
     if pre is not None:
@@ -849,7 +878,7 @@ def triton_arm(args):
                              "tflops": pre["T"] * PREFILL_FLOP_PER_TOKEN / (p_ms / 1e3) / 1e12}
     if dec is not None:
         result["decode"] = {"us_per_step": d_ms * 1e3,
-                            "state_gbs": dec["B"] * (DECODE_STATE_BYTES + DECODE_VEC_BYTES)
+                            "state_gbs": dec["B"] * (DECODE_STATE_BYTES + Tdec * DECODE_VEC_BYTES)
                             / (d_ms / 1e3) / 1e9}
     emit(result)
 

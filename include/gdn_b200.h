@@ -76,6 +76,32 @@ int gdn_decode_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
                                   void *out, float *new_state, void *stream);
 
 /*
+ * Multi-token decode (speculative verify / multi-token prediction): T tokens
+ * per request, applied in order -- the same result as T calls of
+ * gdn_decode_qk4_v8_d128_k_last (bit for bit), with each head's 64 KiB state
+ * streamed through HBM once instead of T times.  No counterpart in the
+ * reference (its decode definition takes one token per request).
+ * q, k      [B,T,4,128] bf16 (8-byte aligned)
+ * v         [B,T,8,128] bf16 (8-byte aligned)
+ * state     [B,8,128,128] fp32 (16-byte aligned) or NULL for a zero state
+ * a, b      [B,T,8] bf16;  A_log, dt_bias [8] fp32;  scale 0.0f -> 1/sqrt(128)
+ * out       [B,T,8,128] bf16 (8-byte aligned)
+ * new_state [B,8,128,128] fp32, the state after the last token; may equal
+ *           `state`
+ * intermediate_states  NULL, or [B,T,8,128,128] fp32 (16-byte aligned,
+ *           overlapping neither state buffer): the state after each token,
+ *           for rolling back rejected speculative tokens
+ * 1 <= T <= GDN_DECODE_MTP_MAX_TOKENS.
+ */
+#define GDN_DECODE_MTP_MAX_TOKENS 64
+int gdn_decode_mtp_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                      const float *state, const float *A_log,
+                                      const void *a, const float *dt_bias,
+                                      const void *b, float scale, int64_t batch,
+                                      int64_t num_tokens, void *out, float *new_state,
+                                      float *intermediate_states, void *stream);
+
+/*
  * Workspace (bytes) the prefill needs for `total_tokens` tokens packed into
  * `num_seqs` sequences.  Independent of the sequence lengths.
  */

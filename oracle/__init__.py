@@ -99,6 +99,29 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale=None, nthreads=None):
     return out, new_state
 
 
+def decode_mtp(q, k, v, state, A_log, a, dt_bias, b, scale=None, nthreads=None):
+    """T decode steps per request, applied in order (the reference decode step,
+    gdn_decode_qk4_v8_d128_k_last/solution/triton/kernel.py:26-79, once per
+    token).  q,k: [B,T,4,128] u16; v: [B,T,8,128] u16; a,b: [B,T,8] u16;
+    state [B,8,128,128] f32 or None.  Returns (out [B,T,8,128] f32,
+    final state [B,8,128,128] f32, states after each token [B,T,8,128,128] f32)."""
+    q, k, v, a, b = map(_u16, (q, k, v, a, b))
+    B, T = q.shape[0], q.shape[1]
+    st = None if state is None else _f32(state)
+    outs, states = [], []
+    for t in range(T):
+        o, st = decode(q[:, t:t + 1], k[:, t:t + 1], v[:, t:t + 1], st, A_log,
+                       a.reshape(B, T, HV)[:, t:t + 1], dt_bias, b.reshape(B, T, HV)[:, t:t + 1],
+                       scale, nthreads)
+        outs.append(o[:, 0])
+        states.append(st)
+    if T == 0:
+        return (np.zeros((B, 0, HV, D), np.float32),
+                np.zeros((B, HV, D, D), np.float32) if st is None else st,
+                np.zeros((B, 0, HV, D, D), np.float32))
+    return np.stack(outs, 1), st, np.stack(states, 1)
+
+
 def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, nthreads=None):
     """Prefill recurrence.  q,k: [T,4,128] u16; v: [T,8,128] u16;
     state: [N,8,128,128] f32 or None; a,b: [T,8] u16; cu_seqlens int64 [N+1].

@@ -51,6 +51,25 @@ def decode_inputs(seed: int, B: int, with_state: bool = True, gate_scale: float 
     return inp
 
 
+def decode_mtp_inputs(seed: int, B: int, T: int, with_state: bool = True,
+                      gate_scale: float = 1.0):
+    """Multi-token decode inputs: the decode distributions with T tokens per
+    request (q, k [B,T,4,128], v [B,T,8,128], a, b [B,T,8])."""
+    rng = np.random.default_rng(seed)
+    inp = {
+        "q": to_bf16_bits(_normed(rng, (B, T, HQK, D))),
+        "k": to_bf16_bits(_normed(rng, (B, T, HQK, D))),
+        "v": to_bf16_bits(rng.standard_normal((B, T, HV, D), dtype=np.float32)),
+        "A_log": (rng.random(HV, dtype=np.float32) * 2.7).astype(np.float32),
+        "a": to_bf16_bits(rng.standard_normal((B, T, HV), dtype=np.float32) * gate_scale),
+        "dt_bias": (rng.standard_normal(HV, dtype=np.float32) * 0.1).astype(np.float32),
+        "b": to_bf16_bits(rng.standard_normal((B, T, HV), dtype=np.float32) * gate_scale),
+    }
+    st = (rng.standard_normal((B, HV, D, D), dtype=np.float32) * 0.02).astype(np.float32)
+    inp["state"] = st if with_state else None
+    return inp
+
+
 def prefill_inputs(seed: int, lens, with_state: bool = True, gate_scale: float = 1.0):
     rng = np.random.default_rng(seed)
     T = int(sum(lens))

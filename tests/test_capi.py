@@ -20,6 +20,7 @@ def header_functions():
 def test_header_declares_expected_entry_points():
     names = header_functions()
     for n in ("gdn_decode_qk4_v8_d128_k_last", "gdn_prefill_qk4_v8_d128_k_last",
+              "gdn_decode_mtp_qk4_v8_d128_k_last", "gdn_prefill_kernel_launches",
               "gdn_prefill_workspace_bytes", "gdn_b200_status_string",
               "gdn_b200_abi_version", "gdn_b200_read_device_status"):
         assert n in names
@@ -87,6 +88,27 @@ def test_argument_validation_without_device(gdn):
     bad[8] = None
     assert lib.gdn_prefill_qk4_v8_d128_k_last(*bad, ok, 1 << 30, None) == 1
     assert lib.gdn_prefill_qk4_v8_d128_k_last(*args[:9], -1, 128, *args[11:], ok, 1 << 30, None) == 2
+
+
+def test_mtp_decode_argument_validation_without_device(gdn):
+    lib = gdn._native.lib
+    P = ctypes.c_void_p
+    ok = P(0x10000)
+    f = lib.gdn_decode_mtp_qk4_v8_d128_k_last
+    base = [ok, ok, ok, None, ok, ok, ok, ok, 0.0]
+    # token count outside 1..64, negative batch
+    assert f(*base, 4, 0, ok, ok, None, None) == 2
+    assert f(*base, 4, 65, ok, ok, None, None) == 2
+    assert f(*base, -1, 2, ok, ok, None, None) == 2
+    assert f(*base, 0, 2, ok, ok, None, None) == 0
+    # NULL output, misaligned intermediate states
+    assert f(*base, 4, 2, None, ok, None, None) == 1
+    assert f(*base, 4, 2, ok, ok, P(0x20008), None) == 3
+    # intermediate states overlapping the state, or the new state
+    st = P(0x1000000)
+    assert f(ok, ok, ok, st, ok, ok, ok, ok, 0.0, 4, 2, ok, P(0x9000000),
+             P(0x1000000 + 1024), None) == 7
+    assert f(*base, 4, 2, ok, P(0x9000000), P(0x9000000 + 4096), None) == 7
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")

@@ -12,6 +12,7 @@ Triton solutions (make_golden.py).  Three restatements are checked:
 import numpy as np
 import pytest
 
+import cases
 import golden_io
 import oracle
 from cases import bits_to_f32
@@ -78,3 +79,30 @@ def test_chunked_equals_recurrence_in_exact_arithmetic():
                                     inp["cu_seqlens"])
     assert np.abs(o1 - o2).max() < 2e-3
     assert np.linalg.norm(s1 - s2) / np.linalg.norm(s1) < 1e-2
+
+
+def test_oracle_multi_token_decode_is_repeated_single_steps():
+    """decode_mtp (T steps per request) equals T single decode calls fed each
+    other's states, and its T = 1 case equals decode."""
+    inp = cases.decode_inputs(seed=11, B=3, with_state=True)
+    rng = np.random.default_rng(12)
+    T = 3
+    q = np.repeat(inp["q"], T, axis=1)
+    k = np.repeat(inp["k"], T, axis=1)
+    v = np.repeat(inp["v"], T, axis=1)
+    a = rng.integers(0x3e00, 0x3f80, size=(3, T, 8)).astype(np.uint16)
+    b = rng.integers(0x3e00, 0x3f80, size=(3, T, 8)).astype(np.uint16)
+    out, fin, states = oracle.decode_mtp(q, k, v, inp["state"], inp["A_log"], a, inp["dt_bias"], b)
+    st = inp["state"]
+    for t in range(T):
+        o, st = oracle.decode(q[:, t:t + 1], k[:, t:t + 1], v[:, t:t + 1], st, inp["A_log"],
+                              a[:, t:t + 1], inp["dt_bias"], b[:, t:t + 1])
+        np.testing.assert_array_equal(out[:, t], o[:, 0])
+        np.testing.assert_array_equal(states[:, t], st)
+    np.testing.assert_array_equal(fin, st)
+    o1, s1, _ = oracle.decode_mtp(inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"],
+                                  inp["a"], inp["dt_bias"], inp["b"])
+    o0, s0 = oracle.decode(inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"],
+                           inp["dt_bias"], inp["b"])
+    np.testing.assert_array_equal(o1[:, 0], o0[:, 0])
+    np.testing.assert_array_equal(s1, s0)

@@ -70,6 +70,29 @@ def test_decode_matches_reference_triton(gdn, B):
     assert _rel(s, rs) <= 1e-6
 
 
+@pytest.mark.parametrize("B,T", [(8, 4), (256, 2)])
+def test_mtp_decode_matches_reference_triton_steps(gdn, B, T):
+    """Multi-token decode against the reference decode applied token by token."""
+    ref = _load("gdn_decode_qk4_v8_d128_k_last")
+    dev = torch.device("cuda")
+    A_log, dt_bias, g = _gates(dev, 1000 + B)
+    q = F.normalize(torch.randn(B, T, 4, 128, generator=g, device=dev), dim=-1).bfloat16()
+    k = F.normalize(torch.randn(B, T, 4, 128, generator=g, device=dev), dim=-1).bfloat16()
+    v = torch.randn(B, T, 8, 128, generator=g, device=dev).bfloat16()
+    a = torch.randn(B, T, 8, generator=g, device=dev).bfloat16()
+    b = torch.randn(B, T, 8, generator=g, device=dev).bfloat16()
+    state = torch.randn(B, 8, 128, 128, generator=g, device=dev) * 0.02
+    o, s = gdn.decode.run_mtp(q, k, v, state, A_log, a, dt_bias, b, None)
+    cur = state
+    for t in range(T):
+        sl = slice(t, t + 1)
+        ro, cur = ref.run(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), cur,
+                          A_log, a[:, sl].contiguous(), dt_bias, b[:, sl].contiguous(), None)
+        assert _rel(o[:, t], ro[:, 0]) <= 1e-3
+    torch.cuda.synchronize()
+    assert _rel(s, cur) <= 1e-6
+
+
 @pytest.mark.parametrize("lengths,with_state", [
     ([4096], False),                                                     # config 2
     (np.random.default_rng(3).integers(17, 3001, size=32).tolist(), True),   # config 3

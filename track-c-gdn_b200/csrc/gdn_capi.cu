@@ -18,6 +18,10 @@ cudaError_t launch_decode(const void *q, const void *k, const void *v, const flo
                           const float *A_log, const void *a, const float *dt_bias,
                           const void *b, float scale, int64_t batch, void *out,
                           float *new_state, cudaStream_t stream);
+cudaError_t launch_decode_mtp(const void *q, const void *k, const void *v, const float *state,
+                              const float *A_log, const void *a, const float *dt_bias,
+                              const void *b, float scale, int64_t batch, int num_tokens,
+                              void *out, float *new_state, float *inter, cudaStream_t stream);
 size_t prefill_workspace_bytes(int64_t T, int64_t N, bool allow_segments);
 int prefill_kernel_launches(int64_t T, int64_t N, bool allow_segments);
 cudaError_t launch_prefill(const void *q, const void *k, const void *v, const float *state,
@@ -110,6 +114,39 @@ int gdn_decode_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
   if (scale == 0.0f) scale = kDefaultScale;
   cudaError_t err = gdn::launch_decode(q, k, v, state, A_log, a, dt_bias, b, scale, batch, out,
                                        new_state, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+int gdn_decode_mtp_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                      const float *state, const float *A_log, const void *a,
+                                      const float *dt_bias, const void *b, float scale,
+                                      int64_t batch, int64_t num_tokens, void *out,
+                                      float *new_state, float *intermediate_states, void *stream) {
+  if (batch < 0 || num_tokens < 1 || num_tokens > GDN_DECODE_MTP_MAX_TOKENS ||
+      batch > (int64_t{1} << 26) / num_tokens)
+    return GDN_ERR_BAD_SIZE;
+  if (batch == 0) return GDN_OK;
+  if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !out || !new_state)
+    return GDN_ERR_NULL_POINTER;
+  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(v, 8) || !aligned(out, 8) ||
+      !aligned(new_state, 16) || (state && !aligned(state, 16)) ||
+      (intermediate_states && !aligned(intermediate_states, 16)) || !aligned(a, 2) ||
+      !aligned(b, 2) || !aligned(A_log, 4) || !aligned(dt_bias, 4))
+    return GDN_ERR_MISALIGNED;
+  const size_t state_bytes = static_cast<size_t>(batch) * gdn::kHV * gdn::kD * gdn::kD * 4;
+  if (state && state != new_state && overlap(state, state_bytes, new_state, state_bytes))
+    return GDN_ERR_ALIASING;
+  if (intermediate_states) {
+    const size_t inter_bytes = state_bytes * static_cast<size_t>(num_tokens);
+    if ((state && overlap(state, state_bytes, intermediate_states, inter_bytes)) ||
+        overlap(new_state, state_bytes, intermediate_states, inter_bytes))
+      return GDN_ERR_ALIASING;
+  }
+  if (int st = check_device(nullptr)) return st;
+  if (scale == 0.0f) scale = kDefaultScale;
+  cudaError_t err = gdn::launch_decode_mtp(q, k, v, state, A_log, a, dt_bias, b, scale, batch,
+                                           static_cast<int>(num_tokens), out, new_state,
+                                           intermediate_states, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 

@@ -112,6 +112,179 @@ gdn_decode_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k
   }
 }
 
+// Multi-token decode (speculative verify / MTP): T tokens per request, the
+// same step applied T times in order -- exactly T calls of the single-token
+// kernel above (same fp32 operations in the same order), with the state kept
+// in registers between tokens.  State traffic is that of one step (64 KiB in
+// + 64 KiB out per head); each extra token adds only its vectors.  Because a
+// CTA now lives through T tokens' dependent reductions, each warp owns 8 rows
+// (a CTA 64 rows, 2 CTAs per head): twice the state bytes in flight per CTA
+// and 8 independent reduction chains to interleave, which keeps the kernel
+// on the HBM roofline.  Token t of request r is row r * T + t of the [B*T, ...]
+// inputs and outputs.  `inter` (optional) receives the state after every
+// token, [B, T, 8, 128, 128] fp32, for rolling back rejected tokens.  All T
+// tokens' vectors for the CTA (q, k of its q/k head, v of its 64 rows, a, b:
+// ~0.6 KiB per token) are staged into shared memory in one round trip that
+// overlaps the state loads, so the token loop never waits on global memory.
+constexpr int kMtpRowsPerWarp = 8;
+
+// Sums v[i] (one value per state row, i < 8) across the warp with a
+// transposing butterfly: at offsets 16, 8 and 4 each lane keeps half of its
+// values and adds the partner's half, then offsets 2 and 1 finish the sum --
+// 9 shuffles instead of 8 x 5.  Every lane returns the total of row
+// (lane >> 2) & 7.  Each row's additions pair the same lanes at the same
+// offsets as warp_sum, and fp32 addition is commutative, so the totals equal
+// warp_sum's bit for bit.
+__device__ __forceinline__ float warp_sum8_transposed(const float (&v)[8], int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  float w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float send = b4 ? v[j] : v[j + 4];
+    const float keep = b4 ? v[j + 4] : v[j];
+    w[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float x[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float send = b3 ? w[j] : w[j + 2];
+    const float keep = b3 ? w[j + 2] : w[j];
+    x[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  const float send = b2 ? x[0] : x[1];
+  const float keep = b2 ? x[1] : x[0];
+  float y = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  y += __shfl_xor_sync(0xffffffffu, y, 2);
+  y += __shfl_xor_sync(0xffffffffu, y, 1);
+  return y;
+}
+constexpr int kMtpRowsPerCta = kDecWarps * kMtpRowsPerWarp;  // 64
+constexpr int kMtpCtasPerHead = kD / kMtpRowsPerCta;         // 2
+
+__global__ void __launch_bounds__(kDecWarps * 32)
+gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
+                      const uint16_t *__restrict__ v, const float *state,
+                      const float *__restrict__ A_log, const uint16_t *__restrict__ a,
+                      const float *__restrict__ dt_bias, const uint16_t *__restrict__ b,
+                      float scale, int T, uint16_t *__restrict__ out, float *new_state,
+                      float *__restrict__ inter) {
+  constexpr int R = kMtpRowsPerWarp;
+  const int64_t head = blockIdx.x / kMtpCtasPerHead;  // request * 8 + v-head
+  const int part = blockIdx.x % kMtpCtasPerHead;
+  const int64_t req = head / kHV;
+  const int hv = static_cast<int>(head % kHV);
+  const int hqk = hv >> 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = part * kMtpRowsPerCta + warp * R;
+  const int64_t sbase = head * kD * kD;
+
+  float4 s[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    if (state != nullptr) {
+      s[i] = __ldcs(reinterpret_cast<const float4 *>(state + sbase + (row0 + i) * kD) + lane);
+    } else {
+      s[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  const float alog = A_log[hv], dtb = dt_bias[hv];
+
+  // Stage every token's vectors (8-byte pieces: q/k/v are only guaranteed
+  // 8-byte aligned): per token 32 + 32 pieces of q, k, 16 of v (this CTA's 64
+  // rows), then a, b.
+  extern __shared__ uint2 mtp_smem[];
+  uint2 *qs = mtp_smem;                 // [T][32]
+  uint2 *ks = qs + 32 * T;              // [T][32]
+  uint2 *vs = ks + 32 * T;              // [T][16]
+  uint16_t *gs = reinterpret_cast<uint16_t *>(vs + 16 * T);  // [T][2]: a, b
+  for (int idx = threadIdx.x; idx < 80 * T; idx += kDecWarps * 32) {
+    const int t = idx / 80, p = idx % 80;
+    const int64_t tok = req * T + t;
+    if (p < 32) {
+      qs[t * 32 + p] = reinterpret_cast<const uint2 *>(q + (tok * kHQK + hqk) * kD)[p];
+    } else if (p < 64) {
+      ks[t * 32 + p - 32] = reinterpret_cast<const uint2 *>(k + (tok * kHQK + hqk) * kD)[p - 32];
+    } else {
+      vs[t * 16 + p - 64] = reinterpret_cast<const uint2 *>(
+          v + (tok * kHV + hv) * kD + part * kMtpRowsPerCta)[p - 64];
+    }
+  }
+  for (int t = threadIdx.x; t < T; t += kDecWarps * 32) {
+    const int64_t tok = req * T + t;
+    gs[2 * t] = a[tok * kHV + hv];
+    gs[2 * t + 1] = b[tok * kHV + hv];
+  }
+  __syncthreads();
+
+  for (int t = 0; t < T; ++t) {
+    const uint2 qr = qs[t * 32 + lane], kr = ks[t * 32 + lane];
+    const uint2 v0 = vs[t * 16 + 2 * warp], v1 = vs[t * 16 + 2 * warp + 1];
+    const uint16_t ar = gs[2 * t], br = gs[2 * t + 1];
+    const int64_t tok = req * T + t;
+    const float q0 = bf16_lo(qr.x) * scale, q1 = bf16_hi(qr.x) * scale;
+    const float q2 = bf16_lo(qr.y) * scale, q3 = bf16_hi(qr.y) * scale;
+    const float k0 = bf16_lo(kr.x), k1 = bf16_hi(kr.x), k2 = bf16_lo(kr.y), k3 = bf16_hi(kr.y);
+    const float g = expf(-expf(alog) * softplus_thr20(bf16_to_f32(ar) + dtb));
+    const float beta = 1.0f / (1.0f + expf(-bf16_to_f32(br)));
+    const float vv[R] = {bf16_lo(v0.x), bf16_hi(v0.x), bf16_lo(v0.y), bf16_hi(v0.y),
+                         bf16_lo(v1.x), bf16_hi(v1.x), bf16_lo(v1.y), bf16_hi(v1.y)};
+
+    float old[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      s[i].x *= g;
+      s[i].y *= g;
+      s[i].z *= g;
+      s[i].w *= g;
+      old[i] = s[i].x * k0 + s[i].y * k1 + s[i].z * k2 + s[i].w * k3;
+    }
+    {
+      const float tot = warp_sum8_transposed(old, lane);
+#pragma unroll
+      for (int i = 0; i < R; ++i) old[i] = __shfl_sync(0xffffffffu, tot, 4 * i);
+    }
+
+    float o[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const float delta = beta * (vv[i] - old[i]);
+      s[i].x += k0 * delta;
+      s[i].y += k1 * delta;
+      s[i].z += k2 * delta;
+      s[i].w += k3 * delta;
+      o[i] = s[i].x * q0 + s[i].y * q1 + s[i].z * q2 + s[i].w * q3;
+      if (inter != nullptr)
+        __stcs(reinterpret_cast<float4 *>(inter + ((tok * kHV + hv) * kD + row0 + i) * kD) + lane,
+               s[i]);
+    }
+    {
+      // lanes 4 i hold row i's output
+      const float tot = warp_sum8_transposed(o, lane);
+      if ((lane & 3) == 0)
+        out[(tok * kHV + hv) * kD + row0 + (lane >> 2)] =
+            __bfloat16_as_ushort(__float2bfloat16_rn(tot));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i)
+    __stcs(reinterpret_cast<float4 *>(new_state + sbase + (row0 + i) * kD) + lane, s[i]);
+}
+
+cudaError_t launch_decode_mtp(const void *q, const void *k, const void *v, const float *state,
+                              const float *A_log, const void *a, const float *dt_bias,
+                              const void *b, float scale, int64_t batch, int num_tokens,
+                              void *out, float *new_state, float *inter, cudaStream_t stream) {
+  if (batch == 0) return cudaSuccess;
+  const int64_t blocks = batch * kHV * kMtpCtasPerHead;
+  const size_t smem = static_cast<size_t>(num_tokens) * (80 * sizeof(uint2) + 2 * sizeof(uint16_t));
+  gdn_decode_mtp_kernel<<<static_cast<unsigned>(blocks), kDecWarps * 32, smem, stream>>>(
+      static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
+      static_cast<const uint16_t *>(v), state, A_log, static_cast<const uint16_t *>(a), dt_bias,
+      static_cast<const uint16_t *>(b), scale, num_tokens, static_cast<uint16_t *>(out),
+      new_state, inter);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_decode(const void *q, const void *k, const void *v, const float *state,
                           const float *A_log, const void *a, const float *dt_bias,
                           const void *b, float scale, int64_t batch, void *out,

@@ -91,3 +91,63 @@ def run_inplace(q, k, v, state, A_log, a, dt_bias, b, scale):
     decode_into(q.contiguous(), k.contiguous(), v.contiguous(), state, _f32(A_log),
                 a.contiguous(), _f32(dt_bias), b.contiguous(), scale, output, state)
     return output
+
+
+# ---------------------------------------------------------------------------
+# multi-token decode (speculative verify / MTP); no counterpart in the reference
+# ---------------------------------------------------------------------------
+MTP_MAX_TOKENS = 64
+
+
+def _check_mtp_inputs(q, k, v, a, b):
+    assert q.dim() == 4 and q.shape[2:] == (HQ, D), "q must be [B,T,4,128]"
+    B, T = q.shape[0], q.shape[1]
+    assert k.shape == (B, T, HQ, D), "k must be [B,T,4,128]"
+    assert v.shape == (B, T, HV, D), "v must be [B,T,8,128]"
+    assert a.numel() == B * T * HV and b.numel() == B * T * HV, "a, b must be [B,T,8]"
+    assert 1 <= T <= MTP_MAX_TOKENS, f"1 <= T <= {MTP_MAX_TOKENS}"
+    for name, t in (("q", q), ("k", k), ("v", v), ("a", a), ("b", b)):
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"GDN decode expects bf16 {name}, got {t.dtype}")
+        if not t.is_cuda:
+            raise ValueError(f"GDN decode expects CUDA tensors ({name} is on {t.device})")
+
+
+def decode_mtp_into(q, k, v, state, A_log, a, dt_bias, b, scale, out, new_state,
+                    intermediate: Optional[torch.Tensor] = None,
+                    stream: Optional[int] = None) -> None:
+    """Destination-passing multi-token decode: T tokens per request applied
+    in order (identical to T single-token steps).  Writes `out` [B,T,8,128]
+    bf16, `new_state` [B,8,128,128] fp32 (may be `state`) and, if given,
+    `intermediate` [B,T,8,128,128] fp32 = the state after each token."""
+    B, T = q.shape[0], q.shape[1]
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+    st = _native.lib.gdn_decode_mtp_qk4_v8_d128_k_last(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(),
+        None if state is None else state.data_ptr(),
+        A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
+        _scale(scale), B, T, out.data_ptr(), new_state.data_ptr(),
+        None if intermediate is None else intermediate.data_ptr(), stream)
+    _native.check(st, "gdn_decode_mtp_qk4_v8_d128_k_last")
+
+
+@torch.no_grad()
+def run_mtp(q, k, v, state, A_log, a, dt_bias, b, scale, return_intermediate: bool = False):
+    """Multi-token decode, value-returning like `run`: q, k [B,T,4,128],
+    v [B,T,8,128], a, b [B,T,8] bf16; state [B,8,128,128] fp32 or None.
+    Returns (output [B,T,8,128] bf16, new_state [B,8,128,128] fp32) and, with
+    return_intermediate, the states after each token [B,T,8,128,128] fp32
+    (what a speculative decoder keeps to roll back rejected tokens)."""
+    _check_mtp_inputs(q, k, v, a, b)
+    B, T = q.shape[0], q.shape[1]
+    if state is not None:
+        assert state.shape == (B, HV, D, D) and state.dtype == torch.float32
+        state = state.contiguous()
+    output = torch.empty(B, T, HV, D, dtype=q.dtype, device=q.device)
+    new_state = torch.empty(B, HV, D, D, dtype=torch.float32, device=q.device)
+    inter = (torch.empty(B, T, HV, D, D, dtype=torch.float32, device=q.device)
+             if return_intermediate else None)
+    decode_mtp_into(q.contiguous(), k.contiguous(), v.contiguous(), state, _f32(A_log),
+                    a.contiguous(), _f32(dt_bias), b.contiguous(), scale, output, new_state, inter)
+    return (output, new_state, inter) if return_intermediate else (output, new_state)
