@@ -47,7 +47,8 @@ const char *gdn_b200_status_string(int status);
  * total_tokens, a bounded wait that ran out) it records a nonzero code in a
  * per-device word and skips the work.  This call copies the word for the
  * current device into *code (stream-ordered, then synchronises `stream`) and
- * clears it.  Codes: 0 none, 1 bad cu_seqlens, 2 wait timeout.
+ * clears it.  Codes: 0 none, 1 bad cu_seqlens, 2 wait timeout, 3 a state-pool
+ * slot index outside [0, pool_slots) (that request / call is skipped).
  */
 int gdn_b200_read_device_status(int *code, void *stream);
 
@@ -102,6 +103,24 @@ int gdn_decode_mtp_qk4_v8_d128_k_last(const void *q, const void *k, const void *
                                       float *intermediate_states, void *stream);
 
 /*
+ * Decode against a paged state pool: the state of request i lives at
+ * state_pool[slots[i]] ([pool_slots,8,128,128] fp32, 16-byte aligned) and is
+ * updated there in place, so a serving engine keeps its GDN cache as one pool
+ * and never gathers or scatters states around the call.  num_tokens = 1 is
+ * gdn_decode_qk4_v8_d128_k_last, > 1 gdn_decode_mtp_qk4_v8_d128_k_last (same
+ * results bit for bit).  slots: [B] int32 on the device, distinct within a
+ * call (requests sharing a slot race); a slot outside [0, pool_slots) sets
+ * device status 3 and that request is skipped.  No counterpart in the
+ * reference (its definitions take dense [B,...] states).
+ */
+int gdn_decode_pool_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                       float *state_pool, int64_t pool_slots,
+                                       const int32_t *slots, const float *A_log,
+                                       const void *a, const float *dt_bias, const void *b,
+                                       float scale, int64_t batch, int64_t num_tokens,
+                                       void *out, void *stream);
+
+/*
  * Workspace (bytes) the prefill needs for `total_tokens` tokens packed into
  * `num_seqs` sequences.  Independent of the sequence lengths.
  */
@@ -145,6 +164,20 @@ int gdn_prefill_qk4_v8_d128_k_last(
     const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
     float scale, void *out, float *final_state, void *workspace,
     size_t workspace_bytes, void *stream);
+
+/*
+ * Prefill against a paged state pool: sequence n starts from
+ * state_pool[slots[n]] and its final state is written back there (a new
+ * sequence's slot must hold zeros or its initial state).  Otherwise as
+ * gdn_prefill_qk4_v8_d128_k_last (same workspace size).  slots: [N] int32 on
+ * the device, distinct; any slot outside [0, pool_slots) sets device status 3
+ * and the call writes nothing.  No counterpart in the reference.
+ */
+int gdn_prefill_pool_qk4_v8_d128_k_last(
+    const void *q, const void *k, const void *v, float *state_pool, int64_t pool_slots,
+    const int32_t *slots, const float *A_log, const void *a, const float *dt_bias,
+    const void *b, const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+    float scale, void *out, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Prefill that allocates nothing -- no counterpart in the reference.

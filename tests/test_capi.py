@@ -21,6 +21,7 @@ def test_header_declares_expected_entry_points():
     names = header_functions()
     for n in ("gdn_decode_qk4_v8_d128_k_last", "gdn_prefill_qk4_v8_d128_k_last",
               "gdn_decode_mtp_qk4_v8_d128_k_last", "gdn_prefill_kernel_launches",
+              "gdn_decode_pool_qk4_v8_d128_k_last", "gdn_prefill_pool_qk4_v8_d128_k_last",
               "gdn_prefill_workspace_bytes", "gdn_b200_status_string",
               "gdn_b200_abi_version", "gdn_b200_read_device_status"):
         assert n in names
@@ -88,6 +89,28 @@ def test_argument_validation_without_device(gdn):
     bad[8] = None
     assert lib.gdn_prefill_qk4_v8_d128_k_last(*bad, ok, 1 << 30, None) == 1
     assert lib.gdn_prefill_qk4_v8_d128_k_last(*args[:9], -1, 128, *args[11:], ok, 1 << 30, None) == 2
+
+
+def test_pool_entry_points_argument_validation_without_device(gdn):
+    lib = gdn._native.lib
+    P = ctypes.c_void_p
+    ok = P(0x10000)
+    dec = lib.gdn_decode_pool_qk4_v8_d128_k_last
+    # (q, k, v, pool, pool_slots, slots, A_log, a, dt_bias, b, scale, B, T, out, stream)
+    assert dec(ok, ok, ok, ok, 0, ok, ok, ok, ok, ok, 0.0, 4, 1, ok, None) == 2   # empty pool
+    assert dec(ok, ok, ok, ok, 8, ok, ok, ok, ok, ok, 0.0, 4, 0, ok, None) == 2   # T = 0
+    assert dec(ok, ok, ok, ok, 8, None, ok, ok, ok, ok, 0.0, 4, 1, ok, None) == 1  # no slots
+    assert dec(ok, ok, ok, P(0x10008), 8, ok, ok, ok, ok, ok, 0.0, 4, 1, ok, None) == 3
+    assert dec(ok, ok, ok, ok, 8, ok, ok, ok, ok, ok, 0.0, 0, 1, ok, None) == 0
+    pre = lib.gdn_prefill_pool_qk4_v8_d128_k_last
+    args = [ok, ok, ok, ok, 8, ok, ok, ok, ok, ok, ok, 2, 128, 0.0, ok]
+    assert pre(*args, ok, 16, None) == 4                       # workspace too small
+    bad = list(args)
+    bad[5] = None
+    assert pre(*bad, ok, 1 << 30, None) == 1                   # no slots
+    bad = list(args)
+    bad[4] = 0
+    assert pre(*bad, ok, 1 << 30, None) == 2                   # empty pool
 
 
 def test_mtp_decode_argument_validation_without_device(gdn):

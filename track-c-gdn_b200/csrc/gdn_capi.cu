@@ -17,18 +17,20 @@ namespace gdn {
 cudaError_t launch_decode(const void *q, const void *k, const void *v, const float *state,
                           const float *A_log, const void *a, const float *dt_bias,
                           const void *b, float scale, int64_t batch, void *out,
-                          float *new_state, cudaStream_t stream);
+                          float *new_state, const int32_t *slots, int64_t pool_slots,
+                          cudaStream_t stream);
 cudaError_t launch_decode_mtp(const void *q, const void *k, const void *v, const float *state,
                               const float *A_log, const void *a, const float *dt_bias,
                               const void *b, float scale, int64_t batch, int num_tokens,
-                              void *out, float *new_state, float *inter, cudaStream_t stream);
+                              void *out, float *new_state, float *inter, const int32_t *slots,
+                              int64_t pool_slots, cudaStream_t stream);
 size_t prefill_workspace_bytes(int64_t T, int64_t N, bool allow_segments);
 int prefill_kernel_launches(int64_t T, int64_t N, bool allow_segments);
 cudaError_t launch_prefill(const void *q, const void *k, const void *v, const float *state,
                            const float *A_log, const void *a, const float *dt_bias, const void *b,
                            const int64_t *cu_seqlens, int64_t N, int64_t T, float scale,
                            void *out, float *final_state, void *workspace, bool allow_segments,
-                           cudaStream_t stream);
+                           const int32_t *slots, int64_t pool_slots, cudaStream_t stream);
 }  // namespace gdn
 
 namespace {
@@ -113,7 +115,7 @@ int gdn_decode_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
   if (int st = check_device(&sms)) return st;
   if (scale == 0.0f) scale = kDefaultScale;
   cudaError_t err = gdn::launch_decode(q, k, v, state, A_log, a, dt_bias, b, scale, batch, out,
-                                       new_state, static_cast<cudaStream_t>(stream));
+                                       new_state, nullptr, 0, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
@@ -146,7 +148,8 @@ int gdn_decode_mtp_qk4_v8_d128_k_last(const void *q, const void *k, const void *
   if (scale == 0.0f) scale = kDefaultScale;
   cudaError_t err = gdn::launch_decode_mtp(q, k, v, state, A_log, a, dt_bias, b, scale, batch,
                                            static_cast<int>(num_tokens), out, new_state,
-                                           intermediate_states, static_cast<cudaStream_t>(stream));
+                                           intermediate_states, nullptr, 0,
+                                           static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
@@ -187,7 +190,66 @@ int gdn_prefill_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
   if (scale == 0.0f) scale = kDefaultScale;
   cudaError_t err = gdn::launch_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
                                         total_tokens, scale, out, final_state, workspace, true,
-                                        static_cast<cudaStream_t>(stream));
+                                        nullptr, 0, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+int gdn_decode_pool_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                       float *state_pool, int64_t pool_slots,
+                                       const int32_t *slots, const float *A_log, const void *a,
+                                       const float *dt_bias, const void *b, float scale,
+                                       int64_t batch, int64_t num_tokens, void *out,
+                                       void *stream) {
+  if (batch < 0 || pool_slots < 0 || num_tokens < 1 || num_tokens > GDN_DECODE_MTP_MAX_TOKENS ||
+      batch > (int64_t{1} << 26) / num_tokens || pool_slots > (int64_t{1} << 26))
+    return GDN_ERR_BAD_SIZE;
+  if (batch == 0) return GDN_OK;
+  if (pool_slots == 0) return GDN_ERR_BAD_SIZE;
+  if (!q || !k || !v || !state_pool || !slots || !A_log || !a || !dt_bias || !b || !out)
+    return GDN_ERR_NULL_POINTER;
+  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(v, 8) || !aligned(out, 8) ||
+      !aligned(state_pool, 16) || !aligned(slots, 4) || !aligned(a, 2) || !aligned(b, 2) ||
+      !aligned(A_log, 4) || !aligned(dt_bias, 4))
+    return GDN_ERR_MISALIGNED;
+  if (int st = check_device(nullptr)) return st;
+  if (scale == 0.0f) scale = kDefaultScale;
+  cudaError_t err =
+      num_tokens == 1
+          ? gdn::launch_decode(q, k, v, state_pool, A_log, a, dt_bias, b, scale, batch, out,
+                               state_pool, slots, pool_slots, static_cast<cudaStream_t>(stream))
+          : gdn::launch_decode_mtp(q, k, v, state_pool, A_log, a, dt_bias, b, scale, batch,
+                                   static_cast<int>(num_tokens), out, state_pool, nullptr, slots,
+                                   pool_slots, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+int gdn_prefill_pool_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                        float *state_pool, int64_t pool_slots,
+                                        const int32_t *slots, const float *A_log, const void *a,
+                                        const float *dt_bias, const void *b,
+                                        const int64_t *cu_seqlens, int64_t num_seqs,
+                                        int64_t total_tokens, float scale, void *out,
+                                        void *workspace, size_t workspace_bytes, void *stream) {
+  if (num_seqs < 0 || total_tokens < 0 || total_tokens > (int64_t{1} << 31) ||
+      num_seqs > (int64_t{1} << 24) || pool_slots < 0 || pool_slots > (int64_t{1} << 26))
+    return GDN_ERR_BAD_SIZE;
+  if (num_seqs == 0) return total_tokens == 0 ? GDN_OK : GDN_ERR_BAD_SIZE;
+  if (pool_slots == 0) return GDN_ERR_BAD_SIZE;
+  if (!cu_seqlens || !A_log || !dt_bias || !state_pool || !slots || !workspace)
+    return GDN_ERR_NULL_POINTER;
+  if (total_tokens > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL_POINTER;
+  if ((q && !aligned(q, 16)) || (k && !aligned(k, 16)) || (v && !aligned(v, 16)) ||
+      (out && !aligned(out, 16)) || !aligned(state_pool, 16) || !aligned(slots, 4) ||
+      !aligned(cu_seqlens, 8))
+    return GDN_ERR_MISALIGNED;
+  if (!aligned(workspace, 1024) ||
+      workspace_bytes < gdn::prefill_workspace_bytes(total_tokens, num_seqs, true))
+    return GDN_ERR_WORKSPACE;
+  if (int st = check_device(nullptr)) return st;
+  if (scale == 0.0f) scale = kDefaultScale;
+  cudaError_t err = gdn::launch_prefill(q, k, v, state_pool, A_log, a, dt_bias, b, cu_seqlens,
+                                        num_seqs, total_tokens, scale, out, state_pool, workspace,
+                                        true, slots, pool_slots, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 

@@ -15,6 +15,7 @@ constexpr int kChunk = 64;   // prefill chunk length (reference BT = 64)
 // Device status codes (see gdn_b200_read_device_status).
 constexpr int kDevStatusBadSeqlens = 1;
 constexpr int kDevStatusWaitTimeout = 2;
+constexpr int kDevStatusBadSlot = 3;  // a state-pool slot index out of range
 
 // Per-device status word (the library is one translation unit, gdn_b200.cu).
 __device__ int g_device_status = 0;

@@ -39,7 +39,8 @@ gdn_decode_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k
                   const uint16_t *__restrict__ v, const float *state,
                   const float *__restrict__ A_log, const uint16_t *__restrict__ a,
                   const float *__restrict__ dt_bias, const uint16_t *__restrict__ b,
-                  float scale, uint16_t *__restrict__ out, float *new_state) {
+                  float scale, uint16_t *__restrict__ out, float *new_state,
+                  const int32_t *__restrict__ slots, int64_t pool_slots) {
   const int64_t head = blockIdx.x / kDecCtasPerHead;  // request * 8 + v-head
   const int part = blockIdx.x % kDecCtasPerHead;
   const int64_t req = head / kHV;
@@ -47,7 +48,13 @@ gdn_decode_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k
   const int hqk = hv >> 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = part * kDecRowsPerCta + warp * kDecRowsPerWarp;  // first v index
-  const int64_t sbase = head * kD * kD;
+  // state of this request: dense (row req) or a slot of a state pool
+  const int64_t sreq = slots != nullptr ? slots[req] : req;
+  if (slots != nullptr && (sreq < 0 || sreq >= pool_slots)) {
+    if (threadIdx.x == 0) set_device_status(kDevStatusBadSlot);
+    return;
+  }
+  const int64_t sbase = (sreq * kHV + hv) * kD * kD;
 
   // Issue the state loads first: they are the long-latency part.
   float4 s[kDecRowsPerWarp];
@@ -161,13 +168,14 @@ __device__ __forceinline__ float warp_sum8_transposed(const float (&v)[8], int l
 constexpr int kMtpRowsPerCta = kDecWarps * kMtpRowsPerWarp;  // 64
 constexpr int kMtpCtasPerHead = kD / kMtpRowsPerCta;         // 2
 
-__global__ void __launch_bounds__(kDecWarps * 32)
+__global__ void __launch_bounds__(kDecWarps * 32, 4)
 gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
                       const uint16_t *__restrict__ v, const float *state,
                       const float *__restrict__ A_log, const uint16_t *__restrict__ a,
                       const float *__restrict__ dt_bias, const uint16_t *__restrict__ b,
                       float scale, int T, uint16_t *__restrict__ out, float *new_state,
-                      float *__restrict__ inter) {
+                      float *__restrict__ inter, const int32_t *__restrict__ slots,
+                      int64_t pool_slots) {
   constexpr int R = kMtpRowsPerWarp;
   const int64_t head = blockIdx.x / kMtpCtasPerHead;  // request * 8 + v-head
   const int part = blockIdx.x % kMtpCtasPerHead;
@@ -176,7 +184,12 @@ gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict
   const int hqk = hv >> 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = part * kMtpRowsPerCta + warp * R;
-  const int64_t sbase = head * kD * kD;
+  const int64_t sreq = slots != nullptr ? slots[req] : req;
+  if (slots != nullptr && (sreq < 0 || sreq >= pool_slots)) {
+    if (threadIdx.x == 0) set_device_status(kDevStatusBadSlot);
+    return;
+  }
+  const int64_t sbase = (sreq * kHV + hv) * kD * kD;
 
   float4 s[R];
 #pragma unroll
@@ -273,7 +286,8 @@ gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict
 cudaError_t launch_decode_mtp(const void *q, const void *k, const void *v, const float *state,
                               const float *A_log, const void *a, const float *dt_bias,
                               const void *b, float scale, int64_t batch, int num_tokens,
-                              void *out, float *new_state, float *inter, cudaStream_t stream) {
+                              void *out, float *new_state, float *inter, const int32_t *slots,
+                              int64_t pool_slots, cudaStream_t stream) {
   if (batch == 0) return cudaSuccess;
   const int64_t blocks = batch * kHV * kMtpCtasPerHead;
   const size_t smem = static_cast<size_t>(num_tokens) * (80 * sizeof(uint2) + 2 * sizeof(uint16_t));
@@ -281,20 +295,22 @@ cudaError_t launch_decode_mtp(const void *q, const void *k, const void *v, const
       static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
       static_cast<const uint16_t *>(v), state, A_log, static_cast<const uint16_t *>(a), dt_bias,
       static_cast<const uint16_t *>(b), scale, num_tokens, static_cast<uint16_t *>(out),
-      new_state, inter);
+      new_state, inter, slots, pool_slots);
   return cudaGetLastError();
 }
 
 cudaError_t launch_decode(const void *q, const void *k, const void *v, const float *state,
                           const float *A_log, const void *a, const float *dt_bias,
                           const void *b, float scale, int64_t batch, void *out,
-                          float *new_state, cudaStream_t stream) {
+                          float *new_state, const int32_t *slots, int64_t pool_slots,
+                          cudaStream_t stream) {
   if (batch == 0) return cudaSuccess;
   const int64_t blocks = batch * kHV * kDecCtasPerHead;
   gdn_decode_kernel<<<static_cast<unsigned>(blocks), kDecWarps * 32, 0, stream>>>(
       static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
       static_cast<const uint16_t *>(v), state, A_log, static_cast<const uint16_t *>(a), dt_bias,
-      static_cast<const uint16_t *>(b), scale, static_cast<uint16_t *>(out), new_state);
+      static_cast<const uint16_t *>(b), scale, static_cast<uint16_t *>(out), new_state, slots,
+      pool_slots);
   return cudaGetLastError();
 }
 

@@ -180,11 +180,27 @@ constexpr int kLptMaxSeqs = 2048;
 __global__ void __launch_bounds__(kMetaThreads)
 gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_t nt_max,
                         int *meta, int *chunk_off, int *seq_order, int2 *chunk_tab,
-                        int seg_chunks, int seg_max, int4 *items, int *seg_off) {
+                        int seg_chunks, int seg_max, int4 *items, int *seg_off,
+                        const int32_t *__restrict__ slots, int64_t pool_slots) {
   __shared__ int s_wtot[32];
   __shared__ int s_carry;
   __shared__ int s_nc[kLptMaxSeqs];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  // state-pool slots (when given) must lie in the pool
+  int bad_slot = 0;
+  if (slots != nullptr)
+    for (int i = tid; i < N; i += kMetaThreads)
+      if (slots[i] < 0 || slots[i] >= pool_slots) bad_slot = 1;
+  if (__syncthreads_or(bad_slot)) {
+    if (tid == 0) {
+      meta[0] = 0;
+      meta[1] = 1;
+      meta[2] = meta[3] = 0;
+      set_device_status(kDevStatusBadSlot);
+    }
+    return;
+  }
 
   int bad = 0;
   for (int i = tid; i < N; i += kMetaThreads)
@@ -820,7 +836,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         uint16_t *__restrict__ out, float *final_state,
                         const int4 *__restrict__ items, int count_slot, int64_t seg_tokens,
                         const int *__restrict__ seg_off, float *seg_ss, float *seg_sb,
-                        float *seg_phi) {
+                        float *seg_phi, const int32_t *__restrict__ slots) {
   using SM = ScanSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_align<1024>(smem_raw);
@@ -851,14 +867,16 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   auto seg_state = [&](float *buf, int p) {
     return buf + (static_cast<int64_t>(seg_off[n] + p) * kHV) * kD * kD + hv_off;
   };
+  // initial / final state of sequence n: dense (index n) or a state-pool slot
+  const int64_t sidx = slots != nullptr ? static_cast<int64_t>(slots[n]) : n;
   const float *init = nullptr;
   if (mode == kItemFull || mode == kItemHead)
-    init = h0 != nullptr ? h0 + static_cast<int64_t>(n) * kHV * kD * kD + hv_off : nullptr;
+    init = h0 != nullptr ? h0 + sidx * kHV * kD * kD + hv_off : nullptr;
   else if (mode == kItemMid || mode == kItemTail)
     init = seg_state(seg_ss, seg);
   float *fin = nullptr;
   if (mode == kItemFull || mode == kItemTail)
-    fin = final_state + static_cast<int64_t>(n) * kHV * kD * kD + hv_off;
+    fin = final_state + sidx * kHV * kD * kD + hv_off;
   else if (mode == kItemHead)
     fin = seg_state(seg_ss, 1);
   else if (mode == kItemZero)
@@ -1354,7 +1372,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
                            const float *A_log, const void *a, const float *dt_bias, const void *b,
                            const int64_t *cu_seqlens, int64_t N, int64_t T, float scale,
                            void *out, float *final_state, void *workspace, bool allow_segments,
-                           cudaStream_t stream) {
+                           const int32_t *slots, int64_t pool_slots, cudaStream_t stream) {
   if (N == 0) return cudaSuccess;
   const PrefillWs w = prefill_ws_layout(T, N, allow_segments);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
@@ -1385,7 +1403,8 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
 
   gdn_prefill_meta_kernel<<<1, kMetaThreads, 0, stream>>>(
       cu_seqlens, static_cast<int>(N), T, w.nt_max, meta, chunk_off, seq_order, chunk_tab,
-      static_cast<int>(w.seg_chunks), static_cast<int>(w.seg_max), items, seg_off);
+      static_cast<int>(w.seg_chunks), static_cast<int>(w.seg_max), items, seg_off, slots,
+      pool_slots);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
 
@@ -1408,7 +1427,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   gdn_prefill_scan_kernel<<<static_cast<unsigned>(n1 * kHV), kScanThreads, ScanSmem::kBytes,
                             stream>>>(tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta,
                                       m2, scale, static_cast<uint16_t *>(out), final_state, items,
-                                      2, seg_tokens, seg_off, seg_ss, seg_sb, seg_phi);
+                                      2, seg_tokens, seg_off, seg_ss, seg_sb, seg_phi, slots);
   err = cudaGetLastError();
   if (err != cudaSuccess || w.seg_chunks == 0) return err;
 
@@ -1425,7 +1444,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
                             ScanSmem::kBytes, stream>>>(
       tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale,
       static_cast<uint16_t *>(out), final_state, items + 2 * w.seg_max, 3, seg_tokens, seg_off,
-      seg_ss, seg_sb, seg_phi);
+      seg_ss, seg_sb, seg_phi, slots);
   return cudaGetLastError();
 }
 

@@ -151,3 +151,34 @@ def run_mtp(q, k, v, state, A_log, a, dt_bias, b, scale, return_intermediate: bo
     decode_mtp_into(q.contiguous(), k.contiguous(), v.contiguous(), state, _f32(A_log),
                     a.contiguous(), _f32(dt_bias), b.contiguous(), scale, output, new_state, inter)
     return (output, new_state, inter) if return_intermediate else (output, new_state)
+
+
+# ---------------------------------------------------------------------------
+# decode against a paged state pool; no counterpart in the reference
+# ---------------------------------------------------------------------------
+@torch.no_grad()
+def run_pool(q, k, v, state_pool, slots, A_log, a, dt_bias, b, scale,
+             stream: Optional[int] = None):
+    """Decode with the states in a pool: request i's state is
+    state_pool[slots[i]] ([P,8,128,128] fp32, updated in place).  q, k, v,
+    a, b as in `run` ([B,1,...]) or `run_mtp` ([B,T,...]); slots: [B] int32
+    CUDA tensor of distinct slots.  Returns output [B,T,8,128] bf16.  A slot
+    outside the pool is reported through the device status (code 3)."""
+    if q.shape[1] == 1 and q.dim() == 4:
+        _check_inputs(q, k, v, a, b)
+    else:
+        _check_mtp_inputs(q, k, v, a, b)
+    B, T = q.shape[0], q.shape[1]
+    assert state_pool.dim() == 4 and state_pool.shape[1:] == (HV, D, D)
+    assert state_pool.dtype == torch.float32 and state_pool.is_contiguous()
+    assert slots.dtype == torch.int32 and slots.numel() == B and slots.is_cuda
+    output = torch.empty(B, T, HV, D, dtype=q.dtype, device=q.device)
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+    st = _native.lib.gdn_decode_pool_qk4_v8_d128_k_last(
+        q.contiguous().data_ptr(), k.contiguous().data_ptr(), v.contiguous().data_ptr(),
+        state_pool.data_ptr(), state_pool.shape[0], slots.contiguous().data_ptr(),
+        _f32(A_log).data_ptr(), a.contiguous().data_ptr(), _f32(dt_bias).data_ptr(),
+        b.contiguous().data_ptr(), _scale(scale), B, T, output.data_ptr(), stream)
+    _native.check(st, "gdn_decode_pool_qk4_v8_d128_k_last")
+    return output

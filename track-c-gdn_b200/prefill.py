@@ -106,3 +106,43 @@ def run(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, state: Optional[torch
                  a.contiguous(), dt_bias.contiguous(), b.contiguous(), cu_seqlens.contiguous(),
                  scale, out, final_state, ws)
     return out, final_state
+
+
+def prefill_pool_into(q, k, v, state_pool, slots, A_log, a, dt_bias, b, cu_seqlens, scale, out,
+                      workspace: torch.Tensor, stream: Optional[int] = None) -> None:
+    """Destination-passing prefill against a paged state pool: sequence n
+    starts from state_pool[slots[n]] and its final state is written back
+    there.  No host sync; a slot outside the pool is reported through the
+    device status (code 3) and nothing is written.  No counterpart in the
+    reference."""
+    T = q.shape[0]
+    N = cu_seqlens.numel() - 1
+    if scale is None or scale == 0.0:
+        scale = 1.0 / math.sqrt(HEAD_SIZE)
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+    wptr, wbytes = _aligned_ptr(workspace)
+    st = _native.lib.gdn_prefill_pool_qk4_v8_d128_k_last(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), state_pool.data_ptr(), state_pool.shape[0],
+        slots.data_ptr(), A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
+        cu_seqlens.data_ptr(), N, T, float(scale), out.data_ptr(), wptr, wbytes, stream)
+    _native.check(st, "gdn_prefill_pool_qk4_v8_d128_k_last")
+
+
+@torch.no_grad()
+def run_pool(q, k, v, state_pool, slots, A_log, a, dt_bias, b, cu_seqlens, scale):
+    """Prefill with the states in a pool ([P,8,128,128] fp32, updated in
+    place at the given slots; slots: [N] int32 CUDA tensor of distinct slots).
+    Returns the output [T,8,128] bf16."""
+    _validate_inputs(q, k, v, None, A_log, a, dt_bias, b, cu_seqlens)
+    assert state_pool.dim() == 4 and state_pool.shape[1:] == (NUM_V_HEADS, HEAD_SIZE, HEAD_SIZE)
+    assert state_pool.dtype == torch.float32 and state_pool.is_contiguous()
+    N = cu_seqlens.numel() - 1
+    assert slots.dtype == torch.int32 and slots.numel() == N and slots.is_cuda
+    T = q.shape[0]
+    out = torch.empty(T, NUM_V_HEADS, HEAD_SIZE, dtype=torch.bfloat16, device=q.device)
+    ws = alloc_workspace(T, N, q.device)
+    prefill_pool_into(q.contiguous(), k.contiguous(), v.contiguous(), state_pool,
+                      slots.contiguous(), A_log.contiguous(), a.contiguous(), dt_bias.contiguous(),
+                      b.contiguous(), cu_seqlens.contiguous(), scale, out, ws)
+    return out
