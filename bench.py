@@ -10,7 +10,7 @@ bin packing by sequence), so scaling is "strong".  All inputs are seeded
 synthetic tensors with the BASELINE value distributions.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference|triton]
-                    [--workload c4|c2|c3|decode|mtp]
+                    [--workload c4|c2|c3|decode|mtp|decode_bf16]
 
 Prints one JSON line (rank 0).  `value` is whole-job tokens/s (decode tokens
 + prefill tokens) over the device time of K steps (max over ranks);
@@ -73,6 +73,9 @@ WORKLOADS = {
     "mtp": dict(desc="multi-token decode (speculative verify): batch 1024 x 4 tokens per request, "
                      "state updated in place",
                 decode_batch=1024, decode_tokens=4, prefill=None),
+    "decode_bf16": dict(desc="decode batch 1024 with the state stored in bf16 (opt-in format), "
+                             "updated in place",
+                        decode_batch=1024, prefill=None, state_bf16=True),
 }
 
 
@@ -251,7 +254,7 @@ def make_prefill_inputs(torch, lengths, with_state, seed, dev):
     return dict(q=q, k=k, v=v, a=a, b=b, h0=h0, cu=torch.from_numpy(cu).to(dev), T=T, N=N)
 
 
-def make_decode_inputs(torch, B, seed, dev, T=1):
+def make_decode_inputs(torch, B, seed, dev, T=1, state_bf16=False):
     import torch.nn.functional as F
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
@@ -261,12 +264,18 @@ def make_decode_inputs(torch, B, seed, dev, T=1):
     a = torch.randn(B, T, HV, generator=g, device=dev).bfloat16()
     b = torch.randn(B, T, HV, generator=g, device=dev).bfloat16()
     state = torch.randn(B, HV, D, D, generator=g, device=dev) * 0.02
-    return dict(q=q, k=k, v=v, a=a, b=b, state=state, B=B, T=T)
+    if state_bf16:
+        state = state.bfloat16()
+    return dict(q=q, k=k, v=v, a=a, b=b, state=state, B=B, T=T, bf16=state_bf16)
 
 
 def run_decode(gdn, dec, A_log, dt_bias, out):
-    """One decode step of the workload (multi-token when T > 1), state in place."""
-    if dec["T"] == 1:
+    """One decode step of the workload (multi-token when T > 1, bf16 state
+    when the workload says so), state in place."""
+    if dec.get("bf16"):
+        gdn.decode.decode_bf16_state_into(dec["q"], dec["k"], dec["v"], dec["state"], A_log,
+                                          dec["a"], dt_bias, dec["b"], None, out)
+    elif dec["T"] == 1:
         gdn.decode.decode_into(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"],
                                dt_bias, dec["b"], None, out, dec["state"])
     else:
@@ -308,7 +317,8 @@ def gpu_arm(args):
     dec_slice = shard.block_partition(B_total, world, rank)
     B = dec_slice.stop - dec_slice.start
     Tdec = wl.get("decode_tokens", 1)
-    dec = make_decode_inputs(torch, B, 100 + rank, dev, Tdec) if B > 0 else None
+    dec = (make_decode_inputs(torch, B, 100 + rank, dev, Tdec, wl.get("state_bf16", False))
+           if B > 0 else None)
     pre = None
     total_prefill_tokens = 0
     seq_counts = [0] * world
@@ -439,6 +449,7 @@ def gpu_arm(args):
             "workload": wl["desc"],
             "decode_batch": B_total,
             "decode_tokens_per_request": Tdec,
+            "state_dtype": "bf16" if wl.get("state_bf16") else "fp32",
             "prefill_sequences": int(sum(seq_counts)) if wl["prefill"] else 0,
             "prefill_tokens": total_prefill_tokens,
             "l2": "inputs larger than L2 (no flush needed)" if total_tokens > 20000 else
@@ -455,7 +466,8 @@ def gpu_arm(args):
         "clocks": clocks,
     }
     if dec is not None:
-        gbs = B * (DECODE_STATE_BYTES + Tdec * DECODE_VEC_BYTES) / (d_ms / 1e3) / 1e9
+        state_bytes = DECODE_STATE_BYTES // 2 if wl.get("state_bf16") else DECODE_STATE_BYTES
+        gbs = B * (state_bytes + Tdec * DECODE_VEC_BYTES) / (d_ms / 1e3) / 1e9
         result["decode"] = {"us_per_step": d_ms_max * 1e3, "state_gbs_rank0": gbs,
                             "batch_per_rank": B}
         result["roofline_decode"] = {
@@ -782,7 +794,8 @@ def triton_arm(args):
     A_log = (torch.rand(HV, generator=g, device=dev) * 2.7).float()
     dt_bias = (torch.randn(HV, generator=g, device=dev) * 0.1).float()
     Tdec = wl.get("decode_tokens", 1)
-    dec = make_decode_inputs(torch, wl["decode_batch"], 100, dev, Tdec) if wl["decode_batch"] else None
+    dec = (make_decode_inputs(torch, wl["decode_batch"], 100, dev, Tdec, wl.get("state_bf16", False))
+           if wl["decode_batch"] else None)
     pre = None
     if wl["prefill"]:
         lengths = prefill_lengths(wl["prefill"])
@@ -790,14 +803,17 @@ def triton_arm(args):
     stream = torch.cuda.current_stream(dev)
     ev = {k: [] for k in ("s", "d", "p")}
     keep = {}
+    # the reference keeps fp32 state: a bf16 state is widened once, outside the timing
+    ref_state = dec["state"].float() if dec is not None else None
 
     def step(record):
         if record:
             ev["s"].append(torch.cuda.Event(enable_timing=True))
             ev["s"][-1].record(stream)
         if dec is not None:
-            # the reference decode takes one token per request: T calls, state chained
-            cur, outs = dec["state"], []
+            # the reference decode takes one token per request (T calls, state
+            # chained) and an fp32 state (a bf16 state is widened)
+            cur, outs = ref_state, []
             for t in range(Tdec):
                 sl = slice(t, t + 1)
                 o_t, cur = dec_mod.run(dec["q"][:, sl].contiguous(), dec["k"][:, sl].contiguous(),
@@ -842,9 +858,14 @@ def triton_arm(args):
 
     parity = {}
     if dec is not None:
-        fn = gdn.decode.run if Tdec == 1 else gdn.decode.run_mtp
-        o, s = fn(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"], dt_bias, dec["b"],
-                  None)
+        if dec.get("bf16"):
+            s = dec["state"].clone()
+            o = gdn.decode.run_bf16_state(dec["q"], dec["k"], dec["v"], s, A_log, dec["a"],
+                                          dt_bias, dec["b"], None)
+        else:
+            fn = gdn.decode.run if Tdec == 1 else gdn.decode.run_mtp
+            o, s = fn(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"], dt_bias,
+                      dec["b"], None)
         parity["decode_out_rel_fro"] = rel(o, keep["dec"][0])
         parity["decode_state_rel_fro"] = rel(s, keep["dec"][1])
     if pre is not None:

@@ -121,6 +121,25 @@ int gdn_decode_pool_qk4_v8_d128_k_last(const void *q, const void *k, const void 
                                        void *out, void *stream);
 
 /*
+ * Decode with the recurrent state stored in bf16 (half the state bytes, so
+ * about twice the decode throughput on the HBM roofline): the state is
+ * widened to fp32, the step computed in fp32 exactly as
+ * gdn_decode_qk4_v8_d128_k_last does (the output uses the unrounded update),
+ * and the new state rounded to nearest even and stored back in place; with
+ * T > 1 tokens the state is rounded after every token, as T separate calls
+ * would.  state_bf16: [B,8,128,128] bf16 when slots is NULL, else a pool
+ * [pool_slots,8,128,128] bf16 addressed by slots ([B] int32, distinct; a slot
+ * outside the pool sets device status 3).  16-byte aligned.  The reference
+ * keeps its state in fp32 only; this is an opt-in storage format.
+ */
+int gdn_decode_bf16_state_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                             void *state_bf16, int64_t pool_slots,
+                                             const int32_t *slots, const float *A_log,
+                                             const void *a, const float *dt_bias, const void *b,
+                                             float scale, int64_t batch, int64_t num_tokens,
+                                             void *out, void *stream);
+
+/*
  * Workspace (bytes) the prefill needs for `total_tokens` tokens packed into
  * `num_seqs` sequences.  Independent of the sequence lengths.
  */

@@ -28,6 +28,8 @@ SIGNATURES = {
     "gdn_prefill_pool_qk4_v8_d128_k_last": (
         ctypes.c_int,
         [_P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P, ctypes.c_size_t, _P]),
+    "gdn_decode_bf16_state_qk4_v8_d128_k_last": (
+        ctypes.c_int, [_P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _F, _I64, _I64, _P, _P]),
     "gdn_prefill_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
     "gdn_prefill_kernel_launches": (ctypes.c_int, [_I64, _I64]),
     "gdn_prefill_qk4_v8_d128_k_last": (

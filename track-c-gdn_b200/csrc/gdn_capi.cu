@@ -24,6 +24,11 @@ cudaError_t launch_decode_mtp(const void *q, const void *k, const void *v, const
                               const void *b, float scale, int64_t batch, int num_tokens,
                               void *out, float *new_state, float *inter, const int32_t *slots,
                               int64_t pool_slots, cudaStream_t stream);
+cudaError_t launch_decode_bf16_state(const void *q, const void *k, const void *v, void *state,
+                                     const float *A_log, const void *a, const float *dt_bias,
+                                     const void *b, float scale, int64_t batch, int num_tokens,
+                                     void *out, const int32_t *slots, int64_t pool_slots,
+                                     cudaStream_t stream);
 size_t prefill_workspace_bytes(int64_t T, int64_t N, bool allow_segments);
 int prefill_kernel_launches(int64_t T, int64_t N, bool allow_segments);
 cudaError_t launch_prefill(const void *q, const void *k, const void *v, const float *state,
@@ -220,6 +225,31 @@ int gdn_decode_pool_qk4_v8_d128_k_last(const void *q, const void *k, const void 
           : gdn::launch_decode_mtp(q, k, v, state_pool, A_log, a, dt_bias, b, scale, batch,
                                    static_cast<int>(num_tokens), out, state_pool, nullptr, slots,
                                    pool_slots, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+int gdn_decode_bf16_state_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
+                                             void *state_bf16, int64_t pool_slots,
+                                             const int32_t *slots, const float *A_log,
+                                             const void *a, const float *dt_bias, const void *b,
+                                             float scale, int64_t batch, int64_t num_tokens,
+                                             void *out, void *stream) {
+  if (batch < 0 || num_tokens < 1 || num_tokens > GDN_DECODE_MTP_MAX_TOKENS ||
+      batch > (int64_t{1} << 26) / num_tokens || pool_slots < 0 || pool_slots > (int64_t{1} << 26))
+    return GDN_ERR_BAD_SIZE;
+  if (batch == 0) return GDN_OK;
+  if (slots && pool_slots == 0) return GDN_ERR_BAD_SIZE;
+  if (!q || !k || !v || !state_bf16 || !A_log || !a || !dt_bias || !b || !out)
+    return GDN_ERR_NULL_POINTER;
+  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(v, 8) || !aligned(out, 8) ||
+      !aligned(state_bf16, 16) || (slots && !aligned(slots, 4)) || !aligned(a, 2) ||
+      !aligned(b, 2) || !aligned(A_log, 4) || !aligned(dt_bias, 4))
+    return GDN_ERR_MISALIGNED;
+  if (int st = check_device(nullptr)) return st;
+  if (scale == 0.0f) scale = kDefaultScale;
+  cudaError_t err = gdn::launch_decode_bf16_state(
+      q, k, v, state_bf16, A_log, a, dt_bias, b, scale, batch, static_cast<int>(num_tokens), out,
+      slots, slots ? pool_slots : 0, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 

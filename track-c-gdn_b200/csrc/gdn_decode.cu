@@ -34,106 +34,39 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
-__global__ void __launch_bounds__(kDecWarps * 32)
-gdn_decode_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
-                  const uint16_t *__restrict__ v, const float *state,
-                  const float *__restrict__ A_log, const uint16_t *__restrict__ a,
-                  const float *__restrict__ dt_bias, const uint16_t *__restrict__ b,
-                  float scale, uint16_t *__restrict__ out, float *new_state,
-                  const int32_t *__restrict__ slots, int64_t pool_slots) {
-  const int64_t head = blockIdx.x / kDecCtasPerHead;  // request * 8 + v-head
-  const int part = blockIdx.x % kDecCtasPerHead;
-  const int64_t req = head / kHV;
-  const int hv = static_cast<int>(head % kHV);
-  const int hqk = hv >> 1;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = part * kDecRowsPerCta + warp * kDecRowsPerWarp;  // first v index
-  // state of this request: dense (row req) or a slot of a state pool
-  const int64_t sreq = slots != nullptr ? slots[req] : req;
-  if (slots != nullptr && (sreq < 0 || sreq >= pool_slots)) {
-    if (threadIdx.x == 0) set_device_status(kDevStatusBadSlot);
-    return;
+// State element access for the fp32 state and the bf16 state variant (the
+// latter: 8 bytes per lane per row, widened to fp32 on load and rounded to
+// nearest even on store; all arithmetic stays fp32).
+template <bool kBf16>
+struct StateIO;
+template <>
+struct StateIO<false> {
+  using T = float;
+  static __device__ __forceinline__ float4 load(const float *row, int lane) {
+    return __ldcs(reinterpret_cast<const float4 *>(row) + lane);
   }
-  const int64_t sbase = (sreq * kHV + hv) * kD * kD;
-
-  // Issue the state loads first: they are the long-latency part.
-  float4 s[kDecRowsPerWarp];
-#pragma unroll
-  for (int i = 0; i < kDecRowsPerWarp; ++i) {
-    if (state != nullptr) {
-      s[i] = __ldcs(reinterpret_cast<const float4 *>(state + sbase + (row0 + i) * kD) + lane);
-    } else {
-      s[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+  static __device__ __forceinline__ void store(float *row, int lane, float4 x) {
+    __stcs(reinterpret_cast<float4 *>(row) + lane, x);
   }
-
-  // Lane l owns k-columns 4l .. 4l+3.
-  const int64_t qk_off = (req * kHQK + hqk) * kD + 4 * lane;
-  const uint2 qr = *reinterpret_cast<const uint2 *>(q + qk_off);
-  const uint2 kr = *reinterpret_cast<const uint2 *>(k + qk_off);
-  const float q0 = bf16_lo(qr.x) * scale, q1 = bf16_hi(qr.x) * scale;
-  const float q2 = bf16_lo(qr.y) * scale, q3 = bf16_hi(qr.y) * scale;
-  const float k0 = bf16_lo(kr.x), k1 = bf16_hi(kr.x), k2 = bf16_lo(kr.y), k3 = bf16_hi(kr.y);
-
-  // Gates (kernel.py:59-65).
-  const float a_val = bf16_to_f32(a[head]);
-  const float b_val = bf16_to_f32(b[head]);
-  const float g = expf(-expf(A_log[hv]) * softplus_thr20(a_val + dt_bias[hv]));
-  const float beta = 1.0f / (1.0f + expf(-b_val));
-
-  // v values of this warp's four rows (row0 is a multiple of 4: 8-byte load).
-  const uint2 vr = *reinterpret_cast<const uint2 *>(v + head * kD + row0);
-  const float vv[4] = {bf16_lo(vr.x), bf16_hi(vr.x), bf16_lo(vr.y), bf16_hi(vr.y)};
-
-  float old[kDecRowsPerWarp];
-#pragma unroll
-  for (int i = 0; i < kDecRowsPerWarp; ++i) {
-    s[i].x *= g;
-    s[i].y *= g;
-    s[i].z *= g;
-    s[i].w *= g;
-    old[i] = s[i].x * k0 + s[i].y * k1 + s[i].z * k2 + s[i].w * k3;
+  static __device__ __forceinline__ float4 round(float4 x) { return x; }
+};
+template <>
+struct StateIO<true> {
+  using T = uint16_t;
+  static __device__ __forceinline__ float4 load(const uint16_t *row, int lane) {
+    const uint2 r = __ldcs(reinterpret_cast<const uint2 *>(row) + lane);
+    return make_float4(bf16_lo(r.x), bf16_hi(r.x), bf16_lo(r.y), bf16_hi(r.y));
   }
-#pragma unroll
-  for (int i = 0; i < kDecRowsPerWarp; ++i) old[i] = warp_sum(old[i]);
-
-  float o[kDecRowsPerWarp];
-#pragma unroll
-  for (int i = 0; i < kDecRowsPerWarp; ++i) {
-    const float delta = beta * (vv[i] - old[i]);
-    s[i].x += k0 * delta;
-    s[i].y += k1 * delta;
-    s[i].z += k2 * delta;
-    s[i].w += k3 * delta;
-    o[i] = s[i].x * q0 + s[i].y * q1 + s[i].z * q2 + s[i].w * q3;
-    __stcs(reinterpret_cast<float4 *>(new_state + sbase + (row0 + i) * kD) + lane, s[i]);
+  static __device__ __forceinline__ void store(uint16_t *row, int lane, float4 x) {
+    __stcs(reinterpret_cast<uint2 *>(row) + lane,
+           make_uint2(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w)));
   }
-#pragma unroll
-  for (int i = 0; i < kDecRowsPerWarp; ++i) o[i] = warp_sum(o[i]);
-
-  if (lane == 0) {
-    uint2 packed;
-    packed.x = pack_bf16x2(o[0], o[1]);
-    packed.y = pack_bf16x2(o[2], o[3]);
-    *reinterpret_cast<uint2 *>(out + head * kD + row0) = packed;
+  // the value a bf16 state holds after a store
+  static __device__ __forceinline__ float4 round(float4 x) {
+    const uint32_t lo = pack_bf16x2(x.x, x.y), hi = pack_bf16x2(x.z, x.w);
+    return make_float4(bf16_lo(lo), bf16_hi(lo), bf16_lo(hi), bf16_hi(hi));
   }
-}
-
-// Multi-token decode (speculative verify / MTP): T tokens per request, the
-// same step applied T times in order -- exactly T calls of the single-token
-// kernel above (same fp32 operations in the same order), with the state kept
-// in registers between tokens.  State traffic is that of one step (64 KiB in
-// + 64 KiB out per head); each extra token adds only its vectors.  Because a
-// CTA now lives through T tokens' dependent reductions, each warp owns 8 rows
-// (a CTA 64 rows, 2 CTAs per head): twice the state bytes in flight per CTA
-// and 8 independent reduction chains to interleave, which keeps the kernel
-// on the HBM roofline.  Token t of request r is row r * T + t of the [B*T, ...]
-// inputs and outputs.  `inter` (optional) receives the state after every
-// token, [B, T, 8, 128, 128] fp32, for rolling back rejected tokens.  All T
-// tokens' vectors for the CTA (q, k of its q/k head, v of its 64 rows, a, b:
-// ~0.6 KiB per token) are staged into shared memory in one round trip that
-// overlaps the state loads, so the token loop never waits on global memory.
-constexpr int kMtpRowsPerWarp = 8;
+};
 
 // Sums v[i] (one value per state row, i < 8) across the warp with a
 // transposing butterfly: at offsets 16, 8 and 4 each lane keeps half of its
@@ -165,17 +98,150 @@ __device__ __forceinline__ float warp_sum8_transposed(const float (&v)[8], int l
   y += __shfl_xor_sync(0xffffffffu, y, 1);
   return y;
 }
+// Single-token step, templated on the state format (fp32 or bf16 storage)
+// and the rows per warp R: fp32 uses R = 4 (32 rows per CTA, 4 CTAs per
+// head); the bf16 state uses R = 8, so a warp still keeps 2 KiB of state in
+// flight, and reduces its rows with the transposing butterfly (same sums, bit
+// for bit, as one warp_sum per row).
+template <bool kBf16, int R>
+__global__ void __launch_bounds__(kDecWarps * 32)
+gdn_decode_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
+                  const uint16_t *__restrict__ v, const typename StateIO<kBf16>::T *state,
+                  const float *__restrict__ A_log, const uint16_t *__restrict__ a,
+                  const float *__restrict__ dt_bias, const uint16_t *__restrict__ b,
+                  float scale, uint16_t *__restrict__ out, typename StateIO<kBf16>::T *new_state,
+                  const int32_t *__restrict__ slots, int64_t pool_slots) {
+  using IO = StateIO<kBf16>;
+  static_assert(R == 4 || R == 8, "4 or 8 rows per warp");
+  constexpr int kRowsPerCta = kDecWarps * R;
+  constexpr int kCtasPerHead = kD / kRowsPerCta;
+  const int64_t head = blockIdx.x / kCtasPerHead;  // request * 8 + v-head
+  const int part = blockIdx.x % kCtasPerHead;
+  const int64_t req = head / kHV;
+  const int hv = static_cast<int>(head % kHV);
+  const int hqk = hv >> 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = part * kRowsPerCta + warp * R;  // first v index
+  // state of this request: dense (row req) or a slot of a state pool
+  const int64_t sreq = slots != nullptr ? slots[req] : req;
+  if (slots != nullptr && (sreq < 0 || sreq >= pool_slots)) {
+    if (threadIdx.x == 0) set_device_status(kDevStatusBadSlot);
+    return;
+  }
+  const int64_t sbase = (sreq * kHV + hv) * kD * kD;
+
+  // Issue the state loads first: they are the long-latency part.
+  float4 s[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    if (state != nullptr) {
+      s[i] = IO::load(state + sbase + (row0 + i) * kD, lane);
+    } else {
+      s[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+
+  // Lane l owns k-columns 4l .. 4l+3.
+  const int64_t qk_off = (req * kHQK + hqk) * kD + 4 * lane;
+  const uint2 qr = *reinterpret_cast<const uint2 *>(q + qk_off);
+  const uint2 kr = *reinterpret_cast<const uint2 *>(k + qk_off);
+  const float q0 = bf16_lo(qr.x) * scale, q1 = bf16_hi(qr.x) * scale;
+  const float q2 = bf16_lo(qr.y) * scale, q3 = bf16_hi(qr.y) * scale;
+  const float k0 = bf16_lo(kr.x), k1 = bf16_hi(kr.x), k2 = bf16_lo(kr.y), k3 = bf16_hi(kr.y);
+
+  // Gates (kernel.py:59-65).
+  const float a_val = bf16_to_f32(a[head]);
+  const float b_val = bf16_to_f32(b[head]);
+  const float g = expf(-expf(A_log[hv]) * softplus_thr20(a_val + dt_bias[hv]));
+  const float beta = 1.0f / (1.0f + expf(-b_val));
+
+  // v values of this warp's rows (row0 is a multiple of 4: 8-byte loads).
+  float vv[R];
+#pragma unroll
+  for (int h = 0; h < R / 4; ++h) {
+    const uint2 vr = *reinterpret_cast<const uint2 *>(v + head * kD + row0 + 4 * h);
+    vv[4 * h] = bf16_lo(vr.x);
+    vv[4 * h + 1] = bf16_hi(vr.x);
+    vv[4 * h + 2] = bf16_lo(vr.y);
+    vv[4 * h + 3] = bf16_hi(vr.y);
+  }
+
+  float old[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    s[i].x *= g;
+    s[i].y *= g;
+    s[i].z *= g;
+    s[i].w *= g;
+    old[i] = s[i].x * k0 + s[i].y * k1 + s[i].z * k2 + s[i].w * k3;
+  }
+  if constexpr (R == 8) {
+    const float tot = warp_sum8_transposed(old, lane);
+#pragma unroll
+    for (int i = 0; i < R; ++i) old[i] = __shfl_sync(0xffffffffu, tot, 4 * i);
+  } else {
+#pragma unroll
+    for (int i = 0; i < R; ++i) old[i] = warp_sum(old[i]);
+  }
+
+  float o[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const float delta = beta * (vv[i] - old[i]);
+    s[i].x += k0 * delta;
+    s[i].y += k1 * delta;
+    s[i].z += k2 * delta;
+    s[i].w += k3 * delta;
+    o[i] = s[i].x * q0 + s[i].y * q1 + s[i].z * q2 + s[i].w * q3;
+    IO::store(new_state + sbase + (row0 + i) * kD, lane, s[i]);
+  }
+  if constexpr (R == 8) {
+    const float tot = warp_sum8_transposed(o, lane);  // lanes 4 i hold row i's output
+    if ((lane & 3) == 0)
+      out[head * kD + row0 + (lane >> 2)] = __bfloat16_as_ushort(__float2bfloat16_rn(tot));
+  } else {
+#pragma unroll
+    for (int i = 0; i < R; ++i) o[i] = warp_sum(o[i]);
+    if (lane == 0) {
+      uint2 packed;
+      packed.x = pack_bf16x2(o[0], o[1]);
+      packed.y = pack_bf16x2(o[2], o[3]);
+      *reinterpret_cast<uint2 *>(out + head * kD + row0) = packed;
+    }
+  }
+}
+
+// Multi-token decode (speculative verify / MTP): T tokens per request, the
+// same step applied T times in order -- exactly T calls of the single-token
+// kernel above (same fp32 operations in the same order), with the state kept
+// in registers between tokens.  State traffic is that of one step (64 KiB in
+// + 64 KiB out per head); each extra token adds only its vectors.  Because a
+// CTA now lives through T tokens' dependent reductions, each warp owns 8 rows
+// (a CTA 64 rows, 2 CTAs per head): twice the state bytes in flight per CTA
+// and 8 independent reduction chains to interleave, which keeps the kernel
+// on the HBM roofline.  Token t of request r is row r * T + t of the [B*T, ...]
+// inputs and outputs.  `inter` (optional) receives the state after every
+// token, [B, T, 8, 128, 128] fp32, for rolling back rejected tokens.  All T
+// tokens' vectors for the CTA (q, k of its q/k head, v of its 64 rows, a, b:
+// ~0.6 KiB per token) are staged into shared memory in one round trip that
+// overlaps the state loads, so the token loop never waits on global memory.
+constexpr int kMtpRowsPerWarp = 8;
+
 constexpr int kMtpRowsPerCta = kDecWarps * kMtpRowsPerWarp;  // 64
 constexpr int kMtpCtasPerHead = kD / kMtpRowsPerCta;         // 2
 
+template <bool kBf16State>
 __global__ void __launch_bounds__(kDecWarps * 32, 4)
 gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
-                      const uint16_t *__restrict__ v, const float *state,
+                      const uint16_t *__restrict__ v,
+                      const typename StateIO<kBf16State>::T *state,
                       const float *__restrict__ A_log, const uint16_t *__restrict__ a,
                       const float *__restrict__ dt_bias, const uint16_t *__restrict__ b,
-                      float scale, int T, uint16_t *__restrict__ out, float *new_state,
-                      float *__restrict__ inter, const int32_t *__restrict__ slots,
-                      int64_t pool_slots) {
+                      float scale, int T, uint16_t *__restrict__ out,
+                      typename StateIO<kBf16State>::T *new_state,
+                      typename StateIO<kBf16State>::T *__restrict__ inter,
+                      const int32_t *__restrict__ slots, int64_t pool_slots) {
+  using IO = StateIO<kBf16State>;
   constexpr int R = kMtpRowsPerWarp;
   const int64_t head = blockIdx.x / kMtpCtasPerHead;  // request * 8 + v-head
   const int part = blockIdx.x % kMtpCtasPerHead;
@@ -195,7 +261,7 @@ gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict
 #pragma unroll
   for (int i = 0; i < R; ++i) {
     if (state != nullptr) {
-      s[i] = __ldcs(reinterpret_cast<const float4 *>(state + sbase + (row0 + i) * kD) + lane);
+      s[i] = IO::load(state + sbase + (row0 + i) * kD, lane);
     } else {
       s[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -266,9 +332,10 @@ gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict
       s[i].z += k2 * delta;
       s[i].w += k3 * delta;
       o[i] = s[i].x * q0 + s[i].y * q1 + s[i].z * q2 + s[i].w * q3;
-      if (inter != nullptr)
-        __stcs(reinterpret_cast<float4 *>(inter + ((tok * kHV + hv) * kD + row0 + i) * kD) + lane,
-               s[i]);
+      if (inter != nullptr) IO::store(inter + ((tok * kHV + hv) * kD + row0 + i) * kD, lane, s[i]);
+      // a bf16 state carries its rounded value into the next token, as T
+      // separate steps would (the output above used the unrounded update)
+      s[i] = IO::round(s[i]);
     }
     {
       // lanes 4 i hold row i's output
@@ -279,8 +346,7 @@ gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict
     }
   }
 #pragma unroll
-  for (int i = 0; i < R; ++i)
-    __stcs(reinterpret_cast<float4 *>(new_state + sbase + (row0 + i) * kD) + lane, s[i]);
+  for (int i = 0; i < R; ++i) IO::store(new_state + sbase + (row0 + i) * kD, lane, s[i]);
 }
 
 cudaError_t launch_decode_mtp(const void *q, const void *k, const void *v, const float *state,
@@ -291,11 +357,39 @@ cudaError_t launch_decode_mtp(const void *q, const void *k, const void *v, const
   if (batch == 0) return cudaSuccess;
   const int64_t blocks = batch * kHV * kMtpCtasPerHead;
   const size_t smem = static_cast<size_t>(num_tokens) * (80 * sizeof(uint2) + 2 * sizeof(uint16_t));
-  gdn_decode_mtp_kernel<<<static_cast<unsigned>(blocks), kDecWarps * 32, smem, stream>>>(
+  gdn_decode_mtp_kernel<false><<<static_cast<unsigned>(blocks), kDecWarps * 32, smem, stream>>>(
       static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
       static_cast<const uint16_t *>(v), state, A_log, static_cast<const uint16_t *>(a), dt_bias,
       static_cast<const uint16_t *>(b), scale, num_tokens, static_cast<uint16_t *>(out),
       new_state, inter, slots, pool_slots);
+  return cudaGetLastError();
+}
+
+// bf16 state variant: T >= 1 tokens, state (dense [B,8,128,128] or a pool with
+// slots) updated in place in bf16.
+cudaError_t launch_decode_bf16_state(const void *q, const void *k, const void *v, void *state,
+                                     const float *A_log, const void *a, const float *dt_bias,
+                                     const void *b, float scale, int64_t batch, int num_tokens,
+                                     void *out, const int32_t *slots, int64_t pool_slots,
+                                     cudaStream_t stream) {
+  if (batch == 0) return cudaSuccess;
+  uint16_t *st = static_cast<uint16_t *>(state);
+  if (num_tokens == 1) {
+    const int64_t blocks = batch * kHV * (kD / (kDecWarps * 8));
+    gdn_decode_kernel<true, 8><<<static_cast<unsigned>(blocks), kDecWarps * 32, 0, stream>>>(
+        static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
+        static_cast<const uint16_t *>(v), st, A_log, static_cast<const uint16_t *>(a), dt_bias,
+        static_cast<const uint16_t *>(b), scale, static_cast<uint16_t *>(out), st, slots,
+        pool_slots);
+    return cudaGetLastError();
+  }
+  const int64_t blocks = batch * kHV * kMtpCtasPerHead;
+  const size_t smem = static_cast<size_t>(num_tokens) * (80 * sizeof(uint2) + 2 * sizeof(uint16_t));
+  gdn_decode_mtp_kernel<true><<<static_cast<unsigned>(blocks), kDecWarps * 32, smem, stream>>>(
+      static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
+      static_cast<const uint16_t *>(v), st, A_log, static_cast<const uint16_t *>(a), dt_bias,
+      static_cast<const uint16_t *>(b), scale, num_tokens, static_cast<uint16_t *>(out), st,
+      nullptr, slots, pool_slots);
   return cudaGetLastError();
 }
 
@@ -306,7 +400,8 @@ cudaError_t launch_decode(const void *q, const void *k, const void *v, const flo
                           cudaStream_t stream) {
   if (batch == 0) return cudaSuccess;
   const int64_t blocks = batch * kHV * kDecCtasPerHead;
-  gdn_decode_kernel<<<static_cast<unsigned>(blocks), kDecWarps * 32, 0, stream>>>(
+  gdn_decode_kernel<false, kDecRowsPerWarp><<<static_cast<unsigned>(blocks), kDecWarps * 32, 0,
+                                              stream>>>(
       static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
       static_cast<const uint16_t *>(v), state, A_log, static_cast<const uint16_t *>(a), dt_bias,
       static_cast<const uint16_t *>(b), scale, static_cast<uint16_t *>(out), new_state, slots,

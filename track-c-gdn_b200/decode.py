@@ -182,3 +182,49 @@ def run_pool(q, k, v, state_pool, slots, A_log, a, dt_bias, b, scale,
         b.contiguous().data_ptr(), _scale(scale), B, T, output.data_ptr(), stream)
     _native.check(st, "gdn_decode_pool_qk4_v8_d128_k_last")
     return output
+
+
+# ---------------------------------------------------------------------------
+# bf16 state storage; no counterpart in the reference (fp32 state only)
+# ---------------------------------------------------------------------------
+@torch.no_grad()
+def run_bf16_state(q, k, v, state_bf16, A_log, a, dt_bias, b, scale,
+                   slots: Optional[torch.Tensor] = None, stream: Optional[int] = None):
+    """Decode with the state stored in bf16 and updated in place: computed
+    in fp32 like `run`, the new state rounded to nearest even (after every
+    token when T > 1).  q, k, v, a, b as in `run` ([B,1,...]) or `run_mtp`
+    ([B,T,...]); state_bf16 [B,8,128,128] bf16, or a pool [P,8,128,128]
+    addressed by `slots` ([B] int32).  Returns output [B,T,8,128] bf16."""
+    if q.shape[1] == 1 and q.dim() == 4:
+        _check_inputs(q, k, v, a, b)
+    else:
+        _check_mtp_inputs(q, k, v, a, b)
+    B, T = q.shape[0], q.shape[1]
+    assert state_bf16.dtype == torch.bfloat16 and state_bf16.is_contiguous()
+    assert state_bf16.dim() == 4 and state_bf16.shape[1:] == (HV, D, D)
+    if slots is None:
+        assert state_bf16.shape[0] == B
+    else:
+        assert slots.dtype == torch.int32 and slots.numel() == B and slots.is_cuda
+    output = torch.empty(B, T, HV, D, dtype=q.dtype, device=q.device)
+    decode_bf16_state_into(q.contiguous(), k.contiguous(), v.contiguous(), state_bf16,
+                           _f32(A_log), a.contiguous(), _f32(dt_bias), b.contiguous(), scale,
+                           output, None if slots is None else slots.contiguous(), stream)
+    return output
+
+
+def decode_bf16_state_into(q, k, v, state_bf16, A_log, a, dt_bias, b, scale, out,
+                           slots: Optional[torch.Tensor] = None,
+                           stream: Optional[int] = None) -> None:
+    """Destination-passing form of run_bf16_state (contiguous CUDA tensors,
+    fp32 A_log / dt_bias; state updated in place)."""
+    B, T = q.shape[0], q.shape[1]
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+    st = _native.lib.gdn_decode_bf16_state_qk4_v8_d128_k_last(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), state_bf16.data_ptr(),
+        0 if slots is None else state_bf16.shape[0],
+        None if slots is None else slots.data_ptr(),
+        A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), _scale(scale), B, T,
+        out.data_ptr(), stream)
+    _native.check(st, "gdn_decode_bf16_state_qk4_v8_d128_k_last")
