@@ -48,7 +48,8 @@ const char *gdn_b200_status_string(int status);
  * per-device word and skips the work.  This call copies the word for the
  * current device into *code (stream-ordered, then synchronises `stream`) and
  * clears it.  Codes: 0 none, 1 bad cu_seqlens, 2 wait timeout, 3 a state-pool
- * slot index outside [0, pool_slots) (that request / call is skipped).
+ * slot index outside [0, pool_slots) (that request / call is skipped), 4 a
+ * device-side index check failed (debug build libgdn_b200_debug.so only).
  */
 int gdn_b200_read_device_status(int *code, void *stream);
 

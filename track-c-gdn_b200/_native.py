@@ -7,9 +7,13 @@ point, importing this module raises.  Build it with __graft_entry__.build()
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libgdn_b200.so"
+# GDN_B200_LIBRARY selects another build of the same library (the debug
+# build with device-side index checks, libgdn_b200_debug.so).
+LIB_PATH = Path(os.environ.get("GDN_B200_LIBRARY") or
+                Path(__file__).resolve().parent / "libgdn_b200.so")
 
 # Every symbol the header declares, with (restype, argtypes).
 _P = ctypes.c_void_p

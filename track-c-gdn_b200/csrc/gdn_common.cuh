@@ -16,6 +16,7 @@ constexpr int kChunk = 64;   // prefill chunk length (reference BT = 64)
 constexpr int kDevStatusBadSeqlens = 1;
 constexpr int kDevStatusWaitTimeout = 2;
 constexpr int kDevStatusBadSlot = 3;  // a state-pool slot index out of range
+constexpr int kDevStatusIndexCheck = 4;  // a debug-build index check failed
 
 // Per-device status word (the library is one translation unit, gdn_b200.cu).
 __device__ int g_device_status = 0;
@@ -23,6 +24,20 @@ __device__ int g_device_status = 0;
 __device__ __forceinline__ void set_device_status(int code) {
   atomicCAS(&g_device_status, 0, code);
 }
+
+// Index checks of the debug build (compile with -DGDN_DEBUG_CHECKS, see
+// build.py): a failed check records device status 4 and execution goes on;
+// nothing traps.  In the regular build they compile to nothing.
+#ifdef GDN_DEBUG_CHECKS
+#define GDN_DCHECK(cond)                                          \
+  do {                                                            \
+    if (!(cond)) ::gdn::set_device_status(::gdn::kDevStatusIndexCheck); \
+  } while (0)
+#else
+#define GDN_DCHECK(cond) \
+  do {                   \
+  } while (0)
+#endif
 
 __device__ __forceinline__ float bf16_lo(uint32_t packed) {
   return __uint_as_float(packed << 16);

@@ -60,6 +60,11 @@ using namespace sm100;
 //          outputs; TAIL writes the final state).
 enum ScanItemMode : int { kItemFull = 0, kItemHead, kItemZero, kItemIdent, kItemMid, kItemTail };
 
+// Header written by the metadata kernel: chunk count, error flag, work items
+// of pass 1 and pass 3, and the call's sizes (read by the debug-build index
+// checks).
+enum MetaSlot : int { kMetaChunks = 0, kMetaError, kMetaPass1, kMetaPass3, kMetaN, kMetaT };
+
 // Segmented evaluation is used for at most this many sequences.
 constexpr int kSegMaxSeqs = 16;
 // Scan CTAs that run at once on a B200 (148 SMs x 2 CTAs).
@@ -97,8 +102,8 @@ inline PrefillWs prefill_ws_layout(int64_t T, int64_t N, bool allow_segments = t
   w.seg_max = w.seg_chunks ? N + (w.nt_max + w.seg_chunks - 1) / w.seg_chunks : 0;
   const int64_t n_items = w.seg_chunks ? 3 * w.seg_max : N;
   size_t off = 0;
-  w.meta = off;
-  off = align_up(off + 4 * sizeof(int), 256);
+  w.meta = off;  // kMeta* slots
+  off = align_up(off + 8 * sizeof(int), 256);
   w.chunk_off = off;
   off = align_up(off + (N + 1) * sizeof(int), 256);
   w.seq_order = off;
@@ -186,6 +191,10 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
   __shared__ int s_carry;
   __shared__ int s_nc[kLptMaxSeqs];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    meta[kMetaN] = N;
+    meta[kMetaT] = static_cast<int>(T < 0x7fffffff ? T : 0x7fffffff);
+  }
 
   // state-pool slots (when given) must lie in the pool
   int bad_slot = 0;
@@ -454,9 +463,11 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int2 e = chunk_tab[gchunk];
+  GDN_DCHECK(e.x >= 0 && e.x < meta[kMetaN] && e.y >= 0);
   const int64_t bos = cu[e.x];
   const int64_t t0 = bos + static_cast<int64_t>(e.y) * kChunk;
   const int L = static_cast<int>(lmin(kChunk, cu[e.x + 1] - t0));
+  GDN_DCHECK(L > 0 && t0 + L <= meta[kMetaT]);
 
   uint8_t *qk = smem + kPrepQK;
   uint8_t *pp = smem + kPrepQK;  // P image, written only once A is no longer read
@@ -858,6 +869,10 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const int64_t len = lmin(cu[n + 1] - bos, seg_tokens);
   const int nchunks = static_cast<int>((len + kChunk - 1) / kChunk);
   const int gbase = chunk_off[n] + static_cast<int>(seg_begin / kChunk);
+  GDN_DCHECK(n >= 0 && n < meta[kMetaN] && mode >= kItemFull && mode <= kItemTail);
+  GDN_DCHECK(len >= 0 && bos + len <= meta[kMetaT]);
+  GDN_DCHECK(gbase >= 0 && gbase + nchunks <= chunk_off[n + 1] && chunk_off[n + 1] <= meta[kMetaChunks]);
+  GDN_DCHECK(mode == kItemFull || (seg_off != nullptr && seg_off[n] + seg < seg_off[n + 1]));
   const bool ident = mode == kItemIdent;
   const bool write_out = mode == kItemFull || mode == kItemHead || mode == kItemMid ||
                          mode == kItemTail;
