@@ -1,13 +1,13 @@
 """Benchmark of the B200 GDN kernel pair (qk4_v8_d128_k_last).
 
-Default workload ("mixed serving load"): one serving step
+Default workload (benchmark config 4, "mixed serving load"): one serving step
 = a decode step for 4096 requests (state updated in place, resident in HBM)
 plus a ragged prefill of 256 new sequences with lengths ~U{512..8192}
 (~1.1M tokens, zero initial state), followed, when N > 1, by the NCCL gather
 to rank 0 of the decode outputs and prefill final states.  The work is a
 fixed total sharded across the N ranks (decode: request blocks; prefill: LPT
 bin packing by sequence), so scaling is "strong".  All inputs are seeded
-synthetic tensors with the BASELINE value distributions.
+synthetic tensors with the benchmark configs' value distributions.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference|triton]
                     [--workload c4|c2|c3|decode|mtp|decode_bf16]
@@ -444,7 +444,7 @@ def gpu_arm(args):
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded; BASELINE value distributions)",
+        "data": "synthetic (seeded; the benchmark configs' value distributions)",
         "config": {
             "workload": wl["desc"],
             "decode_batch": B_total,

@@ -1,6 +1,6 @@
 """Seeded input generators and digests shared by the golden-vector script and tests.
 
-Inputs follow the value distributions of the BASELINE configs: q/k
+Inputs follow the value distributions of the benchmark configs: q/k
 L2-normalised randn, v randn, state randn*0.02, A_log ~ U(0, 2.7),
 a, b ~ N(0, 1), dt_bias ~ N(0, 0.1), all drawn from numpy's PCG64 so that
 fixtures can be regenerated bit-for-bit.  bf16 tensors are carried as uint16
@@ -107,7 +107,7 @@ def state_digest(S: np.ndarray) -> dict:
 # Golden cases: name -> (kind, kwargs).  Kept small: the reference runs under
 # the Triton interpreter to produce them.
 DECODE_CASES = {
-    # BASELINE config 0 shapes: batch 16, state randn*0.02
+    # benchmark config 0 shapes: batch 16, state randn*0.02
     "decode_c0_b16": dict(seed=0, B=16, with_state=True),
     "decode_b1_nostate": dict(seed=1, B=1, with_state=False),
     "decode_b3_scale05": dict(seed=2, B=3, with_state=True, scale=0.5),

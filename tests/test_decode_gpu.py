@@ -1,7 +1,7 @@
 """Decode parity on the GPU: the sm_100a kernel (through the C ABI) against the
 reference's golden vectors and the CPU oracle.
 
-Tolerances (stated per the BASELINE contract): outputs are bf16, compared
+Tolerances (stated per the benchmark definition): outputs are bf16, compared
 after rounding with |d| <= 2e-3 + 1e-2 |ref| (and within one bf16 ulp of the
 reference's own output); the fp32 state must agree with the fp32 oracle to
 <= 1e-5 relative Frobenius (both are fp32 evaluations of the same step).

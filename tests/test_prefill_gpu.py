@@ -2,7 +2,7 @@
 against the fp32 recurrence oracle, the reference's golden vectors, and
 size-independent properties at full sizes.
 
-Tolerances (stated per the BASELINE contract):
+Tolerances (stated per the benchmark definition):
   * outputs (bf16): |d| <= 2e-3 + 1e-2 |ref| against the fp32 recurrence;
   * final state (fp32): relative Frobenius error <= 5e-3 against the fp32
     recurrence.  The reference's own chunked kernel (bf16 w/u/h/v_new
@@ -80,7 +80,7 @@ def test_prefill_many_sequences_wide_path(gdn):
 
 
 def test_prefill_config_c2_t4096(gdn):
-    """BASELINE config: one packed sequence T=4096, zero initial state."""
+    """Benchmark config 2: one packed sequence T=4096, zero initial state."""
     inp = cases.prefill_inputs(seed=0, lens=[4096], with_state=False)
     o, s = _run(gdn, inp)
     ro, rs = _oracle(inp)

@@ -1,5 +1,5 @@
 """Our kernels against the reference's own Triton kernels on the GPU, on the
-same inputs, at sizes the CPU interpreter cannot reach (BASELINE configs 2-4
+same inputs, at sizes the CPU interpreter cannot reach (benchmark configs 2-4
 shapes).  Needs the reference's Triton solutions staged unmodified under
 baseline/_ref/<definition>/solution/triton/kernel.py (the reference is not
 pip-installable); skipped when they are absent.
