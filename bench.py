@@ -3,8 +3,10 @@
 Default workload (benchmark config 4, "mixed serving load"): one serving step
 = a decode step for 4096 requests (state updated in place, resident in HBM)
 plus a ragged prefill of 256 new sequences with lengths ~U{512..8192}
-(~1.1M tokens, zero initial state), followed, when N > 1, by the NCCL gather
-to rank 0 of the decode outputs and prefill final states.  The work is a
+(~1.1M tokens, zero initial state).  When N > 1 the decode outputs and
+prefill final states end the step on rank 0: each rank's kernels store them
+into rank 0's memory over NVLink (default, `--gather peer`), or an NCCL
+gather runs after the compute (`--gather nccl`).  The work is a
 fixed total sharded across the N ranks (decode: request blocks; prefill: LPT
 bin packing by sequence), so scaling is "strong".  All inputs are seeded
 synthetic tensors with the benchmark configs' value distributions.
@@ -335,6 +337,29 @@ def gpu_arm(args):
     dec_out = torch.empty(B, Tdec, HV, D, dtype=torch.bfloat16, device=dev) if B > 0 else None
     max_seqs = max(seq_counts) if seq_counts else 0
     max_dec = math.ceil(B_total / world) if B_total else 0
+
+    # N > 1: the step's results (decode outputs, prefill final states) land on
+    # rank 0.  With --gather peer every rank's kernels store them straight
+    # into rank 0's rank-major buffers (CUDA IPC mapping, plain stores over
+    # NVLink while the step computes) and one 4-byte all-reduce closes the
+    # step; with --gather nccl (or if any rank cannot map) an NCCL gather
+    # runs after the compute.
+    dec_peer = fin_peer = None
+    gather_mode = "none" if world == 1 else args.gather
+    if world > 1 and args.gather == "peer":
+        try:
+            if B_total:
+                dec_peer = shard.PeerResult(
+                    [len(range(B_total)[shard.block_partition(B_total, world, r)])
+                     for r in range(world)], (Tdec, HV, D), torch.bfloat16, dev)
+            if wl["prefill"]:
+                fin_peer = shard.PeerResult(seq_counts, (HV, D, D), torch.float32, dev)
+        except RuntimeError as e:
+            if dec_peer is not None:
+                dec_peer.close()
+            dec_peer = fin_peer = None
+            gather_mode = f"nccl (peer mapping failed: {e})"
+    peer = dec_peer or fin_peer
     total_tokens = B_total * Tdec + total_prefill_tokens
     stream = torch.cuda.current_stream(dev)
 
@@ -347,9 +372,12 @@ def gpu_arm(args):
     side = torch.cuda.Stream(dev) if overlap else stream
     ev["dside"] = []
 
+    dec_dst = dec_peer.rows_for_me() if dec_peer is not None else dec_out
+    fin_dst = fin_peer.rows_for_me() if fin_peer is not None else (pre["final"] if pre else None)
+
     def decode():
         with torch.cuda.stream(side):
-            run_decode(gdn, dec, A_log, dt_bias, dec_out)
+            run_decode(gdn, dec, A_log, dt_bias, dec_dst)
 
     def step(record):
         if record:
@@ -367,7 +395,7 @@ def gpu_arm(args):
         if pre is not None and pre["N"] > 0:
             gdn.prefill.prefill_into(pre["q"], pre["k"], pre["v"], pre["h0"], A_log, pre["a"],
                                      dt_bias, pre["b"], pre["cu"], None, pre["out"],
-                                     pre["final"], pre["ws"])
+                                     fin_dst, pre["ws"])
         if overlap:
             # issued after the prefill, so its CTAs take the SMs the prefill's
             # kernels leave free (their tails and the gaps between them)
@@ -381,7 +409,9 @@ def gpu_arm(args):
             e = torch.cuda.Event(enable_timing=True)
             e.record(stream)
             ev["p"].append(e)
-        if world > 1:
+        if peer is not None:
+            peer.publish()  # one all-reduce closes the step for both buffers (same group, stream)
+        elif world > 1:
             if dec_out is not None or max_dec:
                 t = dec_out if dec_out is not None else torch.empty(0, Tdec, HV, D, dtype=torch.bfloat16, device=dev)
                 shard.gather_padded(t, max_dec)
@@ -457,8 +487,12 @@ def gpu_arm(args):
             "streams": ("decode on a side stream next to the prefill, joined each step" if overlap
                         else "one stream (decode, then prefill)"),
             "parallelism": f"shard{world}: decode request blocks, prefill LPT by sequence; "
-                           + ("NCCL gather of decode outputs + prefill final states to rank 0"
+                           + ("kernels store decode outputs + prefill final states into rank 0's "
+                              "buffers over NVLink (CUDA IPC), one 4-byte all-reduce per step"
+                              if peer is not None else
+                              "NCCL gather of decode outputs + prefill final states to rank 0"
                               if world > 1 else "no collective"),
+            "gather": gather_mode,
         },
         "gpu_launches": args.steps * ((1 if dec is not None else 0) +
                                       (gdn._native.prefill_kernel_launches(pre["T"], pre["N"]) if pre else 0)),
@@ -497,6 +531,9 @@ def gpu_arm(args):
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_seconds)
+    for res in (dec_peer, fin_peer):
+        if res is not None:
+            res.close()
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -921,6 +958,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="device step only (profiling runs)")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: kernels store results into rank 0's memory (peer) or an NCCL "
+                         "gather runs after the compute (nccl)")
     ap.add_argument("--overlap", choices=["on", "off"], default="off",
                     help="run decode on a side stream next to the prefill (C4)")
     args = ap.parse_args()

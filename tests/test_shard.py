@@ -136,3 +136,88 @@ def test_rank_failure_surfaces_as_error_gloo():
         if p.is_alive():
             p.kill()
     assert res != "no error"
+
+
+# ---- results written in place across GPUs (PeerResult), host logic ----
+def test_row_offsets():
+    assert shard.row_offsets([3, 0, 5]) == [0, 3, 3, 8]
+    assert shard.row_offsets([]) == [0]
+    with pytest.raises(ValueError):
+        shard.row_offsets([1, -1])
+
+
+class _FakeIpc:
+    """Stands in for CUDA IPC on CPU: the export is a fixed handle and
+    offset, the mapping a fixed address; failing_rank's open raises."""
+    HANDLE = bytes(range(64))
+    OFFSET = 1024
+    MAPPED = 1 << 40
+
+    def __init__(self, failing_rank=None):
+        self.failing_rank = failing_rank
+        self.closed = []
+
+    def export(self, ptr):
+        return self.HANDLE, self.OFFSET
+
+    def open(self, handle, device):
+        assert handle == self.HANDLE
+        if dist.get_rank() == self.failing_rank:
+            raise OSError("mapping refused")
+        return self.MAPPED
+
+    def close(self, ptr):
+        self.closed.append(ptr)
+
+
+def _peer_protocol_worker(rank, world, port, failing_rank, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ipc = _FakeIpc(failing_rank)
+        rows = [3, 5, 0][:world]
+        try:
+            res = shard.PeerResult(rows, (2, 4), torch.float32, torch.device("cpu"), ipc=ipc)
+        except RuntimeError as e:
+            q.put((rank, "raised", str(e)))
+            return
+        row_bytes = 2 * 4 * 4
+        mine = res.rows_for_me().data_ptr()
+        if rank == 0:
+            ok = mine == res.tensor().data_ptr() and tuple(res.tensor().shape) == (8, 2, 4)
+        else:
+            ok = mine == _FakeIpc.MAPPED + _FakeIpc.OFFSET + res.offsets[rank] * row_bytes
+        res.publish()
+        res.close()
+        ok = ok and ipc.closed == ([] if rank == 0 else [_FakeIpc.MAPPED])
+        q.put((rank, "ok" if ok else "bad addresses", None))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_peer_protocol(world, failing_rank):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_protocol_worker, args=(r, world, port, failing_rank, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return res
+
+
+def test_peer_result_addresses_and_close_gloo():
+    res = _run_peer_protocol(3, None)
+    assert [r[1] for r in res] == ["ok"] * 3
+
+
+def test_peer_result_mapping_failure_raises_on_every_rank_gloo():
+    # one rank cannot map the buffer: every rank raises, none is left waiting
+    res = _run_peer_protocol(2, failing_rank=1)
+    assert [r[1] for r in res] == ["raised", "raised"]
+    assert all("1 rank(s)" in r[2] for r in res)

@@ -819,6 +819,8 @@ struct ScanSmem {
   static constexpr uint32_t kTmemCols = 256;
   static constexpr uint32_t kColSb = 0, kColOi = 64, kColY = 128;
 };
+// the epilogue stages one 64 KB (n, hv) state over the Q, K and [PA;Ainv] tiles
+static_assert(ScanSmem::kQ == 0 && ScanSmem::kXV >= 65536, "state staging region");
 
 // Writes 16 fp32 as bf16 into row `row`, 16-byte chunks c0, c0+1 of a
 // 128-byte swizzled operand.
@@ -1220,10 +1222,27 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     chunk_loop(std::false_type{});
 
   if (fin != nullptr) {
+    // The (n, hv) state is one contiguous 64 KB block.  It goes out through
+    // shared memory so that each warp store covers 512 contiguous bytes (one
+    // state row) rather than 16 bytes of 32 rows: the same bytes, but whole
+    // lines, which is what matters when `fin` is another GPU's memory and
+    // every store crosses NVLink as its own request.  The Q/K/[PA;Ainv] tiles
+    // (first 64 KB) are free: every MMA and TMA load has completed.  Chunk c
+    // of row r is kept at c ^ (r & 7), conflict-free on both sides.
+    float4 *stage = reinterpret_cast<float4 *>(smem + SM::kQ);
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      *reinterpret_cast<float4 *>(fin + srow + 4 * i) =
+    for (int i = 0; i < 16; ++i) {
+      const int c = 16 * hc + i;
+      stage[vrow * 32 + (c ^ (vrow & 7))] =
           make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+    }
+    __syncthreads();
+    float4 *dst = reinterpret_cast<float4 *>(fin);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int j = kScanThreads * i + tid, r = j >> 5, c = j & 31;
+      dst[j] = stage[r * 32 + (c ^ (r & 7))];
+    }
   }
 
   tc_fence_before();

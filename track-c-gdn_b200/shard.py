@@ -107,3 +107,172 @@ def unpad_gathered(stacked: torch.Tensor, counts: Sequence[int], order: Sequence
             idx = torch.as_tensor(np.asarray(ids, np.int64), device=stacked.device)
             out[idx] = stacked[r, :cnt]
     return out
+
+
+# ---------------------------------------------------------------------------
+# Results written in place across GPUs (replaces the gather)
+# ---------------------------------------------------------------------------
+def row_offsets(rows: Sequence[int]) -> List[int]:
+    """Start row of each rank's block in a rank-major result (len world + 1)."""
+    off = [0]
+    for r in rows:
+        if r < 0:
+            raise ValueError("row counts must be >= 0")
+        off.append(off[-1] + int(r))
+    return off
+
+
+class DeviceRows:
+    """A device address handed to the destination-passing entry points
+    (`decode_into`, `prefill_into`, ...), which read only `data_ptr()`."""
+
+    def __init__(self, ptr: int):
+        self._ptr = int(ptr)
+
+    def data_ptr(self) -> int:
+        return self._ptr
+
+
+class CudaIpc:
+    """CUDA IPC through the driver API (cuda-python): export the allocation
+    that holds a pointer, map a peer's export into the current context with
+    lazy peer access.  The current context must be the caller's GPU."""
+
+    def __init__(self):
+        from cuda.bindings import driver
+        self._drv = driver
+
+    def _ok(self, res, what):
+        err, *vals = res
+        if err != self._drv.CUresult.CUDA_SUCCESS:
+            raise RuntimeError(f"{what} failed: {err}")
+        return vals[0] if len(vals) == 1 else vals
+
+    def export(self, ptr: int):
+        base, _ = self._ok(self._drv.cuMemGetAddressRange(ptr), "cuMemGetAddressRange")
+        handle = self._ok(self._drv.cuIpcGetMemHandle(base), "cuIpcGetMemHandle")
+        return bytes(handle.reserved), ptr - int(base)
+
+    def open(self, handle: bytes, device: int) -> int:
+        dev = self._ok(self._drv.cuCtxGetDevice(), "cuCtxGetDevice")
+        if int(dev) != device:
+            raise RuntimeError(f"current CUDA context is on device {int(dev)}, not {device}")
+        h = self._drv.CUipcMemHandle()
+        h.reserved = handle
+        flags = self._drv.CUipcMem_flags.CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS
+        return int(self._ok(self._drv.cuIpcOpenMemHandle(h, flags), "cuIpcOpenMemHandle"))
+
+    def close(self, ptr: int) -> None:
+        self._ok((self._drv.cuIpcCloseMemHandle(ptr)[0], None), "cuIpcCloseMemHandle")
+
+
+class PeerResult:
+    """A step result that lives on rank `dst` and that every rank writes in
+    place, so no gather runs after the step.
+
+    `dst` allocates the rank-major buffer [sum(rows), *row_shape] (rank r's
+    rows start at row_offsets(rows)[r]) and sends its CUDA IPC handle to the
+    group; every other rank maps it with lazy peer access.  A rank passes
+    `rows_for_me()` as the destination of its decode or prefill call, and the
+    kernels' stores cross NVLink while the rest of the step still computes.
+    `publish()` closes a step: a 4-byte all-reduce on the current stream
+    (NCCL), or a device sync and a barrier (other backends).  Each rank joins
+    it after its kernels, so once it returns on `dst`, every rank's kernels
+    have finished and their stores are in `tensor()`; and no rank writes the
+    next step's rows before `dst` has reached the same point.
+
+    Only plain stores reach the peer memory (no TMA, no multicast).  Call
+    `close()` on every rank before the process group goes away."""
+
+    def __init__(self, rows: Sequence[int], row_shape: Sequence[int], dtype: torch.dtype,
+                 device: torch.device, group=None, dst: int = 0, ipc=None):
+        import torch.distributed as dist
+
+        self._dist, self._group, self.dst = dist, group, dst
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if len(rows) != self.world:
+            raise ValueError(f"{len(rows)} row counts for a world of {self.world}")
+        self.offsets = row_offsets(rows)
+        self.row_shape = tuple(int(x) for x in row_shape)
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.row_bytes = int(np.prod(self.row_shape, dtype=np.int64)) * torch.empty(
+            0, dtype=dtype).element_size()
+        self._ipc = ipc if ipc is not None else CudaIpc()
+        self._sync()  # the device's context exists and is current before any mapping
+        self._mapped = None
+        self._buf = None
+        total = self.offsets[-1]
+        payload = [None]
+        if self.rank == dst:
+            self._buf = torch.empty((max(total, 1),) + self.row_shape, dtype=dtype,
+                                    device=self.device)
+            payload = [self._ipc.export(self._buf.data_ptr())]
+        dist.broadcast_object_list(payload, src=dst, group=group,
+                                   device=self.device if self._nccl() else None)
+        error = None
+        if self.rank == dst:
+            self._base = self._buf.data_ptr()
+        else:
+            handle, offset = payload[0]
+            try:
+                self._mapped = self._ipc.open(handle, self.device.index or 0)
+                self._base = self._mapped + offset
+            except Exception as e:  # noqa: BLE001 -- reported on every rank below
+                error = f"rank {self.rank}: {e}"
+        # every rank learns whether all mappings succeeded, so that all of
+        # them raise (or none does) and their collectives stay in step
+        self._flag = torch.zeros(1, dtype=torch.int32,
+                                 device=self.device if self._nccl() else "cpu")
+        self._flag.fill_(0 if error is None else 1)
+        dist.all_reduce(self._flag, group=group)
+        if int(self._flag.item()) != 0:
+            if self._mapped is not None:
+                self._ipc.close(self._mapped)
+                self._mapped = None
+            self._buf = None
+            raise RuntimeError("peer mapping of the result buffer failed on "
+                               f"{int(self._flag.item())} rank(s)" + (f" ({error})" if error else ""))
+        if not self._nccl():
+            self._flag = None
+
+    def _nccl(self) -> bool:
+        return self._dist.get_backend(self._group) == "nccl"
+
+    def rows_for(self, rank: int) -> DeviceRows:
+        """Where `rank`'s first row goes, as an address valid in this process
+        (this rank's own block when rank == self.rank)."""
+        return DeviceRows(self._base + self.offsets[rank] * self.row_bytes)
+
+    def rows_for_me(self) -> DeviceRows:
+        return self.rows_for(self.rank)
+
+    def publish(self) -> None:
+        if self._flag is not None:
+            self._dist.all_reduce(self._flag, group=self._group)
+        else:
+            self._sync()
+            self._dist.barrier(group=self._group)
+
+    def _sync(self) -> None:
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+
+    def tensor(self) -> torch.Tensor:
+        """The whole rank-major result (on `dst` only)."""
+        if self._buf is None:
+            raise RuntimeError("the result lives on rank %d" % self.dst)
+        return self._buf[: self.offsets[-1]]
+
+    def close(self) -> None:
+        """Unmap (all ranks, after their last kernel), then free on `dst`."""
+        self._sync()
+        if self._mapped is not None:
+            self._ipc.close(self._mapped)
+            self._mapped = None
+        if self._nccl():
+            self._dist.barrier(group=self._group, device_ids=[self.device.index])
+        else:
+            self._dist.barrier(group=self._group)
+        self._buf = None
