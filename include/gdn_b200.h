@@ -223,6 +223,37 @@ int gdn_prefill_qk4_v8_d128_k_last_noalloc(
     const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
     float scale, void *out, float *final_state, void *stream);
 
+/*
+ * Backward of the prefill -- no counterpart in the reference, whose prefill
+ * is forward-only (solution/triton/kernel.py:1: "Forward-only").
+ * Gradients of (out, final_state) = gdn_prefill_qk4_v8_d128_k_last(q, k, v,
+ * state, A_log, a, dt_bias, b, cu_seqlens, scale) given
+ *   d_out          [T,8,128] bf16 (16-byte aligned),
+ *   d_final_state  [N,8,128,128] fp32 or NULL (zero),
+ * written as fp32:
+ *   dq, dk [T,4,128]   dv [T,8,128]   da, db [T,8]   dA_log, ddt_bias [8]
+ *   d_state [N,8,128,128] (the initial state's gradient; NULL: not computed).
+ * The inputs are the forward's (state NULL: zero initial state); the call
+ * recomputes the forward's chunk states itself.  dq/dk/dv/d_state/d_final
+ * 16-byte aligned, da/db/dA_log/ddt_bias 4-byte aligned.  The workspace
+ * (1024-byte aligned, gdn_prefill_backward_workspace_bytes(T, N) bytes) holds
+ * the recomputed chunk-start states and their gradients: about
+ * 2 x 512 KiB per 64-token chunk plus 8 KiB per token.  No host
+ * synchronisation; bad cu_seqlens are reported through the device status
+ * (code 1) as in the forward.  Deterministic: identical inputs give
+ * identical gradients bit for bit.
+ */
+size_t gdn_prefill_backward_workspace_bytes(int64_t total_tokens, int64_t num_seqs);
+int gdn_prefill_backward_kernel_launches(void);
+int gdn_prefill_backward_qk4_v8_d128_k_last(
+    const void *q, const void *k, const void *v, const float *state,
+    const float *A_log, const void *a, const float *dt_bias, const void *b,
+    const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+    float scale, const void *d_out, const float *d_final_state,
+    float *dq, float *dk, float *dv, float *da, float *db,
+    float *dA_log, float *ddt_bias, float *d_state,
+    void *workspace, size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,6 +23,8 @@ def test_header_declares_expected_entry_points():
               "gdn_decode_mtp_qk4_v8_d128_k_last", "gdn_prefill_kernel_launches",
               "gdn_decode_pool_qk4_v8_d128_k_last", "gdn_prefill_pool_qk4_v8_d128_k_last",
               "gdn_prefill_workspace_bytes", "gdn_b200_status_string",
+              "gdn_prefill_backward_qk4_v8_d128_k_last",
+              "gdn_prefill_backward_workspace_bytes", "gdn_prefill_backward_kernel_launches",
               "gdn_b200_abi_version", "gdn_b200_read_device_status"):
         assert n in names
 
@@ -132,6 +134,45 @@ def test_mtp_decode_argument_validation_without_device(gdn):
     assert f(ok, ok, ok, st, ok, ok, ok, ok, 0.0, 4, 2, ok, P(0x9000000),
              P(0x1000000 + 1024), None) == 7
     assert f(*base, 4, 2, ok, P(0x9000000), P(0x9000000 + 4096), None) == 7
+
+
+def test_backward_argument_validation_without_device(gdn):
+    lib = gdn._native.lib
+    P = ctypes.c_void_p
+    ok = P(0x10000)
+    f = lib.gdn_prefill_backward_qk4_v8_d128_k_last
+    T, N = 128, 2
+    need = lib.gdn_prefill_backward_workspace_bytes(T, N)
+    assert need > lib.gdn_prefill_workspace_bytes(T, N)
+    # (q, k, v, state, A_log, a, dt_bias, b, cu, N, T, scale, d_out, d_final,
+    #  dq, dk, dv, da, db, dA_log, ddt_bias, d_state, ws, ws_bytes, stream)
+    fwd = [ok, ok, ok, None, ok, ok, ok, ok, ok, N, T, 0.0, ok, None]
+    outs = [ok, ok, ok, ok, ok, ok, ok, None]
+    assert f(*fwd, *outs, ok, 16, None) == 4                    # workspace too small
+    assert f(*fwd, *outs, P(0x10200), need, None) == 4          # workspace misaligned
+    bad = list(outs)
+    bad[0] = None
+    assert f(*fwd, *bad, ok, need, None) == 1                   # no dq
+    bad = list(outs)
+    bad[5] = None
+    assert f(*fwd, *bad, ok, need, None) == 1                   # no dA_log
+    bad = list(fwd)
+    bad[12] = P(0x10008)
+    assert f(*bad, *outs, ok, need, None) == 3                  # misaligned d_out
+    bad = list(fwd)
+    bad[9], bad[10] = -1, T
+    assert f(*bad, *outs, ok, need, None) == 2                  # negative N
+    bad = list(fwd)
+    bad[9], bad[10] = 0, 0
+    assert f(*bad, *outs, ok, need, None) == 0                  # nothing to do
+    # d_state overlapping the initial state
+    st = P(0x1000000)
+    bad = list(fwd)
+    bad[3] = st
+    aliasing = list(outs)
+    aliasing[7] = P(0x1000000 + 4096)
+    assert f(*bad, *aliasing, ok, need, None) == 7
+    assert lib.gdn_prefill_backward_kernel_launches() == 6
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")

@@ -3,5 +3,6 @@
 // as one unit rather than with relocatable device code.
 #include "gdn_decode.cu"
 #include "gdn_prefill.cu"
+#include "gdn_prefill_bwd.cu"
 #include "gdn_capi.cu"
 #include "gdn_prefill_noalloc.cu"

@@ -31,6 +31,15 @@ cudaError_t launch_decode_bf16_state(const void *q, const void *k, const void *v
                                      cudaStream_t stream);
 size_t prefill_workspace_bytes(int64_t T, int64_t N, bool allow_segments);
 int prefill_kernel_launches(int64_t T, int64_t N, bool allow_segments);
+size_t prefill_bwd_workspace_bytes(int64_t T, int64_t N);
+int prefill_bwd_kernel_launches();
+cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, const float *state,
+                               const float *A_log, const void *a, const float *dt_bias,
+                               const void *b, const int64_t *cu_seqlens, int64_t N, int64_t T,
+                               float scale, const void *d_out, const float *d_final, float *dq,
+                               float *dk, float *dv, float *da, float *db, float *dA_log,
+                               float *ddt_bias, float *d_state, void *workspace,
+                               cudaStream_t stream);
 cudaError_t launch_prefill(const void *q, const void *k, const void *v, const float *state,
                            const float *A_log, const void *a, const float *dt_bias, const void *b,
                            const int64_t *cu_seqlens, int64_t N, int64_t T, float scale,
@@ -166,6 +175,51 @@ size_t gdn_prefill_workspace_bytes(int64_t total_tokens, int64_t num_seqs) {
 int gdn_prefill_kernel_launches(int64_t total_tokens, int64_t num_seqs) {
   if (total_tokens < 0 || num_seqs < 0) return 0;
   return gdn::prefill_kernel_launches(total_tokens, num_seqs, true);
+}
+
+size_t gdn_prefill_backward_workspace_bytes(int64_t total_tokens, int64_t num_seqs) {
+  if (total_tokens < 0 || num_seqs < 0) return 0;
+  return gdn::prefill_bwd_workspace_bytes(total_tokens, num_seqs);
+}
+
+int gdn_prefill_backward_kernel_launches(void) { return gdn::prefill_bwd_kernel_launches(); }
+
+int gdn_prefill_backward_qk4_v8_d128_k_last(
+    const void *q, const void *k, const void *v, const float *state, const float *A_log,
+    const void *a, const float *dt_bias, const void *b, const int64_t *cu_seqlens,
+    int64_t num_seqs, int64_t total_tokens, float scale, const void *d_out,
+    const float *d_final_state, float *dq, float *dk, float *dv, float *da, float *db,
+    float *dA_log, float *ddt_bias, float *d_state, void *workspace, size_t workspace_bytes,
+    void *stream) {
+  if (num_seqs < 0 || total_tokens < 0 || total_tokens > (int64_t{1} << 31) ||
+      num_seqs > (int64_t{1} << 24))
+    return GDN_ERR_BAD_SIZE;
+  if (num_seqs == 0) return total_tokens == 0 ? GDN_OK : GDN_ERR_BAD_SIZE;
+  if (!cu_seqlens || !A_log || !dt_bias || !dA_log || !ddt_bias || !workspace)
+    return GDN_ERR_NULL_POINTER;
+  if (total_tokens > 0 &&
+      (!q || !k || !v || !a || !b || !d_out || !dq || !dk || !dv || !da || !db))
+    return GDN_ERR_NULL_POINTER;
+  const void *a16[] = {q, k, v, d_out, dq, dk, dv, state, d_final_state, d_state};
+  for (const void *p : a16)
+    if (p && !aligned(p, 16)) return GDN_ERR_MISALIGNED;
+  if ((da && !aligned(da, 4)) || (db && !aligned(db, 4)) || !aligned(dA_log, 4) ||
+      !aligned(ddt_bias, 4) || !aligned(cu_seqlens, 8))
+    return GDN_ERR_MISALIGNED;
+  if (!aligned(workspace, 1024) ||
+      workspace_bytes < gdn::prefill_bwd_workspace_bytes(total_tokens, num_seqs))
+    return GDN_ERR_WORKSPACE;
+  const size_t state_bytes = static_cast<size_t>(num_seqs) * gdn::kHV * gdn::kD * gdn::kD * 4;
+  if (d_state && ((state && overlap(state, state_bytes, d_state, state_bytes)) ||
+                  (d_final_state && overlap(d_final_state, state_bytes, d_state, state_bytes))))
+    return GDN_ERR_ALIASING;
+  if (int st = check_device(nullptr)) return st;
+  if (scale == 0.0f) scale = kDefaultScale;
+  cudaError_t err = gdn::launch_prefill_bwd(
+      q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens, scale, d_out,
+      d_final_state, dq, dk, dv, da, db, dA_log, ddt_bias, d_state, workspace,
+      static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
 int gdn_prefill_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,

@@ -838,6 +838,12 @@ __device__ __forceinline__ void store16_bf16(uint8_t *base, int row, int c0, con
   *reinterpret_cast<uint4 *>(base + sw128(row, c0 + 1)) = b;
 }
 
+// kSave = true is the backward pass's recompute: FULL items only, no outputs
+// and no final state; instead the state at the start of every chunk goes to
+// save_states[(global chunk) * 8 + hv] (fp32 [128 v][128 k]) and each token's
+// delta (V_new, the v-vector the WY system solves for) to
+// save_delta[(token * 8 + hv) * 128 + v] (fp32).
+template <bool kSave>
 __global__ void __launch_bounds__(kScanThreads, 2)
 gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         const __grid_constant__ CUtensorMap tmap_k,
@@ -849,7 +855,8 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         uint16_t *__restrict__ out, float *final_state,
                         const int4 *__restrict__ items, int count_slot, int64_t seg_tokens,
                         const int *__restrict__ seg_off, float *seg_ss, float *seg_sb,
-                        float *seg_phi, const int32_t *__restrict__ slots) {
+                        float *seg_phi, const int32_t *__restrict__ slots,
+                        float *__restrict__ save_states, float *__restrict__ save_delta) {
   using SM = ScanSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_align<1024>(smem_raw);
@@ -892,7 +899,9 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   else if (mode == kItemMid || mode == kItemTail)
     init = seg_state(seg_ss, seg);
   float *fin = nullptr;
-  if (mode == kItemFull || mode == kItemTail)
+  if (kSave)
+    fin = nullptr;
+  else if (mode == kItemFull || mode == kItemTail)
     fin = final_state + sidx * kHV * kD * kD + hv_off;
   else if (mode == kItemHead)
     fin = seg_state(seg_ss, 1);
@@ -915,7 +924,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 
   // Items without outputs (ZERO, IDENT) need neither Q nor the Q-side MMAs;
   // IDENT treats V as zero and needs no V either.
-  const bool need_q = write_out;
+  const bool need_q = write_out && !kSave;
   const bool need_v = !ident;
 
   // Chunk operand loads, all issued by thread 0.
@@ -1031,6 +1040,13 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const uint32_t bar_k = bar_k0 + 8 * cb;
       GateRegs next_gates;
       if (tid < 64 && c + 1 < nchunks) next_gates = fetch_gates(c + 1);
+      if constexpr (kSave) {
+        float *dst = save_states + static_cast<int64_t>(gbase + c) * kHV * kD * kD + hv_off + srow;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          *reinterpret_cast<float4 *>(dst + 4 * i) =
+              make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+      }
 
       // Q, K and [PA;Ainv] are read only by the tensor core, so only the MMA
       // thread waits for them: thread 0 re-arms each barrier for the next chunk
@@ -1166,6 +1182,13 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         float zv[16];
         tmem_ld16(tlane + SM::kColY + 64 + tb, zv);
         tmem_wait_ld();
+        if constexpr (kSave) {
+          // thread (vrow, hc) holds V_new[vrow][tb .. tb+15]; a warp's store
+          // for one token covers 32 consecutive v (128 B)
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (tb + j < L) save_delta[((t0 + tb + j) * kHV + hv) * kD + vrow] = zv[j];
+        }
   #pragma unroll
         for (int g = 0; g < 4; ++g) {
           const float4 ed4 = *reinterpret_cast<const float4 *>(Ed + cb * 64 + tb + 4 * g);
@@ -1216,7 +1239,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tc_fence_after();
     }
   };
-  if (write_out)
+  if (write_out && !kSave)
     chunk_loop(std::true_type{});
   else
     chunk_loop(std::false_type{});
@@ -1453,15 +1476,16 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
   }
-  err = cudaFuncSetAttribute(gdn_prefill_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             ScanSmem::kBytes);
+  err = cudaFuncSetAttribute(gdn_prefill_scan_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, ScanSmem::kBytes);
   if (err != cudaSuccess) return err;
   // pass 1 (the only pass without segmentation)
   const int64_t n1 = w.seg_chunks ? 2 * w.seg_max : N;
-  gdn_prefill_scan_kernel<<<static_cast<unsigned>(n1 * kHV), kScanThreads, ScanSmem::kBytes,
-                            stream>>>(tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta,
-                                      m2, scale, static_cast<uint16_t *>(out), final_state, items,
-                                      2, seg_tokens, seg_off, seg_ss, seg_sb, seg_phi, slots);
+  gdn_prefill_scan_kernel<false><<<static_cast<unsigned>(n1 * kHV), kScanThreads,
+                                   ScanSmem::kBytes, stream>>>(
+      tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale,
+      static_cast<uint16_t *>(out), final_state, items, 2, seg_tokens, seg_off, seg_ss, seg_sb,
+      seg_phi, slots, nullptr, nullptr);
   err = cudaGetLastError();
   if (err != cudaSuccess || w.seg_chunks == 0) return err;
 
@@ -1474,11 +1498,11 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   // pass 3
-  gdn_prefill_scan_kernel<<<static_cast<unsigned>(w.seg_max * kHV), kScanThreads,
-                            ScanSmem::kBytes, stream>>>(
+  gdn_prefill_scan_kernel<false><<<static_cast<unsigned>(w.seg_max * kHV), kScanThreads,
+                                   ScanSmem::kBytes, stream>>>(
       tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale,
       static_cast<uint16_t *>(out), final_state, items + 2 * w.seg_max, 3, seg_tokens, seg_off,
-      seg_ss, seg_sb, seg_phi, slots);
+      seg_ss, seg_sb, seg_phi, slots, nullptr, nullptr);
   return cudaGetLastError();
 }
 

@@ -146,3 +146,109 @@ def run_pool(q, k, v, state_pool, slots, A_log, a, dt_bias, b, cu_seqlens, scale
                       slots.contiguous(), A_log.contiguous(), a.contiguous(), dt_bias.contiguous(),
                       b.contiguous(), cu_seqlens.contiguous(), scale, out, ws)
     return out
+
+
+# ---------------------------------------------------------------------------
+# backward (no counterpart in the reference, whose prefill is forward-only:
+# solution/triton/kernel.py:1)
+# ---------------------------------------------------------------------------
+def backward_workspace_bytes(total_tokens: int, num_seqs: int) -> int:
+    return int(_native.lib.gdn_prefill_backward_workspace_bytes(total_tokens, num_seqs))
+
+
+def alloc_backward_workspace(total_tokens: int, num_seqs: int, device) -> torch.Tensor:
+    """Workspace for `backward_into` (1 KiB of slack for the 1024-byte
+    alignment, as `alloc_workspace`)."""
+    return torch.empty(backward_workspace_bytes(total_tokens, num_seqs) + 1024,
+                       dtype=torch.uint8, device=device)
+
+
+def backward_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, d_out, d_final_state,
+                  dq, dk, dv, da, db, dA_log, ddt_bias, d_state, workspace: torch.Tensor,
+                  stream: Optional[int] = None) -> None:
+    """Destination-passing backward: fp32 gradients dq, dk [T,4,128], dv
+    [T,8,128], da, db [T,8], dA_log, ddt_bias [8] and (unless None) d_state
+    [N,8,128,128], from d_out [T,8,128] bf16 and d_final_state (None: zero).
+    The inputs are the forward's; the call recomputes what it needs.  No host
+    sync."""
+    T = q.shape[0]
+    N = cu_seqlens.numel() - 1
+    if scale is None or scale == 0.0:
+        scale = 1.0 / math.sqrt(HEAD_SIZE)
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+    wptr, wbytes = _aligned_ptr(workspace)
+
+    def p(x):
+        return None if x is None else x.data_ptr()
+
+    st = _native.lib.gdn_prefill_backward_qk4_v8_d128_k_last(
+        p(q), p(k), p(v), p(state), p(A_log), p(a), p(dt_bias), p(b), p(cu_seqlens), N, T,
+        float(scale), p(d_out), p(d_final_state), p(dq), p(dk), p(dv), p(da), p(db), p(dA_log),
+        p(ddt_bias), p(d_state), wptr, wbytes, stream)
+    _native.check(st, "gdn_prefill_backward_qk4_v8_d128_k_last")
+
+
+@torch.no_grad()
+def backward(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, d_out,
+             d_final_state=None, need_d_state: bool = True):
+    """Gradients of `run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+    scale)` given d_out ([T,8,128]) and d_final_state ([N,8,128,128] or None).
+    Returns a dict of fp32 tensors: dq, dk [T,4,128]; dv [T,8,128]; da, db
+    [T,8]; dA_log, ddt_bias [8]; d_state [N,8,128,128] (None unless
+    need_d_state)."""
+    _validate_inputs(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
+    T = q.shape[0]
+    N = cu_seqlens.numel() - 1
+    assert d_out.shape == (T, NUM_V_HEADS, HEAD_SIZE)
+    if d_final_state is not None:
+        assert d_final_state.shape == (N, NUM_V_HEADS, HEAD_SIZE, HEAD_SIZE)
+    dev = q.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    g = dict(dq=torch.empty(T, NUM_Q_HEADS, HEAD_SIZE, **f32),
+             dk=torch.empty(T, NUM_K_HEADS, HEAD_SIZE, **f32),
+             dv=torch.empty(T, NUM_V_HEADS, HEAD_SIZE, **f32),
+             da=torch.empty(T, NUM_V_HEADS, **f32), db=torch.empty(T, NUM_V_HEADS, **f32),
+             dA_log=torch.empty(NUM_V_HEADS, **f32), ddt_bias=torch.empty(NUM_V_HEADS, **f32),
+             d_state=(torch.empty(N, NUM_V_HEADS, HEAD_SIZE, HEAD_SIZE, **f32)
+                      if need_d_state else None))
+    ws = alloc_backward_workspace(T, N, dev)
+    backward_into(q.contiguous(), k.contiguous(), v.contiguous(),
+                  None if state is None else state.contiguous().float(),
+                  A_log.contiguous().float(), a.contiguous(), dt_bias.contiguous().float(),
+                  b.contiguous(), cu_seqlens.contiguous(), scale,
+                  d_out.to(torch.bfloat16).contiguous(),
+                  None if d_final_state is None else d_final_state.float().contiguous(),
+                  g["dq"], g["dk"], g["dv"], g["da"], g["db"], g["dA_log"], g["ddt_bias"],
+                  g["d_state"], ws)
+    return g
+
+
+class _PrefillFunction(torch.autograd.Function):
+    """out, final_state = run(...), differentiable in q, k, v, a, b, A_log,
+    dt_bias and state (the backward recomputes the forward's chunk states)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
+        out, final_state = run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+        ctx.save_for_backward(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
+        ctx.scale = scale
+        return out, final_state
+
+    @staticmethod
+    def backward(ctx, d_out, d_final):
+        q, k, v, state, A_log, a, dt_bias, b, cu_seqlens = ctx.saved_tensors
+        if d_out is None:
+            d_out = torch.zeros(q.shape[0], NUM_V_HEADS, HEAD_SIZE, dtype=torch.bfloat16,
+                                device=q.device)
+        g = backward(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, ctx.scale, d_out,
+                     d_final, need_d_state=state is not None and ctx.needs_input_grad[3])
+        return (g["dq"], g["dk"], g["dv"], g["d_state"], g["dA_log"], g["da"], g["ddt_bias"],
+                g["db"], None, None)
+
+
+def run_autograd(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
+    """`run` with gradients: the same arguments and results, recorded for
+    torch.autograd (grads come back in each input's dtype).  No counterpart
+    in the reference."""
+    return _PrefillFunction.apply(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
