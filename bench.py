@@ -60,6 +60,11 @@ DECODE_STATE_BYTES = HV * D * D * 4 * 2           # fp32 state read + written pe
 DECODE_VEC_BYTES = 2 * HQK * D * 2 + 2 * HV * D * 2 + 2 * HV * 2  # q,k,v,out,a,b
 PREFILL_FLOP_PER_TOKEN = 1_441_792                # 8 v-heads x 180,224
 PREFILL_BYTES_PER_TOKEN = 6176
+# backward per token: the recompute (counted as one forward) plus, per v-head
+# and 64-token chunk, 4,194,304 MACs in the reverse scan (Z, dX, dS) and
+# 6,815,744 in the chunk kernel (QK^T, KK^T, dO delta^T, dX delta^T, dO S_0,
+# dX S_0, delta dS_C, Mq K, Mq^T Q, Msym K): 8 x 2 x 11,010,048 / 64 per token
+BWD_FLOP_PER_TOKEN = PREFILL_FLOP_PER_TOKEN + 2_752_512
 STATE_BYTES = HV * D * D * 4
 
 WORKLOADS = {
@@ -78,6 +83,13 @@ WORKLOADS = {
     "decode_bf16": dict(desc="decode batch 1024 with the state stored in bf16 (opt-in format), "
                              "updated in place",
                         decode_batch=1024, prefill=None, state_bf16=True),
+    # training: one prefill backward over the C3 / C4 prefill shapes
+    "bwd_c3": dict(desc="prefill backward over C3 (32 sequences U{17..3000}, initial states "
+                        "randn*0.02, d_out and d_final_state random)",
+                   decode_batch=0, prefill="c3", backward=True),
+    "bwd_c4": dict(desc="prefill backward over the C4 prefill (256 sequences U{512..8192}, zero "
+                        "initial state, d_out random, no final-state gradient)",
+                   decode_batch=0, prefill="c4", backward=True),
 }
 
 
@@ -541,6 +553,186 @@ def gpu_arm(args):
         emit(result)
 
 
+def bwd_arm(args):
+    """Training step of the prefill: one backward call (recompute + reverse
+    scan + chunk gradients) per step over the workload's sequences, inputs
+    and d_out resident.  N > 1: sequences sharded by LPT, and the only
+    exchange a training step has here, the sum of the [8] parameter
+    gradients dA_log and ddt_bias over ranks (NCCL all-reduce)."""
+    import torch
+    import torch.distributed as dist
+    from importlib import import_module
+
+    gdn = importlib.import_module("track-c-gdn_b200")
+    shard = import_module("track-c-gdn_b200.shard")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    wl = WORKLOADS[args.workload]
+    lengths = prefill_lengths(wl["prefill"])
+    parts = shard.lpt_partition(lengths.tolist(), world)
+    my = lengths[parts[rank]]
+    with_state = wl["prefill"] == "c3"
+    pre = make_prefill_inputs(torch, my, with_state, 300 + rank, dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    A_log = (torch.rand(HV, generator=gen, device=dev) * 2.7).float()
+    dt_bias = (torch.randn(HV, generator=gen, device=dev) * 0.1).float()
+    T, N = pre["T"], pre["N"]
+    d_out = (torch.randn(T, HV, D, generator=gen, device=dev) * 0.1).bfloat16()
+    d_final = (torch.randn(N, HV, D, D, generator=gen, device=dev) * 0.01) if with_state else None
+    f32 = dict(dtype=torch.float32, device=dev)
+    outs = [torch.empty(T, HQK, D, **f32), torch.empty(T, HQK, D, **f32),
+            torch.empty(T, HV, D, **f32), torch.empty(T, HV, **f32), torch.empty(T, HV, **f32),
+            torch.empty(HV, **f32), torch.empty(HV, **f32),
+            torch.empty(N, HV, D, D, **f32) if with_state else None]
+    ws = gdn.prefill.alloc_backward_workspace(T, N, dev)
+    stream = torch.cuda.current_stream(dev)
+    params = torch.empty(2 * HV, **f32)
+
+    def step():
+        gdn.prefill.backward_into(pre["q"], pre["k"], pre["v"], pre["h0"], A_log, pre["a"],
+                                  dt_bias, pre["b"], pre["cu"], None, d_out, d_final, *outs, ws)
+        if world > 1:
+            params[:HV].copy_(outs[5])
+            params[HV:].copy_(outs[6])
+            dist.all_reduce(params)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(True, local_rank)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = merge_clocks(dist, world, sampler.stop())
+    ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    status = gdn._native.read_device_status()
+    if status:
+        raise SystemExit(f"device status {status} after the timed region")
+    total = int(lengths.sum())
+    tflops = T * BWD_FLOP_PER_TOKEN / (ms / 1e3) / 1e12
+    peaks = load_peaks()
+    result = {
+        "metric": "GDN prefill backward throughput (tokens/s, max-over-ranks device time)",
+        "value": total / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp32 (backward kernels; recompute bf16 MMAs)",
+        "data": "synthetic (seeded; the benchmark configs' value distributions)",
+        "config": {"workload": wl["desc"], "prefill_sequences": len(lengths),
+                   "prefill_tokens": total,
+                   "l2": "inputs larger than L2 (no flush needed)",
+                   "parallelism": f"shard{world}: LPT by sequence" +
+                                  ("; NCCL all-reduce of dA_log, ddt_bias" if world > 1 else "")},
+        "gpu_launches": args.steps * gdn._native.lib.gdn_prefill_backward_kernel_launches(),
+        "roofline": {"kernel": "whole backward call (recompute + reverse scan + chunk gradients)",
+                     "bound": "tensor", "achieved": tflops,
+                     "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": tflops / peaks["bf16_tflops_sustained"], "traffic": None,
+                     "flop_per_token": BWD_FLOP_PER_TOKEN,
+                     "peak_source": peaks["source"] + " bf16 sustained"},
+        "clocks": clocks,
+    }
+    if not args.no_e2e:
+        # end to end: inputs from pinned host memory, gradients back, serial
+        keys = [x for x in ("q", "k", "v", "a", "b", "cu", "h0") if pre.get(x) is not None]
+        host = {x: pre[x].cpu().pin_memory() for x in keys}
+        host["d_out"] = d_out.cpu().pin_memory()
+        if d_final is not None:
+            host["d_final"] = d_final.cpu().pin_memory()
+        devb = {x: torch.empty_like(t, device=dev) for x, t in host.items()}
+        host_out = [None if o is None else torch.empty(o.shape, dtype=o.dtype).pin_memory()
+                    for o in outs]
+        h2d = sum(t.numel() * t.element_size() for t in host.values())
+        d2h = sum(o.numel() * o.element_size() for o in outs if o is not None)
+
+        def e2e_step():
+            for x, t in host.items():
+                devb[x].copy_(t, non_blocking=True)
+            gdn.prefill.backward_into(devb["q"], devb["k"], devb["v"], devb.get("h0"), A_log,
+                                      devb["a"], dt_bias, devb["b"], devb["cu"], None,
+                                      devb["d_out"], devb.get("d_final"), *outs, ws)
+            for o, h in zip(outs, host_out):
+                if o is not None:
+                    h.copy_(o, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        n = max(2, min(args.steps, args.e2e_steps))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ems = max_over_ranks(e0.elapsed_time(e1)) / n
+        result["e2e"] = {"value": total / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems,
+                         "steps": n, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                         "api": "prefill.backward_into, pinned host buffers, one stream",
+                         "bytes_per_step_note": "per rank" if world > 1 else "single GPU"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = bwd_cpu_baseline(lengths, budget_s=args.cpu_seconds)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank == 0:
+        emit(result)
+
+
+def bwd_cpu_baseline(lengths, budget_s: float = 15.0):
+    """Autograd of the restated token recurrence (oracle/autograd_ref.py) in
+    fp32 on the host cores, over whole sequences drawn from the workload
+    until the budget is spent; extrapolated per token."""
+    import torch
+    from oracle import autograd_ref
+    rng = np.random.default_rng(0)
+    toks, secs, n = 0, 0.0, 0
+    t_start = time.perf_counter()
+    while time.perf_counter() - t_start < budget_s and n < len(lengths):
+        L = int(min(lengths[n], 512))
+        n += 1
+        x = {k: torch.from_numpy(rng.standard_normal(s).astype(np.float32))
+             for k, s in (("q", (L, HQK, D)), ("k", (L, HQK, D)), ("v", (L, HV, D)),
+                          ("a", (L, HV)), ("b", (L, HV)))}
+        A_log = torch.rand(HV)
+        dt = torch.randn(HV) * 0.1
+        d_out = torch.randn(L, HV, D) * 0.1
+        t0 = time.perf_counter()
+        autograd_ref.prefill_grads(x["q"], x["k"], x["v"], None, A_log, x["a"], dt, x["b"],
+                                   [0, L], None, d_out, None, dtype=torch.float32)
+        secs += time.perf_counter() - t0
+        toks += L
+    return {"value": toks / secs, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{n} sequences (first {toks} tokens, at most 512 per "
+            "sequence) of the workload: torch autograd of the restated recurrence, fp32",
+            "wall_s": round(time.perf_counter() - t_start, 1)}
+
+
 def e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world, max_over_ranks, barrier,
             total_tokens):
     """The step as a serving loop would run it through the public entry points,
@@ -966,7 +1158,11 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3  # timing rule: at least three warm-up steps
-    if args.impl == "reference":
+    if WORKLOADS[args.workload].get("backward"):
+        if args.impl != "b200":
+            raise SystemExit("backward workloads: --impl b200 only (the reference has no backward)")
+        bwd_arm(args)
+    elif args.impl == "reference":
         reference_arm(args)
     elif args.impl == "triton":
         triton_arm(args)
