@@ -28,7 +28,9 @@
 //             with Mq = scale tril_incl(e^{G_i-G_j} dO_i.delta_j) and
 //                  Ma = strict_lower(-(dX_i.delta_j) beta_i e^{G_i-G_j});
 //   bwd_reduce: dA_log = sum_t dg_t g_t, ddt_bias = sum_t da_t.
-// The two new kernels compute in fp32 on the CUDA cores.  Every sum has a
+// Both kernels run their products on the tensor cores (bf16 operands, fp32
+// accumulators, as the forward) and the rest in fp32; the state gradient
+// itself is carried in fp32.  Every sum has a
 // fixed order; dq and dk (shared by the two v-heads of a q/k head) are the
 // sum of exactly two fp32 atomic additions onto zero, which is
 // order-independent, so the whole backward is deterministic.
@@ -83,26 +85,43 @@ __device__ __forceinline__ void unpack8(const uint4 u, float (&f)[8]) {
 }
 
 // ---------------------------------------------------------------------------
-// reverse scan over chunks
+// reverse scan over chunks (tcgen05)
 // ---------------------------------------------------------------------------
+// One CTA (256 threads) per (sequence, v-head).  Thread (vrow, hc) keeps
+// dS[vrow][64 hc .. 64 hc + 63] in fp32 registers; a bf16 copy in TMEM
+// (columns 0..63) is the A operand of MMA a.  Per chunk, three dependent
+// MMAs (bf16 operands, fp32 accumulators):
+//   a:  Zr = dS K^T                                    [v x t]  cols 128..191
+//   b:  dX / scale = dO^T (P Ainv) + (Z / scale) Ainv  [v x t]  cols 192..255
+//   c:  dS' = dO^T Q' - (beta e^G dX) K                [v x k]  cols 128..255
+// with Z = e^{G_C - G} Zr and Q' = scale e^G Q (built in place over the Q
+// tile); dO, the image and Q', K enter MMAs b and c as MN-major operands.
+// Then dS <- e^{G_C} dS + dS'.
 constexpr int kBwdScanThreads = 256;
 
 struct BwdScanSmem {
-  static constexpr int kK = 0;          // K tile bf16 [64 t][128 k] (q/k head of this v-head)
-  static constexpr int kQ = 16384;      // Q tile bf16 [64 t][128 k]
-  static constexpr int kDO = 32768;     // dO tile bf16 [64 t][128 v] (this v-head)
-  static constexpr int kImg = 49152;    // [P Ainv ; Ainv] bf16 image (prep kernel output)
-  static constexpr int kZX = 65536;     // Z, then dX: fp32 [64 t][128 v]
-  static constexpr int kEG = 98304;     // e^{G_t} (0 past the end)
-  static constexpr int kBT = kEG + 256;  // beta_t (0 past the end)
-  static constexpr int kED = kBT + 256;  // e^{G_C - G_t} (0 past the end)
+  static constexpr int kQ = 0;        // Q tile, then Q' in place: 2 d-blocks x 64 t x 128 B
+  static constexpr int kK0 = 16384;   // K tiles, double buffered (chunks in reverse order)
+  static constexpr int kK1 = 32768;
+  static constexpr int kDO = 49152;   // dO tile: 2 v-blocks x 64 t x 128 B
+  static constexpr int kImg = 65536;  // [P Ainv ; Ainv] image, 128 rows x 128 B
+  static constexpr int kZX = 81920;   // Z / scale, then -beta e^G dX: [128 v][64 t] bf16, K-major
+  static constexpr int kEG = 98304;   // e^{G_t} (0 past the end)
+  static constexpr int kBT = kEG + 256;   // beta_t (0 past the end)
+  static constexpr int kED = kBT + 256;   // e^{G_C - G_t} (0 past the end)
   static constexpr int kEGC = kED + 256;  // e^{G_C}
-  static constexpr int kBytes = kEGC + 16 + 128;  // + base alignment slack
+  static constexpr int kBar = kEGC + 16;  // mma, q, do, img, k0, k1
+  static constexpr int kTmem = kBar + 48;
+  static constexpr int kBroken = kBar + 52;
+  static constexpr int kBytes = kBar + 64 + 1024;  // + base alignment slack
+  static constexpr uint32_t kTmemCols = 256;
+  static constexpr uint32_t kColSb = 0, kColA = 128, kColB = 192;
 };
 
 __global__ void __launch_bounds__(kBwdScanThreads, 2)
-gdn_prefill_bwd_scan_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
-                            const uint16_t *__restrict__ d_out,
+gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                            const __grid_constant__ CUtensorMap tmap_k,
+                            const __grid_constant__ CUtensorMap tmap_do,
                             const float *__restrict__ d_final, const int64_t *__restrict__ cu,
                             const int *__restrict__ meta, const int *__restrict__ chunk_off,
                             const int *__restrict__ seq_order, const float *__restrict__ gcum_ws,
@@ -111,12 +130,12 @@ gdn_prefill_bwd_scan_kernel(const uint16_t *__restrict__ q, const uint16_t *__re
                             float *__restrict__ d_state) {
   using SM = BwdScanSmem;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = smem_align<128>(smem_raw);
+  uint8_t *smem = smem_align<1024>(smem_raw);
   if (meta[kMetaError] != 0) return;
   const int n = seq_order[blockIdx.x / kHV];
   const int hv = blockIdx.x % kHV, hqk = hv >> 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int hc = warp >> 2, vrow = 32 * (warp & 3) + lane;
+  const int quad = warp & 3, hc = warp >> 2, vrow = 32 * quad + lane;
   const int64_t bos = cu[n], len = cu[n + 1] - bos;
   const int nchunks = static_cast<int>((len + kChunk - 1) / kChunk);
   const int gbase = chunk_off[n];
@@ -124,12 +143,44 @@ gdn_prefill_bwd_scan_kernel(const uint16_t *__restrict__ q, const uint16_t *__re
   const int64_t srow = static_cast<int64_t>(vrow) * kD + 64 * hc;
   GDN_DCHECK(n >= 0 && n < meta[kMetaN] && gbase + nchunks <= meta[kMetaChunks]);
 
-  const uint16_t *dOt = reinterpret_cast<const uint16_t *>(smem + SM::kDO);
-  float *ZX = reinterpret_cast<float *>(smem + SM::kZX);
   float *EG = reinterpret_cast<float *>(smem + SM::kEG);
   float *BT = reinterpret_cast<float *>(smem + SM::kBT);
   float *ED = reinterpret_cast<float *>(smem + SM::kED);
   float *EGC = reinterpret_cast<float *>(smem + SM::kEGC);
+  volatile int *broken = reinterpret_cast<volatile int *>(smem + SM::kBroken);
+  uint8_t *zx = smem + SM::kZX;
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t bar_mma = s_base + SM::kBar, bar_q = bar_mma + 8, bar_do = bar_mma + 16,
+                 bar_img = bar_mma + 24, bar_k0 = bar_mma + 32;  // bar_k1 = bar_k0 + 8
+
+  auto chunk_t0 = [&](int c) { return static_cast<int>(bos + static_cast<int64_t>(c) * kChunk); };
+  auto issue_tile2 = [&](const void *tm, uint32_t dst, int x, int c, uint32_t bar) {
+    mbar_arrive_expect_tx(bar, 16384);
+    tma_load_2d(dst, tm, x, chunk_t0(c), bar);
+    tma_load_2d(dst + 8192, tm, x + 64, chunk_t0(c), bar);
+  };
+  auto issue_img = [&](int c) {
+    mbar_arrive_expect_tx(bar_img, static_cast<uint32_t>(kM2Bytes));
+    bulk_load(s_base + SM::kImg, m2_ws + (static_cast<int64_t>(gbase + c) * kHV + hv) * kM2Bytes,
+              static_cast<uint32_t>(kM2Bytes), bar_img);
+  };
+
+  if (warp == 0) tmem_alloc(s_base + SM::kTmem, SM::kTmemCols);
+  if (tid == 0) {
+    *broken = 0;
+    for (int i = 0; i < 6; ++i) mbar_init(bar_mma + 8 * i, 1);
+    mbar_init_fence();
+    if (nchunks > 0) {
+      const int c = nchunks - 1;
+      issue_tile2(&tmap_q, s_base + SM::kQ, hqk * kD, c, bar_q);
+      issue_tile2(&tmap_do, s_base + SM::kDO, hv * kD, c, bar_do);
+      issue_img(c);
+      issue_tile2(&tmap_k, s_base + ((c & 1) ? SM::kK1 : SM::kK0), hqk * kD, c, bar_k0 + 8 * (c & 1));
+      if (c > 0)
+        issue_tile2(&tmap_k, s_base + (((c - 1) & 1) ? SM::kK1 : SM::kK0), hqk * kD, c - 1,
+                    bar_k0 + 8 * ((c - 1) & 1));
+    }
+  }
 
   // dS[vrow][64 hc .. 64 hc + 63]
   float ds[64];
@@ -147,12 +198,37 @@ gdn_prefill_bwd_scan_kernel(const uint16_t *__restrict__ q, const uint16_t *__re
 #pragma unroll
     for (int i = 0; i < 64; ++i) ds[i] = 0.f;
   }
+  __syncthreads();  // barriers initialised, TMEM address published
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + SM::kTmem);
+  const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * quad) << 16);
+  auto put_sb = [&]() {  // bf16 copy of dS -> TMEM columns 32 hc .. 32 hc + 31
+    uint32_t pk[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(ds[2 * j], ds[2 * j + 1]);
+    tmem_st32(tlane + SM::kColSb + 32 * hc, pk);
+    tmem_wait_st();
+  };
+  put_sb();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t id_a = umma_idesc_bf16(128, 64, false, false);
+  const uint32_t id_b1 = umma_idesc_bf16(128, 64, true, true);
+  const uint32_t id_b2 = umma_idesc_bf16(128, 64, false, true);
+  const uint32_t id_c1 = umma_idesc_bf16(128, 128, true, true);
+  const uint32_t id_c2 = umma_idesc_bf16(128, 128, false, true);
+  const float inv_scale = 1.0f / scale;
+  uint32_t ph_mma = 0, ph_q = 0, ph_do = 0, ph_img = 0, ph_k = 0;
 
 #pragma unroll 1
   for (int c = nchunks - 1; c >= 0; --c) {
+    const int cb = c & 1;
     const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
     const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
     const int64_t gc = gbase + c;
+    const uint32_t kbuf = s_base + (cb ? SM::kK1 : SM::kK0);
     {  // the chunk-end gradient, for the chunk-parallel kernel
       float *dst = dsc_ws + gc * kHV * kD * kD + hv_off + srow;
 #pragma unroll
@@ -160,122 +236,165 @@ gdn_prefill_bwd_scan_kernel(const uint16_t *__restrict__ q, const uint16_t *__re
         *reinterpret_cast<float4 *>(dst + 4 * i) =
             make_float4(ds[4 * i], ds[4 * i + 1], ds[4 * i + 2], ds[4 * i + 3]);
     }
-    __syncthreads();  // the previous chunk's shared-memory reads are done
-    // K, Q (q/k head hqk) and dO (v-head hv) tiles; rows past L are zero
-    for (int idx = tid; idx < 3 * 64 * 16; idx += kBwdScanThreads) {
-      const int which = idx >> 10, r = (idx >> 4) & 63, ch = idx & 15;
-      uint4 val = make_uint4(0u, 0u, 0u, 0u);
-      if (r < L) {
-        const uint16_t *src = which == 0   ? k + ((t0 + r) * kHQK + hqk) * kD
-                              : which == 1 ? q + ((t0 + r) * kHQK + hqk) * kD
-                                           : d_out + ((t0 + r) * kHV + hv) * kD;
-        val = *reinterpret_cast<const uint4 *>(src + 8 * ch);
-      }
-      *reinterpret_cast<uint4 *>(smem + which * 16384 + r * 256 + ch * 16) = val;
-    }
-    {
-      const uint4 *src = reinterpret_cast<const uint4 *>(m2_ws + (gc * kHV + hv) * kM2Bytes);
-      uint4 *dst = reinterpret_cast<uint4 *>(smem + SM::kImg);
-      for (int i = tid; i < static_cast<int>(kM2Bytes / 16); i += kBwdScanThreads) dst[i] = src[i];
-    }
     if (tid < 64) {
       const float gC = gcum_ws[(t0 + L - 1) * kHV + hv];
       float eg = 0.f, bt = 0.f, ed = 0.f;
       if (tid < L) {
-        const float g = gcum_ws[(t0 + tid) * kHV + hv];
-        eg = expf(g);
+        const float gg = gcum_ws[(t0 + tid) * kHV + hv];
+        eg = expf(gg);
         bt = beta_ws[(t0 + tid) * kHV + hv];
-        ed = expf(gC - g);
+        ed = expf(gC - gg);
       }
       EG[tid] = eg;
       BT[tid] = bt;
       ED[tid] = ed;
       if (tid == 0) EGC[0] = expf(gC);
     }
+    // every thread sees this chunk's tiles land once; the next loads into
+    // each buffer are issued only after a later __syncthreads
+    wait_phase(bar_k0 + 8 * cb, (ph_k >> cb) & 1, broken);
+    ph_k ^= 1u << cb;
+    wait_phase(bar_q, ph_q, broken);
+    ph_q ^= 1;
+    wait_phase(bar_do, ph_do, broken);
+    ph_do ^= 1;
+    wait_phase(bar_img, ph_img, broken);
+    ph_img ^= 1;
+    if (L < kChunk) {
+      // the first chunk processed is the only partial one: rows past the
+      // sequence end hold the next sequence's tokens (or zero fill)
+      const int nz = kChunk - L;
+      for (int idx = tid; idx < 6 * nz * 8; idx += kBwdScanThreads) {
+        const int ch = idx & 7, r = L + (idx >> 3) % nz, which = (idx >> 3) / nz;  // 0..5
+        const uint32_t base = (which >> 1) == 0 ? SM::kQ : ((which >> 1) == 1 ? (cb ? SM::kK1 : SM::kK0) : SM::kDO);
+        *reinterpret_cast<uint4 *>(smem + base + (which & 1) * 8192 + r * 128 + ch * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+      fence_async_smem();
+    }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
 
-    // Z[v][t] = e^{G_C - G_t} sum_k dS[v][k] K[t][k], 16 tokens at a time;
-    // the two k halves meet in shared memory (stored as ZX[t][v])
-#pragma unroll 1
-    for (int tg = 0; tg < 4; ++tg) {
-      float acc[16];
+    // ---- MMA a: Zr = dS K^T ----
+    if (tid == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
+        umma_bf16_ts(tmem + SM::kColA, tmem + SM::kColSb + 8 * ks,
+                     umma_desc_sw128(kbuf + boff, 16, 1024), id_a, ks > 0);
+      }
+      umma_commit(bar_mma);
+    }
+    // Q' = scale e^{G_t} Q, in place, while MMA a runs (1024 chunks of 8)
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int idx = tid + kBwdScanThreads * m;
+      const int t = (idx >> 3) & 63;
+      uint4 *pq = reinterpret_cast<uint4 *>(smem + SM::kQ + (idx >> 9) * 8192 + t * 128 + (idx & 7) * 16);
+      float f[8];
+      unpack8(*pq, f);
+      const float sc = scale * EG[t];
+      *pq = make_uint4(pack_bf16x2(sc * f[0], sc * f[1]), pack_bf16x2(sc * f[2], sc * f[3]),
+                       pack_bf16x2(sc * f[4], sc * f[5]), pack_bf16x2(sc * f[6], sc * f[7]));
+    }
+    wait_phase(bar_mma, ph_mma, broken);
+    ph_mma ^= 1;
+    tc_fence_after();
+
+    // ---- Z / scale -> K-major tile (tokens 32 hc .. 32 hc + 31 of row vrow) ----
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int tb = 32 * hc + 16 * p;
+      float z[16];
+      tmem_ld16(tlane + SM::kColA + tb, z);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) z[j] *= ED[tb + j] * inv_scale;
+      store16_bf16(zx, vrow, tb >> 3, z);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    // ---- MMA b: dX / scale = dO^T (P Ainv) + (Z / scale) Ainv ----
+    if (tid == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + SM::kColB, umma_desc_sw128(s_base + SM::kDO + ks * 2048, 8192, 1024),
+                  umma_desc_sw128(s_base + SM::kImg + ks * 2048, 8192, 1024), id_b1, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + SM::kColB, umma_desc_sw128(s_base + SM::kZX + ks * 32, 16, 1024),
+                  umma_desc_sw128(s_base + SM::kImg + 8192 + ks * 2048, 8192, 1024), id_b2, 1);
+      umma_commit(bar_mma);
+    }
+    wait_phase(bar_mma, ph_mma, broken);
+    ph_mma ^= 1;
+    tc_fence_after();
+    if (tid == 0 && c > 0) issue_img(c - 1);  // the image is consumed
+
+    // ---- dX: to the workspace (fp32) and -beta e^G dX -> K-major tile ----
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int tb = 32 * hc + 16 * p;
+      float x[16];
+      tmem_ld16(tlane + SM::kColB + tb, x);
+      tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const uint4 *krow =
-            reinterpret_cast<const uint4 *>(smem + SM::kK + (16 * tg + j) * 256 + hc * 128);
-        float a = 0.f;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          float kv[8];
-          unpack8(krow[u], kv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) a += ds[8 * u + e] * kv[e];
-        }
-        acc[j] = a;
+        const int t = tb + j;
+        const float dx = scale * x[j];
+        if (t < L) dx_ws[((t0 + t) * kHV + hv) * kD + vrow] = dx;
+        x[j] = -BT[t] * EG[t] * dx;
       }
-      if (hc == 1) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) ZX[(16 * tg + j) * kD + vrow] = acc[j];
-      }
-      __syncthreads();
-      if (hc == 0) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = 16 * tg + j;
-          ZX[t * kD + vrow] = ED[t] * (acc[j] + ZX[t * kD + vrow]);
-        }
-      }
+      store16_bf16(zx, vrow, tb >> 3, x);
     }
+    fence_async_smem();
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
 
-    // dX[v][t] for t in [32 hc, 32 hc + 32):
-    //   sum_i scale dO[i][v] (P Ainv)[i][t] + Z[v][i] Ainv[i][t]
-    float dx[32];
+    // ---- MMA c: dS' = dO^T Q' - (beta e^G dX) K ----
+    if (tid == 0) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) dx[j] = 0.f;
-    const uint8_t *img = smem + SM::kImg;
-#pragma unroll 1
-    for (int i = 0; i < L; ++i) {
-      const float a = scale * bf16_to_f32(dOt[i * kD + vrow]);
-      const float z = ZX[i * kD + vrow];
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + SM::kColA, umma_desc_sw128(s_base + SM::kDO + ks * 2048, 8192, 1024),
+                  umma_desc_sw128(s_base + SM::kQ + ks * 2048, 8192, 1024), id_c1, ks > 0);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float pa[8], ai[8];
-        unpack8(*reinterpret_cast<const uint4 *>(img + sw128(i, 4 * hc + u)), pa);
-        unpack8(*reinterpret_cast<const uint4 *>(img + sw128(64 + i, 4 * hc + u)), ai);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) dx[8 * u + e] += a * pa[e] + z * ai[e];
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + SM::kColA, umma_desc_sw128(s_base + SM::kZX + ks * 32, 16, 1024),
+                  umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), id_c2, 1);
+      umma_commit(bar_mma);
+    }
+    wait_phase(bar_mma, ph_mma, broken);
+    ph_mma ^= 1;
+    tc_fence_after();
+    if (tid == 0) {  // Q, dO and this K buffer are consumed
+      if (c > 0) {
+        issue_tile2(&tmap_q, s_base + SM::kQ, hqk * kD, c - 1, bar_q);
+        issue_tile2(&tmap_do, s_base + SM::kDO, hv * kD, c - 1, bar_do);
       }
+      if (c > 1) issue_tile2(&tmap_k, kbuf, hqk * kD, c - 2, bar_k0 + 8 * cb);
     }
-    __syncthreads();  // every thread has read Z
+
+    // ---- dS <- e^{G_C} dS + dS' ; bf16(dS) -> TMEM ----
+    {
+      const float egc = EGC[0];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int t = 32 * hc + j;
-      const float val = t < L ? dx[j] : 0.f;
-      ZX[t * kD + vrow] = val;
-      if (t < L) dx_ws[((t0 + t) * kHV + hv) * kD + vrow] = val;
+      for (int p = 0; p < 2; ++p) {
+        float d[32];
+        tmem_ld32(tlane + SM::kColA + 64 * hc + 32 * p, d);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ds[32 * p + j] = egc * ds[32 * p + j] + d[j];
+      }
+      put_sb();
     }
+    tc_fence_before();
     __syncthreads();
-
-    // dS <- e^{G_C} dS + sum_t (scale e^{G_t} dO[t][v]) Q[t] - (beta_t e^{G_t} dX[v][t]) K[t]
-    const float egc = EGC[0];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) ds[i] *= egc;
-#pragma unroll 1
-    for (int t = 0; t < L; ++t) {
-      const float at = scale * EG[t] * bf16_to_f32(dOt[t * kD + vrow]);
-      const float bt = BT[t] * EG[t] * ZX[t * kD + vrow];
-      const uint4 *qrow = reinterpret_cast<const uint4 *>(smem + SM::kQ + t * 256 + hc * 128);
-      const uint4 *krow = reinterpret_cast<const uint4 *>(smem + SM::kK + t * 256 + hc * 128);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        float qv[8], kv[8];
-        unpack8(qrow[u], qv);
-        unpack8(krow[u], kv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ds[8 * u + e] += at * qv[e] - bt * kv[e];
-      }
-    }
+    tc_fence_after();
   }
 
   if (d_state != nullptr) {
@@ -285,49 +404,104 @@ gdn_prefill_bwd_scan_kernel(const uint16_t *__restrict__ q, const uint16_t *__re
       *reinterpret_cast<float4 *>(dst + 4 * i) =
           make_float4(ds[4 * i], ds[4 * i + 1], ds[4 * i + 2], ds[4 * i + 3]);
   }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, SM::kTmemCols);
+  }
 }
 
 // ---------------------------------------------------------------------------
-// chunk-parallel gradients
+// chunk-parallel gradients (tcgen05)
 // ---------------------------------------------------------------------------
-constexpr int kBwdChunkThreads = 256;
-constexpr int kTP = 68;  // row pitch (floats) of the transposed [128][64] tiles
-constexpr int kTT = 65;  // row pitch (floats) of the 64 x 64 matrices
+// One CTA (128 threads, the whole TMEM) per (chunk, v-head).  Eight MMAs on
+// bf16 operands, fp32 accumulators in TMEM:
+//   (a) [Q;K] K^T      -> QK (lanes 0-63), KK (lanes 64-127)      M=128 N=64 K=128
+//   (b) [dO;dX] delta^T -> dO.delta (lanes 0-63), dX.delta (64-127)
+//   (c) S_0^T dO^T = (dO S_0)^T        lanes k, columns t         M=128 N=64 K=128
+//   (d) S_0^T dX^T = (dX S_0)^T
+//   (e) dS_C^T delta^T = (delta dS_C)^T
+//   (f) K^T Mq^T = (Mq K)^T                                       K=64
+//   (g)+(h) Q^T Mq + K^T Msym = (Mq^T Q + Msym K)^T
+// S_0, dS_C ([v][k] in memory) and the Q and K tiles ([t][k]) enter (c)-(h)
+// as MN-major A operands (k contiguous), so nothing is transposed by hand.
+// Mq and Msym come from (a) and (b) by element-wise work on the CUDA cores
+// between the two MMA batches.
+constexpr int kBwdTcThreads = 128;
 
-struct BwdChunkSmem {
-  // three transposed tiles [128 inner][64 t] (fp32, pitch kTP): first Q^T,
-  // K^T; then dO^T, dX^T, delta^T
-  static constexpr int kTile = 128 * kTP * 4;
-  static constexpr int kR = 0;
-  static constexpr int kMat = 3 * kTile;  // QK, KK|Msym, DOD|Mq, DXD|Ma: [64][kTT] fp32
-  static constexpr int kMatBytes = 64 * kTT * 4;
-  static constexpr int kRed = kMat + 4 * kMatBytes;  // float [3][16][64] partial dot products
-  static constexpr int kVec = kRed + 3 * 16 * 64 * 4;  // per-token vectors, 64 floats each
-  static constexpr int kNumVec = 16;
-  static constexpr int kScalars = kVec + kNumVec * 64 * 4;  // e^{G_C}, <dS_C, S_0>, warp partials
-  static constexpr int kBytes = kScalars + 64 * 4 + 128;
+struct BwdTcSmem {
+  static constexpr int kQK = 0;        // [Q;K]: 2 d-blocks x (64 Q rows | 64 K rows) x 128 B (TMA)
+  static constexpr int kOX = 32768;    // [dO;dX]: 2 v-blocks x (64 dO rows (TMA) | 64 dX rows) x 128 B
+  static constexpr int kDL = 65536;    // delta: 2 v-blocks x 64 rows x 128 B
+  static constexpr int kS0 = 81920;    // S_0 as MN-major A: 2 k-blocks x 128 v rows x 128 B
+  static constexpr int kDS = 114688;   // dS_C, same layout
+  static constexpr int kMQ = 147456;   // Mq bf16 [64 t][64 j], 128-byte rows
+  static constexpr int kMS = 155648;   // Msym bf16 [64][64]
+  static constexpr int kMA = 163840;   // Ma fp32 [64][65] (transpose staging)
+  static constexpr int kVec = kMA + 64 * 65 * 4;     // per-token vectors: 16 x 64 fp32
+  static constexpr int kRed = kVec + 16 * 64 * 4;    // warp partials [4][5][64] fp32
+  static constexpr int kBar = kRed + 4 * 5 * 64 * 4;  // 4 mbarriers
+  static constexpr int kTmem = kBar + 32;
+  static constexpr int kBroken = kBar + 36;
+  static constexpr int kScal = kBar + 64;            // 16 fp32 scalars
+  static constexpr int kBytes = kScal + 64 + 1024;   // + base alignment slack
 };
-// per-token vector slots
+static_assert(BwdTcSmem::kMA + 64 * 65 * 4 <= BwdTcSmem::kVec, "layout");
+static_assert(BwdTcSmem::kBytes <= 227 * 1024, "shared memory");
+// TMEM columns
+constexpr uint32_t kTcA = 0, kTcB = 64, kTcP1 = 128, kTcP2 = 192, kTcP3 = 256, kTcF = 320,
+                   kTcGH = 384, kTcCols = 512;
+// per-token vector slots and partial-sum families
 enum BwdVec : int {
-  kVG = 0, kVEG, kVBT, kVED, kVRowWq, kVColWq, kVRowWa, kVColWa, kVDbA, kVDXv, kVZeta,
-  kVDG, kVDB
+  kVG = 0, kVEG, kVBT, kVED, kVRowWq, kVRowWa, kVDbA, kVDXv, kVZeta, kVDG, kVDB
 };
+enum BwdRed : int { kRedRho = 0, kRedXi, kRedZeta, kRedColWq, kRedColWa };
 
-__global__ void __launch_bounds__(kBwdChunkThreads, 1)
-gdn_prefill_bwd_chunk_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
-                             const uint16_t *__restrict__ v, const uint16_t *__restrict__ d_out,
-                             const float *__restrict__ A_log, const uint16_t *__restrict__ a,
-                             const float *__restrict__ dt_bias, const int64_t *__restrict__ cu,
-                             const int *__restrict__ meta, const int2 *__restrict__ chunk_tab,
-                             const float *__restrict__ gcum_ws, const float *__restrict__ beta_ws,
+// Sum over the warp's 32 lanes of v[lane]: a transposing butterfly (31
+// shuffles for 32 sums, instead of 32 x 5).  v is clobbered.
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = up ? v[i] : v[i + o];
+      const float keep = up ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ uint4 pack8(const float4 a, const float4 b) {
+  return make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                    pack_bf16x2(b.z, b.w));
+}
+
+// element (row, col) of a bf16 tile with 128-byte rows and 128-byte swizzle
+__device__ __forceinline__ float tile_at(const uint8_t *tile, int row, int col) {
+  return bf16_to_f32(*reinterpret_cast<const uint16_t *>(
+      tile + row * 128 + ((((col >> 3) ^ row) & 7) << 4) + (col & 7) * 2));
+}
+
+__global__ void __launch_bounds__(kBwdTcThreads, 1)
+gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                             const __grid_constant__ CUtensorMap tmap_k,
+                             const __grid_constant__ CUtensorMap tmap_do,
+                             const uint16_t *__restrict__ v, const float *__restrict__ A_log,
+                             const uint16_t *__restrict__ a, const float *__restrict__ dt_bias,
+                             const int64_t *__restrict__ cu, const int *__restrict__ meta,
+                             const int2 *__restrict__ chunk_tab, const float *__restrict__ gcum_ws,
+                             const float *__restrict__ beta_ws,
                              const float *__restrict__ states_ws, const float *__restrict__ dsc_ws,
                              const float *__restrict__ delta_ws, const float *__restrict__ dx_ws,
                              float scale, float *__restrict__ dq, float *__restrict__ dk,
                              float *__restrict__ dv, float *__restrict__ da,
                              float *__restrict__ db, float *__restrict__ dgg_ws) {
-  using SM = BwdChunkSmem;
+  using SM = BwdTcSmem;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = smem_align<128>(smem_raw);
+  uint8_t *smem = smem_align<1024>(smem_raw);
   const int g = blockIdx.x, hv = blockIdx.y, hqk = hv >> 1;
   if (meta[kMetaError] != 0 || g >= meta[kMetaChunks]) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -339,19 +513,32 @@ gdn_prefill_bwd_chunk_kernel(const uint16_t *__restrict__ q, const uint16_t *__r
   const float *S0 = states_ws + soff;
   const float *dSC = dsc_ws + soff;
 
-  float *T0 = reinterpret_cast<float *>(smem + SM::kR);
-  float *T1 = reinterpret_cast<float *>(smem + SM::kR + SM::kTile);
-  float *T2 = reinterpret_cast<float *>(smem + SM::kR + 2 * SM::kTile);
-  float *QK = reinterpret_cast<float *>(smem + SM::kMat);
-  float *KK = QK + 64 * kTT;  // later Msym = Ma + Ma^T
-  float *M1 = KK + 64 * kTT;  // dO_i.delta_j, then Mq
-  float *M2 = M1 + 64 * kTT;  // dX_i.delta_j, then Ma
-  float *RED = reinterpret_cast<float *>(smem + SM::kRed);
   float *VEC = reinterpret_cast<float *>(smem + SM::kVec);
-  float *SC = reinterpret_cast<float *>(smem + SM::kScalars);
+  float *RED = reinterpret_cast<float *>(smem + SM::kRed);
+  float *SC = reinterpret_cast<float *>(smem + SM::kScal);
+  float *MA = reinterpret_cast<float *>(smem + SM::kMA);
+  volatile int *broken = reinterpret_cast<volatile int *>(smem + SM::kBroken);
   auto vec = [&](int slot) { return VEC + slot * 64; };
+  auto red = [&](int w, int f) { return RED + (w * 5 + f) * 64; };
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t bar_tma = s_base + SM::kBar, bar_m1 = bar_tma + 8, bar_m2 = bar_tma + 16,
+                 bar_m3 = bar_tma + 24;
 
-  // gates of the chunk
+  // ---- TMA of the Q, K and dO tiles; TMEM ----
+  if (warp == 0) tmem_alloc(s_base + SM::kTmem, kTcCols);
+  if (tid == 0) {
+    *broken = 0;
+    for (int i = 0; i < 4; ++i) mbar_init(bar_tma + 8 * i, 1);
+    mbar_init_fence();
+    mbar_arrive_expect_tx(bar_tma, 49152);
+    for (int blk = 0; blk < 2; ++blk) {
+      const int y = static_cast<int>(t0);
+      tma_load_2d(s_base + SM::kQK + blk * 16384, &tmap_q, hqk * kD + 64 * blk, y, bar_tma);
+      tma_load_2d(s_base + SM::kQK + blk * 16384 + 8192, &tmap_k, hqk * kD + 64 * blk, y, bar_tma);
+      tma_load_2d(s_base + SM::kOX + blk * 16384, &tmap_do, hv * kD + 64 * blk, y, bar_tma);
+    }
+  }
+  // ---- gates ----
   if (tid < 64) {
     const float gC = gcum_ws[(t0 + L - 1) * kHV + hv];
     float gg = 0.f, eg = 0.f, bt = 0.f, ed = 0.f;
@@ -367,276 +554,269 @@ gdn_prefill_bwd_chunk_kernel(const uint16_t *__restrict__ q, const uint16_t *__r
     vec(kVED)[tid] = ed;
     if (tid == 0) SC[0] = expf(gC);
   }
-
-  // transposed tile loads: dst[i][t] = row t of the source, 128 values;
-  // a warp covers 32 consecutive tokens (conflict-free shared stores)
-  auto load_t_bf16 = [&](float *dst, const uint16_t *base, int64_t stride) {
-    for (int idx = tid; idx < 64 * 16; idx += kBwdChunkThreads) {
-      const int t = idx & 63, ch = idx >> 6;
-      float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (t < L) unpack8(*reinterpret_cast<const uint4 *>(base + (t0 + t) * stride + 8 * ch), f);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) dst[(8 * ch + u) * kTP + t] = f[u];
-    }
-  };
-  auto load_t_f32 = [&](float *dst, const float *base, int64_t stride) {
-    for (int idx = tid; idx < 64 * 32; idx += kBwdChunkThreads) {
-      const int t = idx & 63, ch = idx >> 6;
-      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (t < L) f = *reinterpret_cast<const float4 *>(base + (t0 + t) * stride + 4 * ch);
-      dst[(4 * ch + 0) * kTP + t] = f.x;
-      dst[(4 * ch + 1) * kTP + t] = f.y;
-      dst[(4 * ch + 2) * kTP + t] = f.z;
-      dst[(4 * ch + 3) * kTP + t] = f.w;
-    }
-  };
-  // C1 += A1 B^T, C2 += A2 B^T over 128 inner values, thread tile 4 x 4
-  // (rows 4 ti.., columns 4 tj..) from transposed tiles
-  const int ti = tid & 15, tj = tid >> 4;
-  auto tt_products = [&](const float *A1, const float *A2, const float *B, float *C1, float *C2) {
-    float c1[4][4], c2[4][4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int s = 0; s < 4; ++s) c1[r][s] = c2[r][s] = 0.f;
-#pragma unroll 4
-    for (int x = 0; x < 128; ++x) {
-      const float4 a1 = *reinterpret_cast<const float4 *>(A1 + x * kTP + 4 * ti);
-      const float4 a2 = *reinterpret_cast<const float4 *>(A2 + x * kTP + 4 * ti);
-      const float4 bb = *reinterpret_cast<const float4 *>(B + x * kTP + 4 * tj);
-      const float av1[4] = {a1.x, a1.y, a1.z, a1.w}, av2[4] = {a2.x, a2.y, a2.z, a2.w};
-      const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          c1[r][s] += av1[r] * bv[s];
-          c2[r][s] += av2[r] * bv[s];
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        C1[(4 * ti + r) * kTT + 4 * tj + s] = c1[r][s];
-        C2[(4 * ti + r) * kTT + 4 * tj + s] = c2[r][s];
-      }
-  };
-
-  // ---- stage 1: Q K^T, K K^T ----
-  load_t_bf16(T0, q + hqk * kD, kHQK * kD);
-  load_t_bf16(T1, k + hqk * kD, kHQK * kD);
-  __syncthreads();
-  tt_products(T0, T1, T1, QK, KK);
   __syncthreads();
 
-  // ---- stage 2: dO delta^T, dX delta^T ----
-  load_t_bf16(T0, d_out + hv * kD, kHV * kD);
-  load_t_f32(T1, dx_ws + hv * kD, kHV * kD);
-  load_t_f32(T2, delta_ws + hv * kD, kHV * kD);
-  __syncthreads();
-  tt_products(T0, T1, T2, M1, M2);
-  __syncthreads();
-
-  // ---- stage 3: Mq, Ma and their gate terms (row i per thread) ----
-  if (tid < 64) {
-    const int i = tid;
-    float rwq = 0.f, rwa = 0.f, dba = 0.f;
-    const float gi = vec(kVG)[i], bi = vec(kVBT)[i];
-    for (int j = 0; j < 64; ++j) {
-      float mq = 0.f, ma = 0.f;
-      if (i < L && j <= i) {
-        const float dec = expf(gi - vec(kVG)[j]);
-        mq = scale * dec * M1[i * kTT + j];
-        rwq += mq * QK[i * kTT + j];
-        if (j < i) {
-          const float dA = -M2[i * kTT + j];
-          ma = dA * bi * dec;
-          rwa += ma * KK[i * kTT + j];
-          dba += dA * dec * KK[i * kTT + j];
-        }
-      }
-      M1[i * kTT + j] = mq;
-      M2[i * kTT + j] = ma;
+  // ---- operands written by the threads (bf16, 128-byte swizzle) ----
+  {  // S_0 and dS_C as MN-major tiles; <dS_C, S_0> on the way
+    float sds = 0.f;
+    for (int idx = tid; idx < 128 * 16; idx += kBwdTcThreads) {
+      const int vr = idx >> 4, kc = idx & 15;  // v row, k = 8 kc .. 8 kc + 7
+      const float4 *x = reinterpret_cast<const float4 *>(S0 + vr * kD + 8 * kc);
+      const float4 *y = reinterpret_cast<const float4 *>(dSC + vr * kD + 8 * kc);
+      const float4 x0 = x[0], x1 = x[1], y0 = y[0], y1 = y[1];
+      sds += x0.x * y0.x + x0.y * y0.y + x0.z * y0.z + x0.w * y0.w + x1.x * y1.x +
+             x1.y * y1.y + x1.z * y1.z + x1.w * y1.w;
+      const uint32_t off = (kc >> 3) * 16384 + vr * 128 + (((kc ^ vr) & 7) << 4);
+      *reinterpret_cast<uint4 *>(smem + SM::kS0 + off) = pack8(x0, x1);
+      *reinterpret_cast<uint4 *>(smem + SM::kDS + off) = pack8(y0, y1);
     }
-    vec(kVRowWq)[i] = rwq;
-    vec(kVRowWa)[i] = rwa;
-    vec(kVDbA)[i] = dba;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sds += __shfl_xor_sync(0xffffffffu, sds, o);
+    if (lane == 0) SC[4 + warp] = sds;
   }
-  __syncthreads();
-  if (tid < 64) {  // column sums (column j per thread)
-    const int j = tid;
-    float cwq = 0.f, cwa = 0.f;
-    for (int i = 0; i < 64; ++i) {
-      cwq += M1[i * kTT + j] * QK[i * kTT + j];
-      cwa += M2[i * kTT + j] * KK[i * kTT + j];
-    }
-    vec(kVColWq)[j] = cwq;
-    vec(kVColWa)[j] = cwa;
-  }
-  __syncthreads();
-  if (tid < 64) {  // Msym = Ma + Ma^T over K K^T (no longer needed)
-    const int i = tid;
-    for (int j = 0; j < 64; ++j) KK[i * kTT + j] = M2[i * kTT + j] + M2[j * kTT + i];
-  }
-  __syncthreads();
-
-  // ---- stage 4: dq and dk, thread tile 4 tokens x 8 k ----
-  const int tg = tid & 15, kg = tid >> 4;
-  const int tr0 = 4 * tg, kc0 = 8 * kg;
-  const float *dOT = T0, *dXT = T1, *DT = T2;
-  const float *EGv = vec(kVEG), *BTv = vec(kVBT), *EDv = vec(kVED);
-  const uint16_t *qh = q + hqk * kD + kc0;  // + token * kHQK * kD
-  const uint16_t *kh = k + hqk * kD + kc0;
-  auto row8 = [&](const uint16_t *base, int t, float (&f)[8]) {
-    unpack8(*reinterpret_cast<const uint4 *>(base + (t0 + t) * kHQK * kD), f);
-  };
-  // acc = A (rows tr0..) x B[128][128] (cols kc0..), A from a transposed tile
-  auto big_product = [&](const float *AT, const float *B, float (&acc)[4][8]) {
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int s = 0; s < 8; ++s) acc[r][s] = 0.f;
-#pragma unroll 2
-    for (int x = 0; x < 128; ++x) {
-      const float4 av = *reinterpret_cast<const float4 *>(AT + x * kTP + tr0);
-      const float4 b0 = __ldg(reinterpret_cast<const float4 *>(B + x * kD + kc0));
-      const float4 b1 = __ldg(reinterpret_cast<const float4 *>(B + x * kD + kc0 + 4));
-      const float ar[4] = {av.x, av.y, av.z, av.w};
-      const float bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int s = 0; s < 8; ++s) acc[r][s] += ar[r] * bs[s];
-    }
-  };
-  // dot partials of acc rows with q or k rows -> RED[slot][kg][t]
-  auto dot_partials = [&](const float (&acc)[4][8], const uint16_t *base, int slot) {
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int t = tr0 + r;
+  {  // dX (into [dO;dX]) and delta tiles; dv = beta dX; dX . v
+    const float *BT = vec(kVBT);
+    for (int idx = tid; idx < 64 * 16; idx += kBwdTcThreads) {
+      const int t = idx >> 4, vc = idx & 15;  // token, v = 8 vc .. 8 vc + 7
+      float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0, e0 = x0, e1 = x0;
       float p = 0.f;
       if (t < L) {
-        float f[8];
-        row8(base, t, f);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) p += acc[r][s] * f[s];
+        const int64_t row = ((t0 + t) * kHV + hv) * kD + 8 * vc;
+        x0 = *reinterpret_cast<const float4 *>(dx_ws + row);
+        x1 = *reinterpret_cast<const float4 *>(dx_ws + row + 4);
+        e0 = *reinterpret_cast<const float4 *>(delta_ws + row);
+        e1 = *reinterpret_cast<const float4 *>(delta_ws + row + 4);
+        const float bt = BT[t];
+        *reinterpret_cast<float4 *>(dv + row) = make_float4(bt * x0.x, bt * x0.y, bt * x0.z, bt * x0.w);
+        *reinterpret_cast<float4 *>(dv + row + 4) =
+            make_float4(bt * x1.x, bt * x1.y, bt * x1.z, bt * x1.w);
+        float vf[8];
+        unpack8(*reinterpret_cast<const uint4 *>(v + row), vf);
+        p = vf[0] * x0.x + vf[1] * x0.y + vf[2] * x0.z + vf[3] * x0.w + vf[4] * x1.x +
+            vf[5] * x1.y + vf[6] * x1.z + vf[7] * x1.w;
       }
-      RED[(slot * 16 + kg) * 64 + t] = p;
+      // the 16 chunks of token t are 16 consecutive lanes
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+      if ((lane & 15) == 0) vec(kVDXv)[t] = p;
+      const uint32_t ch = ((vc ^ t) & 7) << 4;
+      *reinterpret_cast<uint4 *>(smem + SM::kOX + (vc >> 3) * 16384 + 8192 + t * 128 + ch) =
+          pack8(x0, x1);
+      *reinterpret_cast<uint4 *>(smem + SM::kDL + (vc >> 3) * 8192 + t * 128 + ch) = pack8(e0, e1);
     }
-  };
-  float acc[4][8], out[4][8];
+  }
+  // TMA tiles landed; rows past the sequence end hold the next sequence's
+  // tokens: zero them
+  wait_phase(bar_tma, 0, broken);
+  if (L < kChunk) {
+    const int nz = kChunk - L;
+    for (int idx = tid; idx < 6 * nz * 8; idx += kBwdTcThreads) {
+      const int ch = idx & 7, r = L + (idx >> 3) % nz, which = (idx >> 3) / nz;  // 0..5
+      const int base = which < 4 ? SM::kQK + (which >> 1) * 16384 + (which & 1) * 8192
+                                 : SM::kOX + (which - 4) * 16384;
+      *reinterpret_cast<uint4 *>(smem + base + r * 128 + ch * 16) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + SM::kTmem);
 
-  // dq = scale e^G (dO S_0) + Mq K
-  big_product(dOT, S0, acc);
-  dot_partials(acc, qh, 0);  // rho_t = q_t . (S_0^T dO_t)
+  // ---- MMA batch 1: (a), (b); batch 2: (c), (d), (e) ----
+  if (tid == 0) {
+    const uint32_t id_kk = umma_idesc_bf16(128, 64, false, false);
+    const uint32_t id_mn = umma_idesc_bf16(128, 64, true, false);
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+      const uint32_t offd = (ks >> 2) * 8192 + (ks & 3) * 32;
+      umma_bf16(tmem + kTcA, umma_desc_sw128(s_base + SM::kQK + off, 16, 1024),
+                umma_desc_sw128(s_base + SM::kQK + 8192 + off, 16, 1024), id_kk, ks > 0);
+      umma_bf16(tmem + kTcB, umma_desc_sw128(s_base + SM::kOX + off, 16, 1024),
+                umma_desc_sw128(s_base + SM::kDL + offd, 16, 1024), id_kk, ks > 0);
+    }
+    umma_commit(bar_m1);
 #pragma unroll
-    for (int s = 0; s < 8; ++s) out[r][s] = scale * EGv[tr0 + r] * acc[r][s];
+    for (int ks = 0; ks < 8; ++ks) {  // K = v, 16 rows of the MN-major tiles per step
+      const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+      const uint32_t offd = (ks >> 2) * 8192 + (ks & 3) * 32;
+      const uint64_t s0 = umma_desc_sw128(s_base + SM::kS0 + ks * 2048, 16384, 1024);
+      umma_bf16(tmem + kTcP1, s0, umma_desc_sw128(s_base + SM::kOX + off, 16, 1024), id_mn, ks > 0);
+      umma_bf16(tmem + kTcP2, s0, umma_desc_sw128(s_base + SM::kOX + 8192 + off, 16, 1024), id_mn,
+                ks > 0);
+      umma_bf16(tmem + kTcP3, umma_desc_sw128(s_base + SM::kDS + ks * 2048, 16384, 1024),
+                umma_desc_sw128(s_base + SM::kDL + offd, 16, 1024), id_mn, ks > 0);
+    }
+    umma_commit(bar_m2);
+  }
+
+  // ---- Mq, Ma and their gate terms: row i = TMEM lane ----
+  wait_phase(bar_m1, 0, broken);
+  tc_fence_after();
+  const uint32_t tl = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+  {
+    const bool qside = warp < 2;  // lanes 0-63: QK, dO.delta; lanes 64-127: KK, dX.delta
+    const int i = 32 * (warp & 1) + lane;
+    const float gi = vec(kVG)[i], bi = vec(kVBT)[i];
+    float rsum = 0.f, dba = 0.f;
 #pragma unroll 1
-  for (int j = 0; j < L; ++j) {
-    float kv[8];
-    row8(kh, j, kv);
+    for (int h = 0; h < 2; ++h) {
+      float m[32], w[32];
+      tmem_ld32(tl + kTcA + 32 * h, m);  // QK or KK
+      tmem_ld32(tl + kTcB + 32 * h, w);  // dO.delta or dX.delta
+      tmem_wait_ld();
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float m = M1[(tr0 + r) * kTT + j];
-#pragma unroll
-      for (int s = 0; s < 8; ++s) out[r][s] += m * kv[s];
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-    if (tr0 + r < L) {
-      float *dst = dq + ((t0 + tr0 + r) * kHQK + hqk) * kD + kc0;
-#pragma unroll
-      for (int s = 0; s < 8; ++s) atomicAdd(dst + s, out[r][s]);
-    }
-
-  // dk = -beta e^G (dX S_0) + e^{G_C-G} (delta dS_C) + Mq^T Q + Msym K
-  big_product(dXT, S0, acc);
-  dot_partials(acc, kh, 1);  // xi_t = k_t . (S_0^T dX_t)
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int s = 0; s < 8; ++s) out[r][s] = -BTv[tr0 + r] * EGv[tr0 + r] * acc[r][s];
-  big_product(DT, dSC, acc);
-  dot_partials(acc, kh, 2);  // zeta_t = k_t . (dS_C^T delta_t)
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int s = 0; s < 8; ++s) out[r][s] += EDv[tr0 + r] * acc[r][s];
-#pragma unroll 1
-  for (int j = 0; j < L; ++j) {
-    float qv[8], kv[8];
-    row8(qh, j, qv);
-    row8(kh, j, kv);
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float mqt = M1[j * kTT + tr0 + r];   // Mq[j][t]
-      const float ms = KK[(tr0 + r) * kTT + j];  // Msym[t][j]
-#pragma unroll
-      for (int s = 0; s < 8; ++s) out[r][s] += mqt * qv[s] + ms * kv[s];
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-    if (tr0 + r < L) {
-      float *dst = dk + ((t0 + tr0 + r) * kHQK + hqk) * kD + kc0;
-#pragma unroll
-      for (int s = 0; s < 8; ++s) atomicAdd(dst + s, out[r][s]);
-    }
-
-  // ---- stage 5: dv, per-token dot products, <dS_C, S_0> ----
-  for (int idx = tid; idx < 64 * kD; idx += kBwdChunkThreads) {
-    const int t = idx >> 7, vv = idx & 127;
-    if (t < L) dv[((t0 + t) * kHV + hv) * kD + vv] = BTv[t] * dXT[vv * kTP + t];
-  }
-  {  // dX_t . v_t: four threads per token, 32 values each
-    const int t = tid >> 2, part = tid & 3;
-    float p = 0.f;
-    if (t < L) {
-      const uint16_t *vr = v + ((t0 + t) * kHV + hv) * kD + 32 * part;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float f[8];
-        unpack8(*reinterpret_cast<const uint4 *>(vr + 8 * u), f);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) p += f[s] * dXT[(32 * part + 8 * u + s) * kTP + t];
+      for (int u = 0; u < 32; ++u) {
+        const int j = 32 * h + u;
+        const float dec = expf(gi - vec(kVG)[j]);
+        float x;
+        if (qside) {
+          x = (i < L && j <= i) ? scale * dec * w[u] : 0.f;  // Mq
+        } else {
+          const float dA = -w[u];
+          x = (i < L && j < i) ? dA * bi * dec : 0.f;  // Ma
+          if (i < L && j < i) dba += dA * dec * m[u];
+          MA[i * 65 + j] = x;
+        }
+        w[u] = x;
+        m[u] *= x;  // W = M o (QK or KK)
+        rsum += m[u];
       }
-    }
-    p += __shfl_xor_sync(0xffffffffu, p, 1);
-    p += __shfl_xor_sync(0xffffffffu, p, 2);
-    if (part == 0) vec(kVDXv)[t] = p;
-  }
-  {  // <dS_C, S_0>: 64 consecutive values per thread, then a fixed-order reduction
-    const float4 *x = reinterpret_cast<const float4 *>(S0 + tid * 64);
-    const float4 *y = reinterpret_cast<const float4 *>(dSC + tid * 64);
-    float p = 0.f;
-#pragma unroll 4
-    for (int i = 0; i < 16; ++i) {
-      const float4 a4 = x[i], b4 = y[i];
-      p += a4.x * b4.x + a4.y * b4.y + a4.z * b4.z + a4.w * b4.w;
-    }
+      if (qside) {  // row i of Mq, columns 32 h .. 32 h + 31, as bf16
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-    if (lane == 0) SC[8 + warp] = p;
+        for (int cc = 0; cc < 4; ++cc)
+          *reinterpret_cast<uint4 *>(smem + SM::kMQ + i * 128 + (((4 * h + cc) ^ i) & 7) * 16) =
+              make_uint4(pack_bf16x2(w[8 * cc], w[8 * cc + 1]), pack_bf16x2(w[8 * cc + 2], w[8 * cc + 3]),
+                         pack_bf16x2(w[8 * cc + 4], w[8 * cc + 5]),
+                         pack_bf16x2(w[8 * cc + 6], w[8 * cc + 7]));
+      }
+      const float cs = warp_transpose_sum32(m, lane);  // column 32 h + lane over these 32 rows
+      red(warp, qside ? kRedColWq : kRedColWa)[32 * h + lane] = cs;
+    }
+    if (qside) {
+      vec(kVRowWq)[i] = rsum;
+    } else {
+      vec(kVRowWa)[i] = rsum;
+      vec(kVDbA)[i] = dba;
+    }
   }
   __syncthreads();
+  if (tid < 64) {  // Msym = Ma + Ma^T
+    const int i = tid;
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      float x[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = 8 * cc + u;
+        x[u] = MA[i * 65 + j] + MA[j * 65 + i];
+      }
+      *reinterpret_cast<uint4 *>(smem + SM::kMS + i * 128 + ((cc ^ i) & 7) * 16) =
+          make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
+                     pack_bf16x2(x[6], x[7]));
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  // ---- MMA batch 3: (f) K^T Mq^T; (g) Q^T Mq, (h) + K^T Msym ----
+  if (tid == 0) {
+    const uint32_t id_f = umma_idesc_bf16(128, 64, true, false);
+    const uint32_t id_g = umma_idesc_bf16(128, 64, true, true);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {  // K = 64 tokens
+      const uint64_t kt = umma_desc_sw128(s_base + SM::kQK + 8192 + ks * 2048, 16384, 1024);
+      const uint64_t qt = umma_desc_sw128(s_base + SM::kQK + ks * 2048, 16384, 1024);
+      umma_bf16(tmem + kTcF, kt, umma_desc_sw128(s_base + SM::kMQ + ks * 32, 16, 1024), id_f,
+                ks > 0);
+      umma_bf16(tmem + kTcGH, qt, umma_desc_sw128(s_base + SM::kMQ + ks * 2048, 8192, 1024), id_g,
+                ks > 0);
+    }
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+      umma_bf16(tmem + kTcGH, umma_desc_sw128(s_base + SM::kQK + 8192 + ks * 2048, 16384, 1024),
+                umma_desc_sw128(s_base + SM::kMS + ks * 32, 16, 1024), id_f, 1);
+    umma_commit(bar_m3);
+  }
+
+  // ---- per-token dot products with q and k: thread = k (TMEM lane) ----
+  wait_phase(bar_m2, 0, broken);
+  tc_fence_after();
+  const int kk = tid;  // k index of this thread's TMEM lane
+  const uint8_t *qtile = smem + SM::kQK + (kk >> 6) * 16384;
+  const uint8_t *ktile = qtile + 8192;
+#pragma unroll 1
+  for (int f = 0; f < 3; ++f) {
+    const uint32_t col = f == 0 ? kTcP1 : (f == 1 ? kTcP2 : kTcP3);
+    const uint8_t *tile = f == 0 ? qtile : ktile;
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      float x[32];
+      tmem_ld32(tl + col + 32 * h, x);
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; ++u) x[u] *= tile_at(tile, 32 * h + u, kk & 63);
+      red(warp, f)[32 * h + lane] = warp_transpose_sum32(x, lane);
+    }
+  }
+
+  // ---- dq, dk ----
+  wait_phase(bar_m3, 0, broken);
+  tc_fence_after();
+  {
+    const float *EG = vec(kVEG), *BT = vec(kVBT), *ED = vec(kVED);
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      float p[32], f[32];
+      tmem_ld32(tl + kTcP1 + 32 * h, p);
+      tmem_ld32(tl + kTcF + 32 * h, f);
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int t = 32 * h + u;
+        if (t < L) atomicAdd(dq + ((t0 + t) * kHQK + hqk) * kD + kk, scale * EG[t] * p[u] + f[u]);
+      }
+      float p3[32];
+      tmem_ld32(tl + kTcP2 + 32 * h, p);
+      tmem_ld32(tl + kTcGH + 32 * h, f);
+      tmem_ld32(tl + kTcP3 + 32 * h, p3);
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int t = 32 * h + u;
+        if (t < L)
+          atomicAdd(dk + ((t0 + t) * kHQK + hqk) * kD + kk,
+                    f[u] - BT[t] * EG[t] * p[u] + ED[t] * p3[u]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcCols);
+  }
+
+  // ---- gate gradients ----
   if (tid < 64) {
     const int t = tid;
     float rho = 0.f, xi = 0.f, zeta = 0.f;
-    for (int s = 0; s < 16; ++s) {
-      rho += RED[(0 * 16 + s) * 64 + t];
-      xi += RED[(1 * 16 + s) * 64 + t];
-      zeta += RED[(2 * 16 + s) * 64 + t];
+    for (int w = 0; w < 4; ++w) {
+      rho += red(w, kRedRho)[t];
+      xi += red(w, kRedXi)[t];
+      zeta += red(w, kRedZeta)[t];
     }
-    const float eg = EGv[t], bt = BTv[t], ed = EDv[t];
+    const float colwq = red(0, kRedColWq)[t] + red(1, kRedColWq)[t];
+    const float colwa = red(2, kRedColWa)[t] + red(3, kRedColWa)[t];
+    const float eg = vec(kVEG)[t], bt = vec(kVBT)[t], ed = vec(kVED)[t];
     float dG = 0.f, dB = 0.f;
     if (t < L) {
       dB = vec(kVDXv)[t] - eg * xi + vec(kVDbA)[t];
-      dG = scale * eg * rho + vec(kVRowWq)[t] - vec(kVColWq)[t] + vec(kVRowWa)[t] -
-           vec(kVColWa)[t] - bt * eg * xi - ed * zeta;
+      dG = scale * eg * rho + vec(kVRowWq)[t] - colwq + vec(kVRowWa)[t] - colwa -
+           bt * eg * xi - ed * zeta;
     }
     vec(kVZeta)[t] = t < L ? zeta : 0.f;
     vec(kVDG)[t] = dG;
@@ -644,23 +824,22 @@ gdn_prefill_bwd_chunk_kernel(const uint16_t *__restrict__ q, const uint16_t *__r
   }
   __syncthreads();
   if (tid == 0) {  // the chunk-end state depends on G_C
-    float sds = 0.f;
-    for (int w = 0; w < kBwdChunkThreads / 32; ++w) sds += SC[8 + w];
+    const float sds = SC[4] + SC[5] + SC[6] + SC[7];
     float extra = SC[0] * sds;
-    for (int j = 0; j < L; ++j) extra += EDv[j] * vec(kVZeta)[j];
+    for (int j = 0; j < L; ++j) extra += vec(kVED)[j] * vec(kVZeta)[j];
     vec(kVDG)[L - 1] += extra;
   }
   __syncthreads();
   if (tid < L) {
     const int t = tid;
     float dg = 0.f;  // g_t enters every G_s, s >= t, of the chunk
-    for (int s = t; s < L; ++s) dg += vec(kVDG)[s];
+    for (int s2 = t; s2 < L; ++s2) dg += vec(kVDG)[s2];
     const int64_t idx = (t0 + t) * kHV + hv;
     const float x = bf16_to_f32(a[idx]) + dt_bias[hv];
     const float ea = expf(A_log[hv]);
     const float sig = 1.0f / (1.0f + expf(-x));  // d softplus / dx
     const float gt = -ea * softplus_stable(x);
-    const float bt = BTv[t];
+    const float bt = vec(kVBT)[t];
     da[idx] = -dg * ea * sig;
     db[idx] = vec(kVDB)[t] * bt * (1.0f - bt);
     dgg_ws[idx] = dg * gt;
@@ -783,28 +962,29 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
   if (err != cudaSuccess) return err;
 
   // reverse scan
+  CUtensorMap tdo;
+  memset(&tdo, 0, sizeof(tdo));
+  if (T > 0 && !make_tmap_2d(&tdo, d_out, kHV * kD, T, 64, 64, true)) return cudaErrorInvalidValue;
   err = cudaFuncSetAttribute(gdn_prefill_bwd_scan_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, BwdScanSmem::kBytes);
   if (err != cudaSuccess) return err;
   gdn_prefill_bwd_scan_kernel<<<static_cast<unsigned>(N * kHV), kBwdScanThreads,
                                 BwdScanSmem::kBytes, stream>>>(
-      static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
-      static_cast<const uint16_t *>(d_out), d_final, cu_seqlens, meta, chunk_off, seq_order, gcum,
-      beta, m2, scale, dsc, dx, d_state);
+      tq, tk, tdo, d_final, cu_seqlens, meta, chunk_off, seq_order, gcum, beta, m2, scale, dsc, dx,
+      d_state);
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
 
   // chunk-parallel gradients
-  if (f.nt_max > 0) {
+  if (f.nt_max > 0 && T > 0) {
     err = cudaFuncSetAttribute(gdn_prefill_bwd_chunk_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, BwdChunkSmem::kBytes);
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, BwdTcSmem::kBytes);
     if (err != cudaSuccess) return err;
     dim3 grid(static_cast<unsigned>(f.nt_max), kHV);
-    gdn_prefill_bwd_chunk_kernel<<<grid, kBwdChunkThreads, BwdChunkSmem::kBytes, stream>>>(
-        static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
-        static_cast<const uint16_t *>(v), static_cast<const uint16_t *>(d_out), A_log,
-        static_cast<const uint16_t *>(a), dt_bias, cu_seqlens, meta, chunk_tab, gcum, beta,
-        states, dsc, delta, dx, scale, dq, dk, dv, da, db, dgg);
+    gdn_prefill_bwd_chunk_kernel<<<grid, kBwdTcThreads, BwdTcSmem::kBytes, stream>>>(
+        tq, tk, tdo, static_cast<const uint16_t *>(v), A_log, static_cast<const uint16_t *>(a),
+        dt_bias, cu_seqlens, meta, chunk_tab, gcum, beta, states, dsc, delta, dx, scale, dq, dk,
+        dv, da, db, dgg);
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
   }
