@@ -237,8 +237,8 @@ int gdn_prefill_qk4_v8_d128_k_last_noalloc(
  * recomputes the forward's chunk states itself.  dq/dk/dv/d_state/d_final
  * 16-byte aligned, da/db/dA_log/ddt_bias 4-byte aligned.  The workspace
  * (1024-byte aligned, gdn_prefill_backward_workspace_bytes(T, N) bytes) holds
- * the recomputed chunk-start states and their gradients: about
- * 2 x 512 KiB per 64-token chunk plus 8 KiB per token.  No host
+ * the recomputed chunk-start states and their gradients (bf16): about
+ * 2 x 256 KiB per 64-token chunk, plus 8 KiB per token.  No host
  * synchronisation; bad cu_seqlens are reported through the device status
  * (code 1) as in the forward.  Deterministic: identical inputs give
  * identical gradients bit for bit.

@@ -82,6 +82,30 @@ __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a -
 
 constexpr size_t kM2Bytes = 128 * 128;  // [PA ; Ainv] 128 rows x 64 bf16
 constexpr size_t kStateBytes = static_cast<size_t>(kHV) * kD * kD * sizeof(float);
+// a 128 x 128 state (one v-head) as a bf16 tensor-core operand image
+constexpr size_t kStateImgBytes = static_cast<size_t>(kD) * kD * 2;
+// 64 tokens x 128 values of one v-head (one chunk of delta or dX) as a bf16
+// K-major operand image: 2 v-blocks x 64 token rows x 128 B, 128-byte swizzle
+constexpr size_t kTokImgBytes = static_cast<size_t>(kChunk) * kD * 2;
+
+// element (t, v) of a token image
+__device__ __forceinline__ void put_tok_img(uint8_t *img, int t, int v, float x) {
+  *reinterpret_cast<__nv_bfloat16 *>(img + (v >> 6) * 8192 + t * 128 +
+                                     ((((v >> 3) ^ t) & 7) << 4) + (v & 7) * 2) =
+      __float2bfloat16_rn(x);
+}
+
+// Row `row` (v) of a state image, k = 64 hc .. 64 hc + 63 from x[]: the
+// MN-major operand layout (2 k-blocks x 128 v rows x 128 B, 128-byte
+// swizzle) that tcgen05 reads with k contiguous.
+__device__ __forceinline__ void put_state_img_row(uint8_t *img, int row, int hc, const float *x) {
+  uint8_t *r = img + hc * 16384 + row * 128;
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc)
+    *reinterpret_cast<uint4 *>(r + ((cc ^ (row & 7)) << 4)) =
+        make_uint4(pack_bf16x2(x[8 * cc], x[8 * cc + 1]), pack_bf16x2(x[8 * cc + 2], x[8 * cc + 3]),
+                   pack_bf16x2(x[8 * cc + 4], x[8 * cc + 5]), pack_bf16x2(x[8 * cc + 6], x[8 * cc + 7]));
+}
 
 // Segment length (chunks) chosen from T and N alone, so that the workspace
 // size is a function of (T, N): segment only when there are fewer scan
@@ -840,9 +864,10 @@ __device__ __forceinline__ void store16_bf16(uint8_t *base, int row, int c0, con
 
 // kSave = true is the backward pass's recompute: FULL items only, no outputs
 // and no final state; instead the state at the start of every chunk goes to
-// save_states[(global chunk) * 8 + hv] (fp32 [128 v][128 k]) and each token's
-// delta (V_new, the v-vector the WY system solves for) to
-// save_delta[(token * 8 + hv) * 128 + v] (fp32).
+// save_states + ((global chunk) * 8 + hv) * kStateImgBytes as a bf16 operand
+// image (put_state_img_row) and each chunk's delta (V_new, the v-vectors the
+// WY system solves for; 0 past the sequence end) to save_delta +
+// ((global chunk) * 8 + hv) * kTokImgBytes as a token image (put_tok_img).
 template <bool kSave>
 __global__ void __launch_bounds__(kScanThreads, 2)
 gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -856,7 +881,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         const int4 *__restrict__ items, int count_slot, int64_t seg_tokens,
                         const int *__restrict__ seg_off, float *seg_ss, float *seg_sb,
                         float *seg_phi, const int32_t *__restrict__ slots,
-                        float *__restrict__ save_states, float *__restrict__ save_delta) {
+                        uint8_t *__restrict__ save_states, uint8_t *__restrict__ save_delta) {
   using SM = ScanSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_align<1024>(smem_raw);
@@ -1040,13 +1065,9 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const uint32_t bar_k = bar_k0 + 8 * cb;
       GateRegs next_gates;
       if (tid < 64 && c + 1 < nchunks) next_gates = fetch_gates(c + 1);
-      if constexpr (kSave) {
-        float *dst = save_states + static_cast<int64_t>(gbase + c) * kHV * kD * kD + hv_off + srow;
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          *reinterpret_cast<float4 *>(dst + 4 * i) =
-              make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
-      }
+      if constexpr (kSave)
+        put_state_img_row(save_states + (static_cast<int64_t>(gbase + c) * kHV + hv) * kStateImgBytes,
+                          vrow, hc, s);
 
       // Q, K and [PA;Ainv] are read only by the tensor core, so only the MMA
       // thread waits for them: thread 0 re-arms each barrier for the next chunk
@@ -1184,10 +1205,10 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         tmem_wait_ld();
         if constexpr (kSave) {
           // thread (vrow, hc) holds V_new[vrow][tb .. tb+15]; a warp's store
-          // for one token covers 32 consecutive v (128 B)
+          // for one token covers 32 consecutive v (64 B)
+          uint8_t *img = save_delta + (static_cast<int64_t>(gbase + c) * kHV + hv) * kTokImgBytes;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (tb + j < L) save_delta[((t0 + tb + j) * kHV + hv) * kD + vrow] = zv[j];
+          for (int j = 0; j < 16; ++j) put_tok_img(img, tb + j, vrow, tb + j < L ? zv[j] : 0.f);
         }
   #pragma unroll
         for (int g = 0; g < 4; ++g) {

@@ -20,11 +20,12 @@
 //               Z   = e^{G_C-G} (dS K^T)                         [v x t]
 //               dX  = scale dO^T (P Ainv) + Z Ainv               [v x t]
 //               dS <- e^{G_C} dS + scale (e^G dO)^T Q - (beta e^G dX)^T K
-//             and stores dS (chunk end) per chunk and dX per token;
+//             and stores dS (chunk end) per chunk, dX per token (a bf16
+//             operand image) and dv = beta dX;
 //   bwd_chunk (one CTA per (chunk, v-head), all chunks at once):
 //               dq = scale e^G (dO S_0) + Mq K
 //               dk = Mq^T Q + (Ma + Ma^T) K + e^{G_C-G} (delta dS_C) - beta e^G (dX S_0)
-//               dv = beta dX,  dbeta,  dG -> dg (reverse cumsum in the chunk) -> da, db
+//               dbeta,  dG -> dg (reverse cumsum in the chunk) -> da, db
 //             with Mq = scale tril_incl(e^{G_i-G_j} dO_i.delta_j) and
 //                  Ma = strict_lower(-(dX_i.delta_j) beta_i e^{G_i-G_j});
 //   bwd_reduce: dA_log = sum_t dg_t g_t, ddt_bias = sum_t da_t.
@@ -48,17 +49,17 @@ struct PrefillBwdWs {
 inline PrefillBwdWs prefill_bwd_ws_layout(int64_t T, int64_t N) {
   PrefillBwdWs w;
   w.fwd = prefill_ws_layout(T, N, false);
-  const size_t chunk_states = static_cast<size_t>(w.fwd.nt_max) * kStateBytes;
-  const size_t token_vecs = static_cast<size_t>(T) * kHV * kD * sizeof(float);
+  const size_t chunk_states = static_cast<size_t>(w.fwd.nt_max) * kHV * kStateImgBytes;
+  const size_t chunk_toks = static_cast<size_t>(w.fwd.nt_max) * kHV * kTokImgBytes;
   size_t off = align_up(w.fwd.total, 1024);
-  w.states = off;  // fp32 [chunks][8][128][128]: state at each chunk start
+  w.states = off;  // [chunks][8] bf16 images (put_state_img_row): state at each chunk start
   off = align_up(off + chunk_states, 1024);
-  w.dsc = off;  // fp32 [chunks][8][128][128]: gradient of each chunk-end state
+  w.dsc = off;  // [chunks][8] bf16 images: gradient of each chunk-end state
   off = align_up(off + chunk_states, 1024);
-  w.delta = off;  // fp32 [T][8][128]
-  off = align_up(off + token_vecs, 1024);
-  w.dx = off;  // fp32 [T][8][128]
-  off = align_up(off + token_vecs, 1024);
+  w.delta = off;  // [chunks][8] token images (put_tok_img): delta
+  off = align_up(off + chunk_toks, 1024);
+  w.dx = off;  // [chunks][8] token images: dX
+  off = align_up(off + chunk_toks, 1024);
   w.dgg = off;  // fp32 [T][8]: dg_t * g_t
   off = align_up(off + static_cast<size_t>(T) * kHV * sizeof(float), 1024);
   w.total = off;
@@ -126,8 +127,8 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                             const int *__restrict__ meta, const int *__restrict__ chunk_off,
                             const int *__restrict__ seq_order, const float *__restrict__ gcum_ws,
                             const float *__restrict__ beta_ws, const uint8_t *__restrict__ m2_ws,
-                            float scale, float *__restrict__ dsc_ws, float *__restrict__ dx_ws,
-                            float *__restrict__ d_state) {
+                            float scale, uint8_t *__restrict__ dsc_ws, uint8_t *__restrict__ dx_ws,
+                            float *__restrict__ dv, float *__restrict__ d_state) {
   using SM = BwdScanSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_align<1024>(smem_raw);
@@ -229,13 +230,8 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
     const int64_t gc = gbase + c;
     const uint32_t kbuf = s_base + (cb ? SM::kK1 : SM::kK0);
-    {  // the chunk-end gradient, for the chunk-parallel kernel
-      float *dst = dsc_ws + gc * kHV * kD * kD + hv_off + srow;
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        *reinterpret_cast<float4 *>(dst + 4 * i) =
-            make_float4(ds[4 * i], ds[4 * i + 1], ds[4 * i + 2], ds[4 * i + 3]);
-    }
+    // the chunk-end gradient, as the chunk-parallel kernel's operand image
+    put_state_img_row(dsc_ws + (gc * kHV + hv) * kStateImgBytes, vrow, hc, ds);
     if (tid < 64) {
       const float gC = gcum_ws[(t0 + L - 1) * kHV + hv];
       float eg = 0.f, bt = 0.f, ed = 0.f;
@@ -335,7 +331,9 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     tc_fence_after();
     if (tid == 0 && c > 0) issue_img(c - 1);  // the image is consumed
 
-    // ---- dX: to the workspace (fp32) and -beta e^G dX -> K-major tile ----
+    // ---- dX: dv = beta dX (fp32), dX as the chunk kernel's token image,
+    // and -beta e^G dX -> K-major tile ----
+    uint8_t *dximg = dx_ws + (gc * kHV + hv) * kTokImgBytes;
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const int tb = 32 * hc + 16 * p;
@@ -345,8 +343,9 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int t = tb + j;
-        const float dx = scale * x[j];
-        if (t < L) dx_ws[((t0 + t) * kHV + hv) * kD + vrow] = dx;
+        const float dx = t < L ? scale * x[j] : 0.f;
+        put_tok_img(dximg, t, vrow, dx);
+        if (t < L) dv[((t0 + t) * kHV + hv) * kD + vrow] = BT[t] * dx;
         x[j] = -BT[t] * EG[t] * dx;
       }
       store16_bf16(zx, vrow, tb >> 3, x);
@@ -418,7 +417,8 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // One CTA (128 threads, the whole TMEM) per (chunk, v-head).  Eight MMAs on
 // bf16 operands, fp32 accumulators in TMEM:
 //   (a) [Q;K] K^T      -> QK (lanes 0-63), KK (lanes 64-127)      M=128 N=64 K=128
-//   (b) [dO;dX] delta^T -> dO.delta (lanes 0-63), dX.delta (64-127)
+//   (b) [dO;dX] [delta;V]^T -> dO.delta (lanes 0-63), dX.delta and dX.v
+//                          (lanes 64-127; the diagonal of dX.v is dX_t.v_t)  N=128
 //   (c) S_0^T dO^T = (dO S_0)^T        lanes k, columns t         M=128 N=64 K=128
 //   (d) S_0^T dX^T = (dX S_0)^T
 //   (e) dS_C^T delta^T = (delta dS_C)^T
@@ -426,22 +426,25 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 //   (g)+(h) Q^T Mq + K^T Msym = (Mq^T Q + Msym K)^T
 // S_0, dS_C ([v][k] in memory) and the Q and K tiles ([t][k]) enter (c)-(h)
 // as MN-major A operands (k contiguous), so nothing is transposed by hand.
+// Every input arrives by TMA (Q, K, dO, V tiles) or bulk copy (the S_0,
+// dS_C, delta and dX images the recompute and the reverse scan wrote).
 // Mq and Msym come from (a) and (b) by element-wise work on the CUDA cores
 // between the two MMA batches.
-constexpr int kBwdTcThreads = 128;
+constexpr int kBwdTcThreads = 256;  // warps w and w + 4 share TMEM lanes 32 (w & 3) ..
 
 struct BwdTcSmem {
   static constexpr int kQK = 0;        // [Q;K]: 2 d-blocks x (64 Q rows | 64 K rows) x 128 B (TMA)
   static constexpr int kOX = 32768;    // [dO;dX]: 2 v-blocks x (64 dO rows (TMA) | 64 dX rows) x 128 B
-  static constexpr int kDL = 65536;    // delta: 2 v-blocks x 64 rows x 128 B
-  static constexpr int kS0 = 81920;    // S_0 as MN-major A: 2 k-blocks x 128 v rows x 128 B
-  static constexpr int kDS = 114688;   // dS_C, same layout
-  static constexpr int kMQ = 147456;   // Mq bf16 [64 t][64 j], 128-byte rows
-  static constexpr int kMS = 155648;   // Msym bf16 [64][64]
-  static constexpr int kMA = 163840;   // Ma fp32 [64][65] (transpose staging)
+  static constexpr int kDV = 65536;    // [delta;V]: 2 v-blocks x (64 delta rows | 64 V rows (TMA)) x 128 B
+  static constexpr int kS0 = 98304;    // S_0 as MN-major A: 2 k-blocks x 128 v rows x 128 B
+  static constexpr int kDS = 131072;   // dS_C, same layout
+  static constexpr int kMQ = 163840;   // Mq bf16 [64 t][64 j], 128-byte rows
+  static constexpr int kMS = 172032;   // Msym bf16 [64][64]
+  static constexpr int kMA = 180224;   // Ma fp32 [64][65] (transpose staging)
   static constexpr int kVec = kMA + 64 * 65 * 4;     // per-token vectors: 16 x 64 fp32
-  static constexpr int kRed = kVec + 16 * 64 * 4;    // warp partials [4][5][64] fp32
-  static constexpr int kBar = kRed + 4 * 5 * 64 * 4;  // 4 mbarriers
+  static constexpr int kRed = kVec + 16 * 64 * 4;    // partials [4 lane quadrants][5][64] fp32
+  static constexpr int kRow = kRed + 4 * 5 * 64 * 4;  // row-sum halves [2][3][64] fp32
+  static constexpr int kBar = kRow + 2 * 3 * 64 * 4;  // 4 mbarriers
   static constexpr int kTmem = kBar + 32;
   static constexpr int kBroken = kBar + 36;
   static constexpr int kScal = kBar + 64;            // 16 fp32 scalars
@@ -450,8 +453,8 @@ struct BwdTcSmem {
 static_assert(BwdTcSmem::kMA + 64 * 65 * 4 <= BwdTcSmem::kVec, "layout");
 static_assert(BwdTcSmem::kBytes <= 227 * 1024, "shared memory");
 // TMEM columns
-constexpr uint32_t kTcA = 0, kTcB = 64, kTcP1 = 128, kTcP2 = 192, kTcP3 = 256, kTcF = 320,
-                   kTcGH = 384, kTcCols = 512;
+constexpr uint32_t kTcA = 0, kTcB = 64, kTcP1 = 192, kTcP2 = 256, kTcP3 = 320, kTcF = 384,
+                   kTcGH = 448, kTcCols = 512;
 // per-token vector slots and partial-sum families
 enum BwdVec : int {
   kVG = 0, kVEG, kVBT, kVED, kVRowWq, kVRowWa, kVDbA, kVDXv, kVZeta, kVDG, kVDB
@@ -489,16 +492,19 @@ __global__ void __launch_bounds__(kBwdTcThreads, 1)
 gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
                              const __grid_constant__ CUtensorMap tmap_k,
                              const __grid_constant__ CUtensorMap tmap_do,
-                             const uint16_t *__restrict__ v, const float *__restrict__ A_log,
+                             const __grid_constant__ CUtensorMap tmap_v,
+                             const float *__restrict__ A_log,
                              const uint16_t *__restrict__ a, const float *__restrict__ dt_bias,
                              const int64_t *__restrict__ cu, const int *__restrict__ meta,
                              const int2 *__restrict__ chunk_tab, const float *__restrict__ gcum_ws,
                              const float *__restrict__ beta_ws,
-                             const float *__restrict__ states_ws, const float *__restrict__ dsc_ws,
-                             const float *__restrict__ delta_ws, const float *__restrict__ dx_ws,
-                             float scale, float *__restrict__ dq, float *__restrict__ dk,
-                             float *__restrict__ dv, float *__restrict__ da,
-                             float *__restrict__ db, float *__restrict__ dgg_ws) {
+                             const uint8_t *__restrict__ states_ws,
+                             const uint8_t *__restrict__ dsc_ws,
+                             const uint8_t *__restrict__ delta_ws,
+                             const uint8_t *__restrict__ dx_ws, float scale,
+                             float *__restrict__ dq, float *__restrict__ dk,
+                             float *__restrict__ da, float *__restrict__ db,
+                             float *__restrict__ dgg_ws) {
   using SM = BwdTcSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_align<1024>(smem_raw);
@@ -509,9 +515,8 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const int64_t t0 = cu[e.x] + static_cast<int64_t>(e.y) * kChunk;
   const int L = static_cast<int>(lmin(kChunk, cu[e.x + 1] - t0));
   GDN_DCHECK(e.x >= 0 && e.x < meta[kMetaN] && L > 0 && t0 + L <= meta[kMetaT]);
-  const int64_t soff = (static_cast<int64_t>(g) * kHV + hv) * kD * kD;
-  const float *S0 = states_ws + soff;
-  const float *dSC = dsc_ws + soff;
+  const int64_t soff = (static_cast<int64_t>(g) * kHV + hv) * kStateImgBytes;
+  const int64_t toff = (static_cast<int64_t>(g) * kHV + hv) * kTokImgBytes;
 
   float *VEC = reinterpret_cast<float *>(smem + SM::kVec);
   float *RED = reinterpret_cast<float *>(smem + SM::kRed);
@@ -524,18 +529,24 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const uint32_t bar_tma = s_base + SM::kBar, bar_m1 = bar_tma + 8, bar_m2 = bar_tma + 16,
                  bar_m3 = bar_tma + 24;
 
-  // ---- TMA of the Q, K and dO tiles; TMEM ----
+  // ---- TMA of the Q, K, dO and V tiles, bulk copies of the images; TMEM ----
   if (warp == 0) tmem_alloc(s_base + SM::kTmem, kTcCols);
   if (tid == 0) {
     *broken = 0;
     for (int i = 0; i < 4; ++i) mbar_init(bar_tma + 8 * i, 1);
     mbar_init_fence();
-    mbar_arrive_expect_tx(bar_tma, 49152);
+    mbar_arrive_expect_tx(bar_tma, 65536 + 2 * static_cast<uint32_t>(kStateImgBytes) +
+                                       2 * static_cast<uint32_t>(kTokImgBytes));
+    bulk_load(s_base + SM::kS0, states_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_tma);
+    bulk_load(s_base + SM::kDS, dsc_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_tma);
     for (int blk = 0; blk < 2; ++blk) {
       const int y = static_cast<int>(t0);
       tma_load_2d(s_base + SM::kQK + blk * 16384, &tmap_q, hqk * kD + 64 * blk, y, bar_tma);
       tma_load_2d(s_base + SM::kQK + blk * 16384 + 8192, &tmap_k, hqk * kD + 64 * blk, y, bar_tma);
       tma_load_2d(s_base + SM::kOX + blk * 16384, &tmap_do, hv * kD + 64 * blk, y, bar_tma);
+      tma_load_2d(s_base + SM::kDV + blk * 16384 + 8192, &tmap_v, hv * kD + 64 * blk, y, bar_tma);
+      bulk_load(s_base + SM::kOX + blk * 16384 + 8192, dx_ws + toff + blk * 8192, 8192, bar_tma);
+      bulk_load(s_base + SM::kDV + blk * 16384, delta_ws + toff + blk * 8192, 8192, bar_tma);
     }
   }
   // ---- gates ----
@@ -557,63 +568,29 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   __syncthreads();
 
   // ---- operands written by the threads (bf16, 128-byte swizzle) ----
-  {  // S_0 and dS_C as MN-major tiles; <dS_C, S_0> on the way
+  // tiles and images landed; rows past the sequence end of the TMA tiles
+  // hold the next sequence's tokens: zero them (the images are zero there)
+  wait_phase(bar_tma, 0, broken);
+  {  // <dS_C, S_0> (the images share one layout)
     float sds = 0.f;
-    for (int idx = tid; idx < 128 * 16; idx += kBwdTcThreads) {
-      const int vr = idx >> 4, kc = idx & 15;  // v row, k = 8 kc .. 8 kc + 7
-      const float4 *x = reinterpret_cast<const float4 *>(S0 + vr * kD + 8 * kc);
-      const float4 *y = reinterpret_cast<const float4 *>(dSC + vr * kD + 8 * kc);
-      const float4 x0 = x[0], x1 = x[1], y0 = y[0], y1 = y[1];
-      sds += x0.x * y0.x + x0.y * y0.y + x0.z * y0.z + x0.w * y0.w + x1.x * y1.x +
-             x1.y * y1.y + x1.z * y1.z + x1.w * y1.w;
-      const uint32_t off = (kc >> 3) * 16384 + vr * 128 + (((kc ^ vr) & 7) << 4);
-      *reinterpret_cast<uint4 *>(smem + SM::kS0 + off) = pack8(x0, x1);
-      *reinterpret_cast<uint4 *>(smem + SM::kDS + off) = pack8(y0, y1);
+    for (int idx = tid; idx < static_cast<int>(kStateImgBytes / 16); idx += kBwdTcThreads) {
+      float x[8], y[8];
+      unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kS0 + 16 * idx), x);
+      unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kDS + 16 * idx), y);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sds += x[u] * y[u];
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sds += __shfl_xor_sync(0xffffffffu, sds, o);
-    if (lane == 0) SC[4 + warp] = sds;
+    if (lane == 0) SC[4 + warp] = sds;  // SC[4..11]
   }
-  {  // dX (into [dO;dX]) and delta tiles; dv = beta dX; dX . v
-    const float *BT = vec(kVBT);
-    for (int idx = tid; idx < 64 * 16; idx += kBwdTcThreads) {
-      const int t = idx >> 4, vc = idx & 15;  // token, v = 8 vc .. 8 vc + 7
-      float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0, e0 = x0, e1 = x0;
-      float p = 0.f;
-      if (t < L) {
-        const int64_t row = ((t0 + t) * kHV + hv) * kD + 8 * vc;
-        x0 = *reinterpret_cast<const float4 *>(dx_ws + row);
-        x1 = *reinterpret_cast<const float4 *>(dx_ws + row + 4);
-        e0 = *reinterpret_cast<const float4 *>(delta_ws + row);
-        e1 = *reinterpret_cast<const float4 *>(delta_ws + row + 4);
-        const float bt = BT[t];
-        *reinterpret_cast<float4 *>(dv + row) = make_float4(bt * x0.x, bt * x0.y, bt * x0.z, bt * x0.w);
-        *reinterpret_cast<float4 *>(dv + row + 4) =
-            make_float4(bt * x1.x, bt * x1.y, bt * x1.z, bt * x1.w);
-        float vf[8];
-        unpack8(*reinterpret_cast<const uint4 *>(v + row), vf);
-        p = vf[0] * x0.x + vf[1] * x0.y + vf[2] * x0.z + vf[3] * x0.w + vf[4] * x1.x +
-            vf[5] * x1.y + vf[6] * x1.z + vf[7] * x1.w;
-      }
-      // the 16 chunks of token t are 16 consecutive lanes
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-      if ((lane & 15) == 0) vec(kVDXv)[t] = p;
-      const uint32_t ch = ((vc ^ t) & 7) << 4;
-      *reinterpret_cast<uint4 *>(smem + SM::kOX + (vc >> 3) * 16384 + 8192 + t * 128 + ch) =
-          pack8(x0, x1);
-      *reinterpret_cast<uint4 *>(smem + SM::kDL + (vc >> 3) * 8192 + t * 128 + ch) = pack8(e0, e1);
-    }
-  }
-  // TMA tiles landed; rows past the sequence end hold the next sequence's
-  // tokens: zero them
-  wait_phase(bar_tma, 0, broken);
   if (L < kChunk) {
     const int nz = kChunk - L;
-    for (int idx = tid; idx < 6 * nz * 8; idx += kBwdTcThreads) {
-      const int ch = idx & 7, r = L + (idx >> 3) % nz, which = (idx >> 3) / nz;  // 0..5
-      const int base = which < 4 ? SM::kQK + (which >> 1) * 16384 + (which & 1) * 8192
-                                 : SM::kOX + (which - 4) * 16384;
+    for (int idx = tid; idx < 8 * nz * 8; idx += kBwdTcThreads) {
+      const int ch = idx & 7, r = L + (idx >> 3) % nz, which = (idx >> 3) / nz;  // 0..7
+      const int base = which < 4   ? SM::kQK + (which >> 1) * 16384 + (which & 1) * 8192
+                       : which < 6 ? SM::kOX + (which - 4) * 16384
+                                   : SM::kDV + (which - 6) * 16384 + 8192;
       *reinterpret_cast<uint4 *>(smem + base + r * 128 + ch * 16) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
@@ -626,86 +603,91 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   // ---- MMA batch 1: (a), (b); batch 2: (c), (d), (e) ----
   if (tid == 0) {
     const uint32_t id_kk = umma_idesc_bf16(128, 64, false, false);
+    const uint32_t id_kk2 = umma_idesc_bf16(128, 128, false, false);
     const uint32_t id_mn = umma_idesc_bf16(128, 64, true, false);
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-      const uint32_t offd = (ks >> 2) * 8192 + (ks & 3) * 32;
       umma_bf16(tmem + kTcA, umma_desc_sw128(s_base + SM::kQK + off, 16, 1024),
                 umma_desc_sw128(s_base + SM::kQK + 8192 + off, 16, 1024), id_kk, ks > 0);
       umma_bf16(tmem + kTcB, umma_desc_sw128(s_base + SM::kOX + off, 16, 1024),
-                umma_desc_sw128(s_base + SM::kDL + offd, 16, 1024), id_kk, ks > 0);
+                umma_desc_sw128(s_base + SM::kDV + off, 16, 1024), id_kk2, ks > 0);
     }
     umma_commit(bar_m1);
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {  // K = v, 16 rows of the MN-major tiles per step
       const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-      const uint32_t offd = (ks >> 2) * 8192 + (ks & 3) * 32;
       const uint64_t s0 = umma_desc_sw128(s_base + SM::kS0 + ks * 2048, 16384, 1024);
       umma_bf16(tmem + kTcP1, s0, umma_desc_sw128(s_base + SM::kOX + off, 16, 1024), id_mn, ks > 0);
       umma_bf16(tmem + kTcP2, s0, umma_desc_sw128(s_base + SM::kOX + 8192 + off, 16, 1024), id_mn,
                 ks > 0);
       umma_bf16(tmem + kTcP3, umma_desc_sw128(s_base + SM::kDS + ks * 2048, 16384, 1024),
-                umma_desc_sw128(s_base + SM::kDL + offd, 16, 1024), id_mn, ks > 0);
+                umma_desc_sw128(s_base + SM::kDV + off, 16, 1024), id_mn, ks > 0);
     }
     umma_commit(bar_m2);
   }
 
-  // ---- Mq, Ma and their gate terms: row i = TMEM lane ----
+  // ---- Mq, Ma and their gate terms: row i = TMEM lane, columns 32 hh.. ----
   wait_phase(bar_m1, 0, broken);
   tc_fence_after();
-  const uint32_t tl = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+  const int quad = warp & 3, hh = warp >> 2;
+  const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
+  float *ROW = reinterpret_cast<float *>(smem + SM::kRow);  // [hh][Wq | Wa | dbA][i]
   {
-    const bool qside = warp < 2;  // lanes 0-63: QK, dO.delta; lanes 64-127: KK, dX.delta
-    const int i = 32 * (warp & 1) + lane;
+    const bool qside = quad < 2;  // lanes 0-63: QK, dO.delta; lanes 64-127: KK, dX.delta
+    const int i = 32 * (quad & 1) + lane;
     const float gi = vec(kVG)[i], bi = vec(kVBT)[i];
     float rsum = 0.f, dba = 0.f;
-#pragma unroll 1
-    for (int h = 0; h < 2; ++h) {
-      float m[32], w[32];
-      tmem_ld32(tl + kTcA + 32 * h, m);  // QK or KK
-      tmem_ld32(tl + kTcB + 32 * h, w);  // dO.delta or dX.delta
-      tmem_wait_ld();
+    float m[32], w[32];
+    tmem_ld32(tl + kTcA + 32 * hh, m);  // QK or KK
+    tmem_ld32(tl + kTcB + 32 * hh, w);  // dO.delta or dX.delta
+    tmem_wait_ld();
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int j = 32 * h + u;
-        const float dec = expf(gi - vec(kVG)[j]);
-        float x;
-        if (qside) {
-          x = (i < L && j <= i) ? scale * dec * w[u] : 0.f;  // Mq
-        } else {
-          const float dA = -w[u];
-          x = (i < L && j < i) ? dA * bi * dec : 0.f;  // Ma
-          if (i < L && j < i) dba += dA * dec * m[u];
-          MA[i * 65 + j] = x;
-        }
-        w[u] = x;
-        m[u] *= x;  // W = M o (QK or KK)
-        rsum += m[u];
+    for (int u = 0; u < 32; ++u) {
+      const int j = 32 * hh + u;
+      const float dec = expf(gi - vec(kVG)[j]);
+      float x;
+      if (qside) {
+        x = (i < L && j <= i) ? scale * dec * w[u] : 0.f;  // Mq
+      } else {
+        const float dA = -w[u];
+        x = (i < L && j < i) ? dA * bi * dec : 0.f;  // Ma
+        if (i < L && j < i) dba += dA * dec * m[u];
+        MA[i * 65 + j] = x;
       }
-      if (qside) {  // row i of Mq, columns 32 h .. 32 h + 31, as bf16
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc)
-          *reinterpret_cast<uint4 *>(smem + SM::kMQ + i * 128 + (((4 * h + cc) ^ i) & 7) * 16) =
-              make_uint4(pack_bf16x2(w[8 * cc], w[8 * cc + 1]), pack_bf16x2(w[8 * cc + 2], w[8 * cc + 3]),
-                         pack_bf16x2(w[8 * cc + 4], w[8 * cc + 5]),
-                         pack_bf16x2(w[8 * cc + 6], w[8 * cc + 7]));
-      }
-      const float cs = warp_transpose_sum32(m, lane);  // column 32 h + lane over these 32 rows
-      red(warp, qside ? kRedColWq : kRedColWa)[32 * h + lane] = cs;
+      w[u] = x;
+      m[u] *= x;  // W = M o (QK or KK)
+      rsum += m[u];
     }
-    if (qside) {
-      vec(kVRowWq)[i] = rsum;
+    if (qside) {  // row i of Mq, columns 32 hh .. 32 hh + 31, as bf16
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        *reinterpret_cast<uint4 *>(smem + SM::kMQ + i * 128 + (((4 * hh + cc) ^ i) & 7) * 16) =
+            make_uint4(pack_bf16x2(w[8 * cc], w[8 * cc + 1]), pack_bf16x2(w[8 * cc + 2], w[8 * cc + 3]),
+                       pack_bf16x2(w[8 * cc + 4], w[8 * cc + 5]),
+                       pack_bf16x2(w[8 * cc + 6], w[8 * cc + 7]));
+      ROW[(hh * 3 + 0) * 64 + i] = rsum;
     } else {
-      vec(kVRowWa)[i] = rsum;
-      vec(kVDbA)[i] = dba;
+      ROW[(hh * 3 + 1) * 64 + i] = rsum;
+      ROW[(hh * 3 + 2) * 64 + i] = dba;
+      if (hh == (quad & 1)) {  // dX_i . v_i sits in this column half
+        float x[32];
+        tmem_ld32(tl + kTcB + 64 + 32 * hh, x);
+        tmem_wait_ld();
+        float d = 0.f;
+#pragma unroll
+        for (int u = 0; u < 32; ++u) d = u == lane ? x[u] : d;
+        vec(kVDXv)[i] = i < L ? d : 0.f;
+      }
     }
+    const float cs = warp_transpose_sum32(m, lane);  // column 32 hh + lane over these 32 rows
+    red(quad, qside ? kRedColWq : kRedColWa)[32 * hh + lane] = cs;
   }
   __syncthreads();
-  if (tid < 64) {  // Msym = Ma + Ma^T
-    const int i = tid;
+  {  // Msym = Ma + Ma^T: row i = tid & 63, 16 columns per thread
+    const int i = tid & 63, q4 = tid >> 6;
 #pragma unroll
-    for (int cc = 0; cc < 8; ++cc) {
+    for (int cc = 2 * q4; cc < 2 * q4 + 2; ++cc) {
       float x[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -742,25 +724,22 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     umma_commit(bar_m3);
   }
 
-  // ---- per-token dot products with q and k: thread = k (TMEM lane) ----
+  // ---- per-token dot products with q and k: thread = k (TMEM lane), tokens 32 hh.. ----
   wait_phase(bar_m2, 0, broken);
   tc_fence_after();
-  const int kk = tid;  // k index of this thread's TMEM lane
+  const int kk = 32 * quad + lane;  // k index of this thread's TMEM lane
   const uint8_t *qtile = smem + SM::kQK + (kk >> 6) * 16384;
   const uint8_t *ktile = qtile + 8192;
 #pragma unroll 1
   for (int f = 0; f < 3; ++f) {
     const uint32_t col = f == 0 ? kTcP1 : (f == 1 ? kTcP2 : kTcP3);
     const uint8_t *tile = f == 0 ? qtile : ktile;
-#pragma unroll 1
-    for (int h = 0; h < 2; ++h) {
-      float x[32];
-      tmem_ld32(tl + col + 32 * h, x);
-      tmem_wait_ld();
+    float x[32];
+    tmem_ld32(tl + col + 32 * hh, x);
+    tmem_wait_ld();
 #pragma unroll
-      for (int u = 0; u < 32; ++u) x[u] *= tile_at(tile, 32 * h + u, kk & 63);
-      red(warp, f)[32 * h + lane] = warp_transpose_sum32(x, lane);
-    }
+    for (int u = 0; u < 32; ++u) x[u] *= tile_at(tile, 32 * hh + u, kk & 63);
+    red(quad, f)[32 * hh + lane] = warp_transpose_sum32(x, lane);
   }
 
   // ---- dq, dk ----
@@ -768,29 +747,25 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   tc_fence_after();
   {
     const float *EG = vec(kVEG), *BT = vec(kVBT), *ED = vec(kVED);
-#pragma unroll 1
-    for (int h = 0; h < 2; ++h) {
-      float p[32], f[32];
-      tmem_ld32(tl + kTcP1 + 32 * h, p);
-      tmem_ld32(tl + kTcF + 32 * h, f);
-      tmem_wait_ld();
+    float p[32], f[32], p3[32];
+    tmem_ld32(tl + kTcP1 + 32 * hh, p);
+    tmem_ld32(tl + kTcF + 32 * hh, f);
+    tmem_wait_ld();
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int t = 32 * h + u;
-        if (t < L) atomicAdd(dq + ((t0 + t) * kHQK + hqk) * kD + kk, scale * EG[t] * p[u] + f[u]);
-      }
-      float p3[32];
-      tmem_ld32(tl + kTcP2 + 32 * h, p);
-      tmem_ld32(tl + kTcGH + 32 * h, f);
-      tmem_ld32(tl + kTcP3 + 32 * h, p3);
-      tmem_wait_ld();
+    for (int u = 0; u < 32; ++u) {
+      const int t = 32 * hh + u;
+      if (t < L) atomicAdd(dq + ((t0 + t) * kHQK + hqk) * kD + kk, scale * EG[t] * p[u] + f[u]);
+    }
+    tmem_ld32(tl + kTcP2 + 32 * hh, p);
+    tmem_ld32(tl + kTcGH + 32 * hh, f);
+    tmem_ld32(tl + kTcP3 + 32 * hh, p3);
+    tmem_wait_ld();
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int t = 32 * h + u;
-        if (t < L)
-          atomicAdd(dk + ((t0 + t) * kHQK + hqk) * kD + kk,
-                    f[u] - BT[t] * EG[t] * p[u] + ED[t] * p3[u]);
-      }
+    for (int u = 0; u < 32; ++u) {
+      const int t = 32 * hh + u;
+      if (t < L)
+        atomicAdd(dk + ((t0 + t) * kHQK + hqk) * kD + kk,
+                  f[u] - BT[t] * EG[t] * p[u] + ED[t] * p3[u]);
     }
   }
   tc_fence_before();
@@ -800,40 +775,53 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     tmem_dealloc(tmem, kTcCols);
   }
 
-  // ---- gate gradients ----
+  // ---- gate gradients (tokens t = tid < 64, two warps) ----
+  float dG = 0.f, dB = 0.f, ez = 0.f;
   if (tid < 64) {
     const int t = tid;
     float rho = 0.f, xi = 0.f, zeta = 0.f;
-    for (int w = 0; w < 4; ++w) {
-      rho += red(w, kRedRho)[t];
-      xi += red(w, kRedXi)[t];
-      zeta += red(w, kRedZeta)[t];
+    for (int q = 0; q < 4; ++q) {
+      rho += red(q, kRedRho)[t];
+      xi += red(q, kRedXi)[t];
+      zeta += red(q, kRedZeta)[t];
     }
     const float colwq = red(0, kRedColWq)[t] + red(1, kRedColWq)[t];
     const float colwa = red(2, kRedColWa)[t] + red(3, kRedColWa)[t];
+    const float rowwq = ROW[0 * 64 + t] + ROW[3 * 64 + t];
+    const float rowwa = ROW[1 * 64 + t] + ROW[4 * 64 + t];
+    const float dba = ROW[2 * 64 + t] + ROW[5 * 64 + t];
     const float eg = vec(kVEG)[t], bt = vec(kVBT)[t], ed = vec(kVED)[t];
-    float dG = 0.f, dB = 0.f;
     if (t < L) {
-      dB = vec(kVDXv)[t] - eg * xi + vec(kVDbA)[t];
-      dG = scale * eg * rho + vec(kVRowWq)[t] - colwq + vec(kVRowWa)[t] - colwa -
-           bt * eg * xi - ed * zeta;
+      dB = vec(kVDXv)[t] - eg * xi + dba;
+      dG = scale * eg * rho + rowwq - colwq + rowwa - colwa - bt * eg * xi - ed * zeta;
+      ez = ed * zeta;  // the chunk-end state depends on G_C through every token
     }
-    vec(kVZeta)[t] = t < L ? zeta : 0.f;
-    vec(kVDG)[t] = dG;
-    vec(kVDB)[t] = dB;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ez += __shfl_xor_sync(0xffffffffu, ez, o);
+    if (lane == 0) SC[12 + warp] = ez;
   }
   __syncthreads();
-  if (tid == 0) {  // the chunk-end state depends on G_C
-    const float sds = SC[4] + SC[5] + SC[6] + SC[7];
-    float extra = SC[0] * sds;
-    for (int j = 0; j < L; ++j) extra += vec(kVED)[j] * vec(kVZeta)[j];
-    vec(kVDG)[L - 1] += extra;
+  if (tid < 64) {
+    const int t = tid;
+    if (t == L - 1) {
+      float sds = 0.f;  // <dS_C, S_0>, eight warp partials in a fixed order
+      for (int w = 0; w < 8; ++w) sds += SC[4 + w];
+      dG += SC[0] * sds + SC[12] + SC[13];
+    }
+    // dg_t = sum_{s >= t} dG_s: suffix scan within each warp, then warp 1's total into warp 0
+    float x = dG;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_down_sync(0xffffffffu, x, o);
+      if (lane + o < 32) x += y;
+    }
+    if (t == 32) SC[14] = x;  // total of tokens 32..63
+    vec(kVDG)[t] = x;
   }
   __syncthreads();
   if (tid < L) {
     const int t = tid;
-    float dg = 0.f;  // g_t enters every G_s, s >= t, of the chunk
-    for (int s2 = t; s2 < L; ++s2) dg += vec(kVDG)[s2];
+    const float dg = vec(kVDG)[t] + (t < 32 ? SC[14] : 0.f);
     const int64_t idx = (t0 + t) * kHV + hv;
     const float x = bf16_to_f32(a[idx]) + dt_bias[hv];
     const float ea = expf(A_log[hv]);
@@ -841,7 +829,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const float gt = -ea * softplus_stable(x);
     const float bt = vec(kVBT)[t];
     da[idx] = -dg * ea * sig;
-    db[idx] = vec(kVDB)[t] * bt * (1.0f - bt);
+    db[idx] = dB * bt * (1.0f - bt);
     dgg_ws[idx] = dg * gt;
   }
 }
@@ -909,10 +897,10 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
   uint8_t *m2 = ws + f.m2;
   int4 *items = reinterpret_cast<int4 *>(ws + f.items);
   int *seg_off = reinterpret_cast<int *>(ws + f.seg_off);
-  float *states = reinterpret_cast<float *>(ws + w.states);
-  float *dsc = reinterpret_cast<float *>(ws + w.dsc);
-  float *delta = reinterpret_cast<float *>(ws + w.delta);
-  float *dx = reinterpret_cast<float *>(ws + w.dx);
+  uint8_t *states = ws + w.states;
+  uint8_t *dsc = ws + w.dsc;
+  uint8_t *delta = ws + w.delta;
+  uint8_t *dx = ws + w.dx;
   float *dgg = reinterpret_cast<float *>(ws + w.dgg);
 
   CUtensorMap tq, tk, tv;
@@ -971,20 +959,22 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
   gdn_prefill_bwd_scan_kernel<<<static_cast<unsigned>(N * kHV), kBwdScanThreads,
                                 BwdScanSmem::kBytes, stream>>>(
       tq, tk, tdo, d_final, cu_seqlens, meta, chunk_off, seq_order, gcum, beta, m2, scale, dsc, dx,
-      d_state);
+      dv, d_state);
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
 
   // chunk-parallel gradients
   if (f.nt_max > 0 && T > 0) {
+    CUtensorMap tvs;  // V with 128-byte swizzle, 64-wide boxes (the forward's map is unswizzled)
+    memset(&tvs, 0, sizeof(tvs));
+    if (!make_tmap_2d(&tvs, v, kHV * kD, T, 64, 64, true)) return cudaErrorInvalidValue;
     err = cudaFuncSetAttribute(gdn_prefill_bwd_chunk_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, BwdTcSmem::kBytes);
     if (err != cudaSuccess) return err;
     dim3 grid(static_cast<unsigned>(f.nt_max), kHV);
     gdn_prefill_bwd_chunk_kernel<<<grid, kBwdTcThreads, BwdTcSmem::kBytes, stream>>>(
-        tq, tk, tdo, static_cast<const uint16_t *>(v), A_log, static_cast<const uint16_t *>(a),
-        dt_bias, cu_seqlens, meta, chunk_tab, gcum, beta, states, dsc, delta, dx, scale, dq, dk,
-        dv, da, db, dgg);
+        tq, tk, tdo, tvs, A_log, static_cast<const uint16_t *>(a), dt_bias, cu_seqlens, meta,
+        chunk_tab, gcum, beta, states, dsc, delta, dx, scale, dq, dk, da, db, dgg);
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
   }
