@@ -403,6 +403,31 @@ __device__ __forceinline__ void img_put(uint8_t *img, int r, int c, float x) {
       __float2bfloat16_rn(x);
 }
 
+// Elements (r, c) and (r, c + 1) of the image, c even: one 32-bit store.
+__device__ __forceinline__ void img_put2(uint8_t *img, int r, int c, float x0, float x1) {
+  *reinterpret_cast<uint32_t *>(img + r * 128 + (((c >> 3) ^ (r & 7)) << 4) + (c & 7) * 2) =
+      pack_bf16x2(x0, x1);
+}
+
+// fp32 -> tf32 (round to nearest, ties away from zero), as a 32-bit pattern.
+__device__ __forceinline__ uint32_t f32_to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// d[16 x 8] += a[16 x 8] b[8 x 8], one warp, tf32 operands, fp32 accumulator.
+// Fragments (g = lane / 4, t = lane % 4): a = {(g, t), (g + 8, t), (g, t + 4),
+// (g + 8, t + 4)}, b = {(t, g), (t + 4, g)}, d = {(g, 2t), (g, 2t + 1),
+// (g + 8, 2t), (g + 8, 2t + 1)}.
+__device__ __forceinline__ void mma_tf32_m16n8k8(float (&d)[4], const uint32_t (&a)[4],
+                                                 const uint32_t (&b)[2]) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
 __device__ __forceinline__ void solve_diag_block_column(const float *AT, int c, int h,
                                                         uint32_t txs, uint8_t *img) {
   if (h == 1) {
@@ -600,8 +625,9 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     tmem_wait_ld();
 #pragma unroll 1
     for (int j = 0; j < 2; ++j) {
-      const float bi = Bs[j * 64 + i];
-      float dec = 1.f;  // e^{G_i - G_c} for the current column c (1 for c >= i)
+      // e^{G_i - G_c} for the current column c (1 for c >= i), times beta_i
+      // for the A rows (warps 2, 3)
+      float dec = warp >= 2 ? Bs[j * 64 + i] : 1.f;
       uint32_t prow[32];  // row i of P_j as bf16 pairs (warps 0,1)
 #pragma unroll
       for (int cc = 7; cc >= 0; --cc) {
@@ -619,7 +645,7 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int col = 8 * cc + u;
-            AT[(j * 64 + col) * 64 + i] = (rv && col < i) ? a8[u] * dc[u] * bi : 0.f;
+            AT[(j * 64 + col) * 64 + i] = (rv && col < i) ? a8[u] * dc[u] : 0.f;
           }
         } else {
           float vals[8];
@@ -655,69 +681,88 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     tc_fence_before();
     __syncthreads();  // every diagonal block solved: L11 and L22 are no longer read
     tc_fence_after();
-    // fp32 copies, row-major 32 x 32, into the retired L22 columns of A_j:
-    // X11 at ATj[32*64 ..), X22 at ATj[48*64 ..)
-    float *Xh = ATj + 32 * 64 + 1024 * h;
+    // Steps 2 and 3 are 32 x 32 x 32 products: warp-level TF32 MMAs
+    // (m16n8k8, fp32 accumulation) -- the reference merges its blocks in TF32
+    // too (kernel.py:718-737), and the result is rounded to bf16 below.
+    // Operands are laid out so that every fragment load below is free of
+    // bank conflicts:
+    //   X11^T in the retired L22 columns, rows padded to 36 floats:
+    //         X11T[n * 36 + k] = X11[k][n] (later T^T in the same place);
+    //   X22   row-major in the retired L11 area with an XOR-swizzled column:
+    //         X22[m][c] at ATj[m * 64 + (c ^ 4 (m & 7))].
+    float *X11T = ATj + 32 * 64;
     {
       float x[32];
-      tmem_ld32(txs + 32 * h, x);
+      tmem_ld32(txs + 32 * h, x);  // x[k] = X_hh[k][lane]
       tmem_wait_ld();
+      if (h == 0) {
+        float4 *dst = reinterpret_cast<float4 *>(X11T + lane * 36);
 #pragma unroll
-      for (int k = 0; k < 32; ++k) Xh[k * 32 + lane] = x[k];
+        for (int q = 0; q < 8; ++q)
+          dst[q] = make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) ATj[k * 64 + (lane ^ (4 * (k & 7)))] = x[k];
+      }
     }
     __syncthreads();
-    // step 2: T = L21 X11 (rows 16 h .. 16 h + 15 of column `lane`), with
-    // L21[r][k] = ATj[k * 64 + 32 + r]; T goes into the retired L11 area,
-    // row r at ATj[r * 64 + 0 .. 31]
-    {
-      const float *X11 = ATj + 32 * 64;
-      float t[16];
+    // fragment coordinates (PTX m16n8k8 .tf32 layout): g = lane / 4, t = lane % 4
+    const int g = lane >> 2, t4 = lane & 3;
+    // step 2: T = L21 X11, rows 16 h .. 16 h + 15 (this warp), all 32 columns;
+    // L21[r][k] = ATj[k * 64 + 32 + r]
+    float acc[4][4];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) t[i] = 0.f;
-#pragma unroll 4
-      for (int k = 0; k < 32; ++k) {
-        const float xk = X11[k * 32 + lane];
-        const float4 *l = reinterpret_cast<const float4 *>(ATj + k * 64 + 32 + 16 * h);
-        const float4 a0 = l[0], a1 = l[1], a2 = l[2], a3 = l[3];
-        t[0] += a0.x * xk;
-        t[1] += a0.y * xk;
-        t[2] += a0.z * xk;
-        t[3] += a0.w * xk;
-        t[4] += a1.x * xk;
-        t[5] += a1.y * xk;
-        t[6] += a1.z * xk;
-        t[7] += a1.w * xk;
-        t[8] += a2.x * xk;
-        t[9] += a2.y * xk;
-        t[10] += a2.z * xk;
-        t[11] += a2.w * xk;
-        t[12] += a3.x * xk;
-        t[13] += a3.y * xk;
-        t[14] += a3.z * xk;
-        t[15] += a3.w * xk;
+    for (int nt = 0; nt < 4; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    {
+      const float *l21 = ATj + 32 + 16 * h + g;
+#pragma unroll
+      for (int kt = 0; kt < 4; ++kt) {
+        const int k0 = 8 * kt;
+        const uint32_t af[4] = {f32_to_tf32(l21[(k0 + t4) * 64]), f32_to_tf32(l21[(k0 + t4) * 64 + 8]),
+                                f32_to_tf32(l21[(k0 + t4 + 4) * 64]),
+                                f32_to_tf32(l21[(k0 + t4 + 4) * 64 + 8])};
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const float *bp = X11T + (8 * nt + g) * 36 + k0 + t4;
+          const uint32_t bf[2] = {f32_to_tf32(bp[0]), f32_to_tf32(bp[4])};
+          mma_tf32_m16n8k8(acc[nt], af, bf);
+        }
+      }
+    }
+    __syncthreads();  // X11 fully read: T^T replaces it
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int n = 8 * nt + 2 * t4, m = 16 * h + g;
+      X11T[n * 36 + m] = acc[nt][0];
+      X11T[(n + 1) * 36 + m] = acc[nt][1];
+      X11T[n * 36 + m + 8] = acc[nt][2];
+      X11T[(n + 1) * 36 + m + 8] = acc[nt][3];
+    }
+    __syncthreads();
+    // step 3: X21 = -X22 T, rows 16 h .. 16 h + 15 -> image rows 32 .. 63,
+    // columns 0 .. 31 (rows m and m + 8 share the swizzle: (m & 7) = g)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    {
+      const int m = 16 * h + g;
+      const float *x22a = ATj + m * 64, *x22b = ATj + (m + 8) * 64;
+#pragma unroll
+      for (int kt = 0; kt < 4; ++kt) {
+        const int c0 = (8 * kt + t4) ^ (4 * g), c1 = (8 * kt + t4 + 4) ^ (4 * g);
+        const uint32_t af[4] = {f32_to_tf32(x22a[c0]), f32_to_tf32(x22b[c0]), f32_to_tf32(x22a[c1]),
+                                f32_to_tf32(x22b[c1])};
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const float *bp = X11T + (8 * nt + g) * 36 + 8 * kt + t4;
+          const uint32_t bf[2] = {f32_to_tf32(bp[0]), f32_to_tf32(bp[4])};
+          mma_tf32_m16n8k8(acc[nt], af, bf);
+        }
       }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) ATj[(16 * h + i) * 64 + lane] = t[i];
-    }
-    __syncthreads();
-    // step 3: X21 = -X22 T (rows 16 h .. 16 h + 15 of column `lane`) -> image
-    // rows 32 .. 63, columns 0 .. 31
-    {
-      const float *X22 = ATj + 48 * 64;
-      float tc[32];
-#pragma unroll
-      for (int k = 0; k < 32; ++k) tc[k] = ATj[k * 64 + lane];
-#pragma unroll 2
-      for (int i = 0; i < 16; ++i) {
-        const int r = 16 * h + i;
-        const float4 *xr = reinterpret_cast<const float4 *>(X22 + r * 32);
-        float s = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 a = xr[q];
-          s += a.x * tc[4 * q] + a.y * tc[4 * q + 1] + a.z * tc[4 * q + 2] + a.w * tc[4 * q + 3];
-        }
-        img_put(img, 32 + r, lane, -s);
+      for (int nt = 0; nt < 4; ++nt) {
+        const int c = 8 * nt + 2 * t4;
+        img_put2(img, 32 + m, c, -acc[nt][0], -acc[nt][1]);
+        img_put2(img, 40 + m, c, -acc[nt][2], -acc[nt][3]);
       }
     }
   }
