@@ -392,12 +392,12 @@ constexpr uint32_t kPrepTmemCols = 128;
 //   X21 = -X22 (L21 X11).
 // Step 1 (this function): thread (h, lane) solves column c = 32 h + lane of
 // its diagonal block X_hh by blocked forward substitution in fp32 (16-row
-// blocks; block 2h's x values wait in the thread's TMEM lane at columns
-// txs + 32 h .. for block 2h+1; A's rows are broadcast from shared memory),
-// and writes them as bf16 into the 64 x 64 Ainv image `img` (128-byte rows,
-// 128-byte swizzle), with the zeros above the diagonal block for h = 1.
-// Steps 2 and 3 (the two products) run in the kernel, split over all four
-// warps.
+// blocks, A's columns broadcast from shared memory; the coupling of the
+// second 16-row block to the first is one warp-level TF32 product), keeps
+// the x values in its TMEM lane (columns txs + 32 h ..) and writes them as
+// bf16 into the 64 x 64 Ainv image `img` (128-byte rows, 128-byte swizzle),
+// with the zeros above the diagonal block for h = 1.  Steps 2 and 3 (the two
+// products) run in the kernel, split over all four warps.
 __device__ __forceinline__ void img_put(uint8_t *img, int r, int c, float x) {
   *reinterpret_cast<__nv_bfloat16 *>(img + r * 128 + (((c >> 3) ^ (r & 7)) << 4) + (c & 7) * 2) =
       __float2bfloat16_rn(x);
@@ -428,12 +428,22 @@ __device__ __forceinline__ void mma_tf32_m16n8k8(float (&d)[4], const uint32_t (
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-__device__ __forceinline__ void solve_diag_block_column(const float *AT, int c, int h,
-                                                        uint32_t txs, uint8_t *img) {
+__device__ __forceinline__ void solve_diag_block_column(const float *AT, float *scr, int lane,
+                                                        int h, uint32_t txs, uint8_t *img) {
+  const int c = 32 * h + lane;
   if (h == 1) {
-#pragma unroll 4
-    for (int r = 0; r < 32; ++r) img_put(img, r, c, 0.f);
+    // rows 0..31, columns 32..63 of the image are zero: 16-byte stores
+#pragma unroll
+    for (int ch = 4; ch < 8; ++ch)
+      *reinterpret_cast<uint4 *>(img + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+          make_uint4(0u, 0u, 0u, 0u);
   }
+  // The warp's scratch `scr` holds 32 rows n of 16 floats: element k of row n
+  // at scr[(n >> 1) * 64 + (n & 1) * 16 + (k ^ 4 ((n >> 1) & 3))], a layout in
+  // which the fragment loads, the float4 row accesses and (up to two-way) the
+  // accumulator stores below are free of bank conflicts.
+  const int g = lane >> 2, t4 = lane & 3, sq = (lane >> 1) & 3;
+  float *srow = scr + (lane >> 1) * 64 + (lane & 1) * 16;
 #pragma unroll 1
   for (int bb = 0; bb < 2; ++bb) {
     const int r0 = 32 * h + 16 * bb;
@@ -441,31 +451,44 @@ __device__ __forceinline__ void solve_diag_block_column(const float *AT, int c, 
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = 0.f;
     if (bb == 1) {
-      // contribution of the block above, within the diagonal block
-      float xp[16];
-      tmem_ld16(txs + 32 * h, xp);
-      tmem_wait_ld();
+      // contribution of the block above, within the diagonal block, for the
+      // warp's 32 columns at once: acc = A[r0 .., 32 h ..] X[32 h .., c] as
+      // one 16 x 32 x 16 TF32 product (block 0's x values are in `scr`)
+      float d[4][4];
 #pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        const float4 *col = reinterpret_cast<const float4 *>(AT + (32 * h + jj) * 64 + r0);
-        const float4 a0 = col[0], a1 = col[1], a2 = col[2], a3 = col[3];
-        const float xj = xp[jj];
-        acc[0] += a0.x * xj;
-        acc[1] += a0.y * xj;
-        acc[2] += a0.z * xj;
-        acc[3] += a0.w * xj;
-        acc[4] += a1.x * xj;
-        acc[5] += a1.y * xj;
-        acc[6] += a1.z * xj;
-        acc[7] += a1.w * xj;
-        acc[8] += a2.x * xj;
-        acc[9] += a2.y * xj;
-        acc[10] += a2.z * xj;
-        acc[11] += a2.w * xj;
-        acc[12] += a3.x * xj;
-        acc[13] += a3.y * xj;
-        acc[14] += a3.z * xj;
-        acc[15] += a3.w * xj;
+      for (int nt = 0; nt < 4; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+#pragma unroll
+      for (int kt = 0; kt < 2; ++kt) {
+        const float *ap = AT + (32 * h + 8 * kt + t4) * 64 + r0 + g;
+        const uint32_t af[4] = {f32_to_tf32(ap[0]), f32_to_tf32(ap[8]), f32_to_tf32(ap[4 * 64]),
+                                f32_to_tf32(ap[4 * 64 + 8])};
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const int n = 8 * nt + g, s = 4 * ((n >> 1) & 3);
+          const float *bp = scr + (n >> 1) * 64 + (n & 1) * 16;
+          const uint32_t bf[2] = {f32_to_tf32(bp[(8 * kt + t4) ^ s]),
+                                  f32_to_tf32(bp[(8 * kt + t4 + 4) ^ s])};
+          mma_tf32_m16n8k8(d[nt], af, bf);
+        }
+      }
+      __syncwarp();  // every lane's fragment loads are done: reuse `scr` for D
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int n = 8 * nt + 2 * t4, s = 4 * ((n >> 1) & 3);
+        float *p = scr + (n >> 1) * 64;  // rows n (even) and n + 1
+        p[g ^ s] = d[nt][0];
+        p[16 + (g ^ s)] = d[nt][1];
+        p[(g + 8) ^ s] = d[nt][2];
+        p[16 + ((g + 8) ^ s)] = d[nt][3];
+      }
+      __syncwarp();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 v = *reinterpret_cast<const float4 *>(srow + 4 * (q ^ sq));
+        acc[4 * q] = v.x;
+        acc[4 * q + 1] = v.y;
+        acc[4 * q + 2] = v.z;
+        acc[4 * q + 3] = v.w;
       }
     }
     // inside the 16-row block, right-looking: x_jp is final once the rows
@@ -486,6 +509,13 @@ __device__ __forceinline__ void solve_diag_block_column(const float *AT, int c, 
         if (4 * q + 2 > jp) acc[4 * q + 2] += a.z * xb[jp];
         if (4 * q + 3 > jp) acc[4 * q + 3] += a.w * xb[jp];
       }
+    }
+    if (bb == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<float4 *>(srow + 4 * (q ^ sq)) =
+            make_float4(xb[4 * q], xb[4 * q + 1], xb[4 * q + 2], xb[4 * q + 3]);
+      __syncwarp();
     }
     uint32_t u[16];
 #pragma unroll
@@ -619,50 +649,65 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const int i = (warp & 1) * 32 + lane;
     const bool rv = i < L;
     const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
-    float acc[64];  // row i of Q K^T (warps 0,1) or K K^T (warps 2,3): one TMEM round trip
-    tmem_ld32(trow, *reinterpret_cast<float(*)[32]>(acc));
-    tmem_ld32(trow + 32, *reinterpret_cast<float(*)[32]>(acc + 32));
-    tmem_wait_ld();
+    // Rows 0..31 (warps 0 and 2) have no nonzero entry right of column 31:
+    // their P rows are zero there and their A rows are not stored there (that
+    // block of A is never read; the solve uses it as scratch).
+    auto rows = [&](auto upper_tag) {
+      constexpr bool kUpper = decltype(upper_tag)::value;
+      constexpr int kGroups = kUpper ? 4 : 8;  // 8-column groups that can be nonzero
+      float acc[8 * kGroups];  // row i of Q K^T (warps 0,1) or K K^T (warps 2,3)
+      tmem_ld32(trow, *reinterpret_cast<float(*)[32]>(acc));
+      if constexpr (!kUpper) tmem_ld32(trow + 32, *reinterpret_cast<float(*)[32]>(acc + 32));
+      tmem_wait_ld();
 #pragma unroll 1
-    for (int j = 0; j < 2; ++j) {
-      // e^{G_i - G_c} for the current column c (1 for c >= i), times beta_i
-      // for the A rows (warps 2, 3)
-      float dec = warp >= 2 ? Bs[j * 64 + i] : 1.f;
-      uint32_t prow[32];  // row i of P_j as bf16 pairs (warps 0,1)
+      for (int j = 0; j < 2; ++j) {
+        // e^{G_i - G_c} for the current column c (1 for c >= i), times beta_i
+        // for the A rows (warps 2, 3)
+        float dec = warp >= 2 ? Bs[j * 64 + i] : 1.f;
+        uint32_t prow[32];  // row i of P_j as bf16 pairs (warps 0,1)
 #pragma unroll
-      for (int cc = 7; cc >= 0; --cc) {
-        const float4 g0 = *reinterpret_cast<const float4 *>(Gn + j * 64 + 8 * cc);
-        const float4 g1 = *reinterpret_cast<const float4 *>(Gn + j * 64 + 8 * cc + 4);
-        const float gn[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        float dc[8];
+        for (int cc = kGroups - 1; cc >= 0; --cc) {
+          const float4 g0 = *reinterpret_cast<const float4 *>(Gn + j * 64 + 8 * cc);
+          const float4 g1 = *reinterpret_cast<const float4 *>(Gn + j * 64 + 8 * cc + 4);
+          const float gn[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+          float dc[8];
 #pragma unroll
-        for (int u = 7; u >= 0; --u) {
-          if (8 * cc + u < i) dec *= gn[u];
-          dc[u] = dec;
-        }
-        const float *a8 = acc + 8 * cc;
-        if (warp >= 2) {
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int col = 8 * cc + u;
-            AT[(j * 64 + col) * 64 + i] = (rv && col < i) ? a8[u] * dc[u] : 0.f;
+          for (int u = 7; u >= 0; --u) {
+            if (8 * cc + u < i) dec *= gn[u];
+            dc[u] = dec;
           }
-        } else {
-          float vals[8];
+          const float *a8 = acc + 8 * cc;
+          if (warp >= 2) {
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int col = 8 * cc + u;
-            vals[u] = (rv && col <= i) ? a8[u] * dc[u] : 0.f;
+            for (int u = 0; u < 8; ++u) {
+              const int col = 8 * cc + u;
+              AT[(j * 64 + col) * 64 + i] = (rv && col < i) ? a8[u] * dc[u] : 0.f;
+            }
+          } else {
+            float vals[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int col = 8 * cc + u;
+              vals[u] = (rv && col <= i) ? a8[u] * dc[u] : 0.f;
+            }
+            prow[4 * cc + 0] = pack_bf16x2(vals[0], vals[1]);
+            prow[4 * cc + 1] = pack_bf16x2(vals[2], vals[3]);
+            prow[4 * cc + 2] = pack_bf16x2(vals[4], vals[5]);
+            prow[4 * cc + 3] = pack_bf16x2(vals[6], vals[7]);
           }
-          prow[4 * cc + 0] = pack_bf16x2(vals[0], vals[1]);
-          prow[4 * cc + 1] = pack_bf16x2(vals[2], vals[3]);
-          prow[4 * cc + 2] = pack_bf16x2(vals[4], vals[5]);
-          prow[4 * cc + 3] = pack_bf16x2(vals[6], vals[7]);
         }
+        if constexpr (kUpper) {
+#pragma unroll
+          for (int k = 16; k < 32; ++k) prow[k] = 0u;
+        }
+        // D's columns 0..63 were read above; lanes 0..63 now keep P_0 | P_1
+        if (warp < 2) tmem_st32(trow + 32 * j, prow);
       }
-      // D's columns 0..63 were read above; lanes 0..63 now keep P_0 | P_1
-      if (warp < 2) tmem_st32(trow + 32 * j, prow);
-    }
+    };
+    if (warp & 1)
+      rows(std::false_type{});
+    else
+      rows(std::true_type{});
     tmem_wait_st();
   }
   tc_fence_before();
@@ -677,7 +722,9 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     uint8_t *img = ai + j * 8192;
     const uint32_t txs = tmem + (static_cast<uint32_t>(32 * warp) << 16) + 64;
     // step 1: diagonal blocks X11 (h = 0) and X22 (h = 1), in parallel
-    solve_diag_block_column(ATj, 32 * h + lane, h, txs, img);
+    // scratch of step 1: rows 0..31 of columns 32 + 16 h .. 47 + 16 h of A_j,
+    // the zero block above L22, which is neither written nor read
+    solve_diag_block_column(ATj, ATj + (32 + 16 * h) * 64, lane, h, txs, img);
     tc_fence_before();
     __syncthreads();  // every diagonal block solved: L11 and L22 are no longer read
     tc_fence_after();
