@@ -897,14 +897,18 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // warp / 4) owns row v = 32 q + l and column half h of every [v x 64] tile
 // (k-half h of the state).
 //   S      fp32 S[v][k] in registers (64 k per thread)
-//   TMEM   cols [0, 64)    bf16(S): A operand of MMA 1 (two bf16 per column)
+//   TMEM   cols [0, 64)    bf16(S): A operand of MMA 1 (two bf16 per column);
+//                          then V_new, then bf16 V_dec (A operand of MMA 3)
 //          cols [64, 128)  O_intra = X PA^T
-//          cols [128, 256) Yq | Yk, then Yq | V_new, then dS
+//          cols [128, 256) Yq | Yk, then Yq | bf16 X (A operand of MMA 2), then dS
+// Every A operand is read from TMEM (the TS form), so no intermediate goes
+// through shared memory; B operands (Q, K, [PA;Ainv]) are in shared memory.
 // Per chunk (t = token of the chunk, L valid tokens):
 //   MMA 1   Yq = S Q^T, Yk = S K^T                    M=128, N=64+64, K=128
-//           X[v][t] = beta_t (V[t][v] - e^{G_t} Yk[v][t]),  Yq[v][t] *= e^{G_t}
-//   MMA 2   O' = Yq + X PA^T,  V_new = X Ainv^T       M=128, N=64+64, K=64
-//           out[t][v] = scale O'[v][t];  V_dec[v][t] = e^{G_last - G_t} V_new[v][t]
+//           X[v][t] = beta_t (V[t][v] - e^{G_t} Yk[v][t])
+//   MMA 2   O_intra = X PA^T,  V_new = X Ainv^T       M=128, N=64+64, K=64
+//           out[t][v] = scale (e^{G_t} Yq[v][t] + O_intra[v][t]);
+//           V_dec[v][t] = e^{G_last - G_t} V_new[v][t]
 //   MMA 3   dS = V_dec K                               M=128, N=128,   K=64
 //           S = e^{G_last} S + dS,  bf16(S) -> TMEM
 // Operands arrive by TMA (Q and K tiles with 128-byte swizzle, V tile plain)
@@ -918,11 +922,10 @@ struct ScanSmem {
   static constexpr int kK0 = 16384;    // K tiles, same layout, double buffered
   static constexpr int kK1 = 32768;
   static constexpr int kM2 = 49152;    // [PA ; Ainv] image, 128 rows x 128 B
-  static constexpr int kXV = 65536;    // X, then V_dec: 128 v rows x 64 t, K-major (16 KB)
-  static constexpr int kV = 81920;     // V tile: 64 t rows x 128 v bf16, unswizzled (16 KB)
+  static constexpr int kV = 65536;     // V tile: 64 t rows x 128 v bf16, unswizzled (16 KB)
   // per-token gate factors of the current / next chunk, computed once per
   // chunk: e^{G_t}, beta_t, e^{G_last - G_t} (0 past the end), e^{G_last}
-  static constexpr int kG = 98304;     // float eG[2][64]
+  static constexpr int kG = 81920;     // float eG[2][64]
   static constexpr int kB = kG + 512;  // float beta[2][64]
   static constexpr int kDec = kB + 512;  // float eDec[2][64]
   static constexpr int kGl = kDec + 512;  // float eGlast[2]
@@ -934,9 +937,13 @@ struct ScanSmem {
   static constexpr int kBytes = kBar + 64 + 1024;  // + base alignment slack
   static constexpr uint32_t kTmemCols = 256;
   static constexpr uint32_t kColSb = 0, kColOi = 64, kColY = 128;
+  // bf16 operand images that MMA 2 and MMA 3 read from TMEM: X over the Yk
+  // columns (thread half hc: columns kColX + 32 hc .. + 15, two tokens per
+  // column), V_new and then V_dec over the bf16(S) columns
+  static constexpr uint32_t kColX = kColY + 64, kColVn = kColSb;
 };
 // the epilogue stages one 64 KB (n, hv) state over the Q, K and [PA;Ainv] tiles
-static_assert(ScanSmem::kQ == 0 && ScanSmem::kXV >= 65536, "state staging region");
+static_assert(ScanSmem::kQ == 0 && ScanSmem::kV >= 65536, "state staging region");
 
 // Writes 16 fp32 as bf16 into row `row`, 16-byte chunks c0, c0+1 of a
 // 128-byte swizzled operand.
@@ -1027,7 +1034,6 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   else if (mode == kItemIdent)
     fin = seg_state(seg_phi, seg);
 
-  uint8_t *xv = smem + SM::kXV;
   const uint16_t *vt = reinterpret_cast<const uint16_t *>(smem + SM::kV);
   float *Eg = reinterpret_cast<float *>(smem + SM::kG);
   float *Bs = reinterpret_cast<float *>(smem + SM::kB);
@@ -1216,7 +1222,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         ph_v ^= 1;
       }
 
-      // ---- X = beta (V - e^G Yk) -> smem ----
+      // ---- X = beta (V - e^G Yk) -> TMEM ----
   #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const int tb = 32 * hc + 16 * p;
@@ -1236,9 +1242,13 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
             yk[j] = bt[u] * (vv - eg[u] * yk[j]);
           }
         }
-        store16_bf16(xv, vrow, tb >> 3, yk);
+        // bf16 X into the Yk columns this thread has read (MMA 2's A operand)
+        uint32_t pk[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) pk[j] = pack_bf16x2(yk[2 * j], yk[2 * j + 1]);
+        tmem_st8(tlane + SM::kColX + 32 * hc + 8 * p, pk);
       }
-      fence_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
@@ -1251,14 +1261,14 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         if constexpr (kOut) {
   #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
-            umma_bf16(tmem + SM::kColOi, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
-                      umma_desc_sw128(s_base + SM::kM2 + ks * 32, 16, 1024), idesc_n64, ks > 0);
+            umma_bf16_ts(tmem + SM::kColOi, tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
+                         umma_desc_sw128(s_base + SM::kM2 + ks * 32, 16, 1024), idesc_n64, ks > 0);
         }
   #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          umma_bf16(tmem + SM::kColY + 64, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
-                    umma_desc_sw128(s_base + SM::kM2 + 8192 + ks * 32, 16, 1024), idesc_n64,
-                    ks > 0);
+          umma_bf16_ts(tmem + SM::kColVn, tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
+                       umma_desc_sw128(s_base + SM::kM2 + 8192 + ks * 32, 16, 1024), idesc_n64,
+                       ks > 0);
         umma_commit(bar_mma);
       }
       ph_m2 ^= 1;
@@ -1293,7 +1303,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
           }
         }
         float zv[16];
-        tmem_ld16(tlane + SM::kColY + 64 + tb, zv);
+        tmem_ld16(tlane + SM::kColVn + tb, zv);
         tmem_wait_ld();
         if constexpr (kSave) {
           // thread (vrow, hc) holds V_new[vrow][tb .. tb+15]; a warp's store
@@ -1309,9 +1319,13 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   #pragma unroll
           for (int u = 0; u < 4; ++u) zv[4 * g + u] *= ed[u];  // e^{G_last - G_t}, 0 past the end
         }
-        store16_bf16(xv, vrow, tb >> 3, zv);
+        // bf16 V_dec into the V_new columns this thread has read (MMA 3's A operand)
+        uint32_t pk[8];
+  #pragma unroll
+        for (int j = 0; j < 8; ++j) pk[j] = pack_bf16x2(zv[2 * j], zv[2 * j + 1]);
+        tmem_st8(tlane + SM::kColVn + 32 * hc + 8 * p, pk);
       }
-      fence_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
@@ -1320,8 +1334,8 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       if (tid == 0) {
   #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          umma_bf16(tmem + SM::kColY, umma_desc_sw128(s_base + SM::kXV + ks * 32, 16, 1024),
-                    umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), idesc_ds, ks > 0);
+          umma_bf16_ts(tmem + SM::kColY, tmem + SM::kColVn + 32 * (ks >> 1) + 8 * (ks & 1),
+                       umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), idesc_ds, ks > 0);
         umma_commit(bar_mma);
       }
       if (tid < 64 && c + 1 < nchunks) store_gates(next_gates, cb ^ 1);

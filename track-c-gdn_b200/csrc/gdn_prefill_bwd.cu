@@ -96,7 +96,8 @@ __device__ __forceinline__ void unpack8(const uint4 u, float (&f)[8]) {
 //   b:  dX / scale = dO^T (P Ainv) + (Z / scale) Ainv  [v x t]  cols 192..255
 //   c:  dS' = dO^T Q' - (beta e^G dX) K                [v x k]  cols 128..255
 // with Z = e^{G_C - G} Zr and Q' = scale e^G Q (built in place over the Q
-// tile); dO, the image and Q', K enter MMAs b and c as MN-major operands.
+// tile); dO, the image and Q', K enter MMAs b and c as MN-major operands,
+// Z / scale and -beta e^G dX as bf16 A operands in TMEM (columns 64..127).
 // Then dS <- e^{G_C} dS + dS'.
 constexpr int kBwdScanThreads = 256;
 
@@ -106,8 +107,7 @@ struct BwdScanSmem {
   static constexpr int kK1 = 32768;
   static constexpr int kDO = 49152;   // dO tile: 2 v-blocks x 64 t x 128 B
   static constexpr int kImg = 65536;  // [P Ainv ; Ainv] image, 128 rows x 128 B
-  static constexpr int kZX = 81920;   // Z / scale, then -beta e^G dX: [128 v][64 t] bf16, K-major
-  static constexpr int kEG = 98304;   // e^{G_t} (0 past the end)
+  static constexpr int kEG = 81920;   // e^{G_t} (0 past the end)
   static constexpr int kBT = kEG + 256;   // beta_t (0 past the end)
   static constexpr int kED = kBT + 256;   // e^{G_C - G_t} (0 past the end)
   static constexpr int kEGC = kED + 256;  // e^{G_C}
@@ -116,7 +116,9 @@ struct BwdScanSmem {
   static constexpr int kBroken = kBar + 52;
   static constexpr int kBytes = kBar + 64 + 1024;  // + base alignment slack
   static constexpr uint32_t kTmemCols = 256;
-  static constexpr uint32_t kColSb = 0, kColA = 128, kColB = 192;
+  // bf16 Z / scale, then -beta e^G dX: the TMEM A operand of MMAs b and c
+  // (thread half hc: columns kColZX + 32 hc .. + 15, two tokens per column)
+  static constexpr uint32_t kColSb = 0, kColZX = 64, kColA = 128, kColB = 192;
 };
 
 __global__ void __launch_bounds__(kBwdScanThreads, 2)
@@ -149,7 +151,6 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   float *ED = reinterpret_cast<float *>(smem + SM::kED);
   float *EGC = reinterpret_cast<float *>(smem + SM::kEGC);
   volatile int *broken = reinterpret_cast<volatile int *>(smem + SM::kBroken);
-  uint8_t *zx = smem + SM::kZX;
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar_mma = s_base + SM::kBar, bar_q = bar_mma + 8, bar_do = bar_mma + 16,
                  bar_img = bar_mma + 24, bar_k0 = bar_mma + 32;  // bar_k1 = bar_k0 + 8
@@ -307,9 +308,12 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) z[j] *= ED[tb + j] * inv_scale;
-      store16_bf16(zx, vrow, tb >> 3, z);
+      uint32_t pk[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pk[j] = pack_bf16x2(z[2 * j], z[2 * j + 1]);
+      tmem_st8(tlane + SM::kColZX + 32 * hc + 8 * p, pk);
     }
-    fence_async_smem();
+    tmem_wait_st();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -322,8 +326,8 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                   umma_desc_sw128(s_base + SM::kImg + ks * 2048, 8192, 1024), id_b1, ks > 0);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(tmem + SM::kColB, umma_desc_sw128(s_base + SM::kZX + ks * 32, 16, 1024),
-                  umma_desc_sw128(s_base + SM::kImg + 8192 + ks * 2048, 8192, 1024), id_b2, 1);
+        umma_bf16_ts(tmem + SM::kColB, tmem + SM::kColZX + 32 * (ks >> 1) + 8 * (ks & 1),
+                     umma_desc_sw128(s_base + SM::kImg + 8192 + ks * 2048, 8192, 1024), id_b2, 1);
       umma_commit(bar_mma);
     }
     wait_phase(bar_mma, ph_mma, broken);
@@ -348,9 +352,12 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         if (t < L) dv[((t0 + t) * kHV + hv) * kD + vrow] = BT[t] * dx;
         x[j] = -BT[t] * EG[t] * dx;
       }
-      store16_bf16(zx, vrow, tb >> 3, x);
+      uint32_t pk[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pk[j] = pack_bf16x2(x[2 * j], x[2 * j + 1]);
+      tmem_st8(tlane + SM::kColZX + 32 * hc + 8 * p, pk);
     }
-    fence_async_smem();
+    tmem_wait_st();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -363,8 +370,8 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                   umma_desc_sw128(s_base + SM::kQ + ks * 2048, 8192, 1024), id_c1, ks > 0);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(tmem + SM::kColA, umma_desc_sw128(s_base + SM::kZX + ks * 32, 16, 1024),
-                  umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), id_c2, 1);
+        umma_bf16_ts(tmem + SM::kColA, tmem + SM::kColZX + 32 * (ks >> 1) + 8 * (ks & 1),
+                     umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), id_c2, 1);
       umma_commit(bar_mma);
     }
     wait_phase(bar_mma, ph_mma, broken);
