@@ -1146,7 +1146,7 @@ def main():
                     help="b200: this build; reference: CPU restatement of the reference path; "
                          "triton: the reference's Triton kernels staged under baseline/_ref (1 GPU)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c4")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="device step only (profiling runs)")
