@@ -26,9 +26,12 @@
 //      beta and the 128x64 bf16 matrix [P Ainv ; Ainv] for both v-heads of the
 //      q/k head, written to the workspace in the exact shared-memory image the
 //      scan kernel feeds to the tensor core;
-//   3. gdn_prefill_scan_kernel   (one CTA per (sequence, v-head, v-slice))
-//      runs the inter-chunk scan with the fp32 state slice held in registers
-//      and a bf16 copy in shared memory as the MMA operand.
+//   3. gdn_prefill_scan_kernel   (one CTA per (work item, v-head)) runs the
+//      inter-chunk scan with the fp32 state held in registers and a bf16 copy
+//      in TMEM as the A operand of the first MMA (the other two MMAs take
+//      their A operands, X and V_dec, from TMEM as well);
+//   4. gdn_prefill_compose_kernel (segmented evaluation only) joins the
+//      segments' affine state maps in fp32.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
