@@ -10,6 +10,7 @@ MMAs on bf16 operands, as the forward does, and the backward reuses its bf16
 backward is also deterministic, and the autograd wrapper returns exactly the
 direct call's gradients.
 """
+import numpy as np
 import pytest
 import torch
 
@@ -73,6 +74,25 @@ def test_backward_matches_autograd_reference(gdn, lens, with_state, with_dfinal)
         ref0 = autograd_ref.prefill_grads(q, k, v, z, A_log, a, dt, b, cu.cpu().tolist(), None,
                                           d_out.float(), d_final)
         assert _rel(got["d_state"], ref0["d_state"]) < TOL
+
+
+@pytest.mark.parametrize("lens", [[600, 130]])
+def test_backward_with_slow_decay(gdn, lens):
+    """A_log in [-5, -2]: the state and its gradient stay large from chunk to
+    chunk, so the reverse scan's carried dS (and the chunk-start states the
+    recompute saves) are exercised."""
+    args, d_out, d_final = _case(17 + sum(lens), lens, True, True)
+    q, k, v, state, A_log, a, dt, b, cu = args
+    A_log = torch.from_numpy(
+        (np.random.default_rng(7).random(8, dtype=np.float32) * 3.0 - 5.0).astype(np.float32)
+    ).to(A_log.device)
+    args = (q, k, v, state, A_log, a, dt, b, cu)
+    got = gdn.prefill.backward(*args, None, d_out.cuda(), d_final.cuda())
+    ref = autograd_ref.prefill_grads(q, k, v, state, A_log, a, dt, b, cu.cpu().tolist(), None,
+                                     d_out.float(), d_final)
+    errs = {name: _rel(got[name], ref[name].view_as(got[name])) for name in NAMES}
+    print(lens, {n: f"{e:.2e}" for n, e in errs.items()})
+    assert all(e < TOL for e in errs.values()), errs
 
 
 def test_backward_is_deterministic(gdn):

@@ -107,6 +107,47 @@ def test_segmented_evaluation_matches_recurrence(gdn, lens, with_state):
         np.testing.assert_array_equal(s[0].cpu().numpy(), inp["state"][0])
 
 
+@pytest.mark.parametrize("lens", [[4096], [3000, 1500]])
+def test_segmented_composition_with_slow_decay(gdn, lens):
+    """With the benchmark gates a 256-token segment decays its state map Phi
+    to zero in fp32, so the composition S(p+1) = S(p) Phi(p) + B(p) reduces
+    to B(p).  Here A_log in [-5, -2] keeps the segment decay between e^-1.5
+    and e^-17, so the S(p) Phi(p) products carry the state across segments
+    and are checked against the recurrence."""
+    assert gdn._native.prefill_kernel_launches(sum(lens), len(lens)) == 5
+    inp = cases.prefill_inputs(seed=sum(lens) + 11, lens=lens, with_state=True)
+    inp["A_log"] = (np.random.default_rng(5).random(8, dtype=np.float32) * 3.0 - 5.0).astype(
+        np.float32)
+    o, s = _run(gdn, inp)
+    ro, rs = _oracle(inp)
+    f = bits_to_f32
+    _, cs = oracle.prefill_chunked(f(inp["q"]), f(inp["k"]), f(inp["v"]), inp["state"],
+                                   inp["A_log"], f(inp["a"]), inp["dt_bias"], f(inp["b"]),
+                                   inp["cu_seqlens"])
+    assert out_err(o, ro) <= 1.0
+    assert rel_fro(s.cpu().numpy(), rs) < STATE_TOL
+    assert rel_fro(s.cpu().numpy(), rs) <= 1.5 * rel_fro(cs, rs) + 1e-4
+
+
+def test_single_pass_with_slow_decay(gdn):
+    """Ragged sequences on the single-pass scan with A_log in [-5, -2]: the
+    state carried from chunk to chunk (and h0) stays large, so the inter-chunk
+    update of the scan is exercised, not only the intra-chunk terms."""
+    lens = [700, 5, 129, 64, 1000]
+    assert gdn._native.prefill_kernel_launches(sum(lens), len(lens)) == 3
+    inp = cases.prefill_inputs(seed=sum(lens) + 13, lens=lens, with_state=True)
+    inp["A_log"] = (np.random.default_rng(6).random(8, dtype=np.float32) * 3.0 - 5.0).astype(
+        np.float32)
+    o, s = _run(gdn, inp)
+    ro, rs = _oracle(inp)
+    f = bits_to_f32
+    _, cs = oracle.prefill_chunked(f(inp["q"]), f(inp["k"]), f(inp["v"]), inp["state"],
+                                   inp["A_log"], f(inp["a"]), inp["dt_bias"], f(inp["b"]),
+                                   inp["cu_seqlens"])
+    assert out_err(o, ro) <= 1.0
+    assert rel_fro(s.cpu().numpy(), rs) <= 1.5 * rel_fro(cs, rs) + 1e-4
+
+
 def test_segmented_state_error_not_worse_than_reference(gdn):
     inp = cases.prefill_inputs(seed=42, lens=[1500], with_state=True)
     assert gdn._native.prefill_kernel_launches(1500, 1) == 5
