@@ -948,22 +948,6 @@ struct ScanSmem {
 // the epilogue stages one 64 KB (n, hv) state over the Q, K and [PA;Ainv] tiles
 static_assert(ScanSmem::kQ == 0 && ScanSmem::kV >= 65536, "state staging region");
 
-// Writes 16 fp32 as bf16 into row `row`, 16-byte chunks c0, c0+1 of a
-// 128-byte swizzled operand.
-__device__ __forceinline__ void store16_bf16(uint8_t *base, int row, int c0, const float *x) {
-  uint4 a, b;
-  a.x = pack_bf16x2(x[0], x[1]);
-  a.y = pack_bf16x2(x[2], x[3]);
-  a.z = pack_bf16x2(x[4], x[5]);
-  a.w = pack_bf16x2(x[6], x[7]);
-  b.x = pack_bf16x2(x[8], x[9]);
-  b.y = pack_bf16x2(x[10], x[11]);
-  b.z = pack_bf16x2(x[12], x[13]);
-  b.w = pack_bf16x2(x[14], x[15]);
-  *reinterpret_cast<uint4 *>(base + sw128(row, c0)) = a;
-  *reinterpret_cast<uint4 *>(base + sw128(row, c0 + 1)) = b;
-}
-
 // kSave = true is the backward pass's recompute: FULL items only, no outputs
 // and no final state; instead the state at the start of every chunk goes to
 // save_states + ((global chunk) * 8 + hv) * kStateImgBytes as a bf16 operand
