@@ -369,9 +369,10 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
 // q/k head.  The [Q;K] tile arrives by TMA; D = [Q;K] K^T on the tensor core
 // gives Q K^T (TMEM lanes 0..63) and K K^T (lanes 64..127) at once; each
 // thread turns one row into P_j (bf16, parked in its own TMEM lane) or A_j
-// (fp32, shared memory); thread (j, c) solves column c of (I + A_j)^-1 by fp32
-// forward substitution; P moves into the retired A region and a second MMA
-// forms P_j Ainv_j.  Output per (chunk, v-head): the 16 KiB [P Ainv ; Ainv]
+// (fp32, shared memory); (I + A_j)^-1 is a 2 x 2 block inverse: thread
+// (j, c) solves column c of its 32 x 32 diagonal block by fp32 forward
+// substitution, and the block products run as warp-level TF32 MMAs; P moves
+// into the retired A region and a second MMA forms P_j Ainv_j.  Output per (chunk, v-head): the 16 KiB [P Ainv ; Ainv]
 // image in the scan kernel's shared-memory operand layout.  About 51 KB of
 // shared memory, 128 TMEM columns and 128 registers per thread: 4 CTAs/SM.
 constexpr int kPrepThreads = 128;
