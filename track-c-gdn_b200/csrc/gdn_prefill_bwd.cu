@@ -28,7 +28,8 @@
 //               dbeta,  dG -> dg (reverse cumsum in the chunk) -> da, db
 //             with Mq = scale tril_incl(e^{G_i-G_j} dO_i.delta_j) and
 //                  Ma = strict_lower(-(dX_i.delta_j) beta_i e^{G_i-G_j});
-//   bwd_reduce: dA_log = sum_t dg_t g_t, ddt_bias = sum_t da_t.
+//   bwd_reduce (two fixed-order stages): dA_log = sum_t dg_t g_t,
+//             ddt_bias = sum_t da_t.
 // Both kernels run their products on the tensor cores (bf16 operands, fp32
 // accumulators, as the forward) and the rest in fp32; the state gradient
 // itself is carried in fp32.  Every sum has a
@@ -41,9 +42,12 @@ namespace gdn {
 // ---------------------------------------------------------------------------
 // workspace
 // ---------------------------------------------------------------------------
+// token blocks of the first stage of the dA_log / ddt_bias reduction
+constexpr int kBwdRedBlocks = 256;
+
 struct PrefillBwdWs {
   PrefillWs fwd;  // the forward's layout without segmentation (prep, tables)
-  size_t states, delta, dsc, dx, dgg, total;
+  size_t states, delta, dsc, dx, dgg, red, total;
 };
 
 inline PrefillBwdWs prefill_bwd_ws_layout(int64_t T, int64_t N) {
@@ -62,6 +66,8 @@ inline PrefillBwdWs prefill_bwd_ws_layout(int64_t T, int64_t N) {
   off = align_up(off + chunk_toks, 1024);
   w.dgg = off;  // fp32 [T][8]: dg_t * g_t
   off = align_up(off + static_cast<size_t>(T) * kHV * sizeof(float), 1024);
+  w.red = off;  // fp32 [kBwdRedBlocks][8][2]: per-block partial sums of dg g and da
+  off = align_up(off + static_cast<size_t>(kBwdRedBlocks) * kHV * 2 * sizeof(float), 1024);
   w.total = off;
   return w;
 }
@@ -846,18 +852,59 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // ---------------------------------------------------------------------------
 constexpr int kBwdReduceThreads = 256;
 
+// dA_log = sum_t dg_t g_t and ddt_bias = sum_t da_t per v-head, in two fixed-
+// order stages (deterministic).  Stage 1: block b sums its contiguous token
+// range, thread (token slot ts, head h) reading the [T][8] arrays coalesced;
+// the four lanes of a warp that share h are combined by shuffles, the eight
+// warps in order.
 __global__ void __launch_bounds__(kBwdReduceThreads)
-gdn_prefill_bwd_reduce_kernel(const int *__restrict__ meta, const float *__restrict__ dgg_ws,
-                              const float *__restrict__ da, int64_t T, float *__restrict__ dA_log,
-                              float *__restrict__ ddt_bias) {
-  __shared__ float s1[kBwdReduceThreads / 32], s2[kBwdReduceThreads / 32];
-  const int hv = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+gdn_prefill_bwd_reduce_partial_kernel(const int *__restrict__ meta,
+                                      const float *__restrict__ dgg_ws,
+                                      const float *__restrict__ da, int64_t T,
+                                      float *__restrict__ red) {
+  __shared__ float s1[kBwdReduceThreads / 32][kHV], s2[kBwdReduceThreads / 32][kHV];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hv = tid & (kHV - 1), ts = tid / kHV;  // 32 tokens x 8 heads per pass
+  const int64_t per = (T + kBwdRedBlocks - 1) / kBwdRedBlocks;
+  const int64_t t_begin = static_cast<int64_t>(blockIdx.x) * per;
+  const int64_t t_end = t_begin + per < T ? t_begin + per : T;
   float x = 0.f, y = 0.f;
   if (meta[kMetaError] == 0)
-    for (int64_t t = tid; t < T; t += kBwdReduceThreads) {
+    for (int64_t t = t_begin + ts; t < t_end; t += kBwdReduceThreads / kHV) {
       x += dgg_ws[t * kHV + hv];
       y += da[t * kHV + hv];
     }
+  // lanes h, h + 8, h + 16, h + 24 hold head h
+  x += __shfl_xor_sync(0xffffffffu, x, 8);
+  y += __shfl_xor_sync(0xffffffffu, y, 8);
+  x += __shfl_xor_sync(0xffffffffu, x, 16);
+  y += __shfl_xor_sync(0xffffffffu, y, 16);
+  if (lane < kHV) {
+    s1[warp][lane] = x;
+    s2[warp][lane] = y;
+  }
+  __syncthreads();
+  if (tid < kHV) {
+    float a1 = 0.f, a2 = 0.f;
+    for (int w = 0; w < kBwdReduceThreads / 32; ++w) {
+      a1 += s1[w][tid];
+      a2 += s2[w][tid];
+    }
+    red[(static_cast<int64_t>(blockIdx.x) * kHV + tid) * 2] = a1;
+    red[(static_cast<int64_t>(blockIdx.x) * kHV + tid) * 2 + 1] = a2;
+  }
+}
+
+// Stage 2: one CTA per v-head sums the kBwdRedBlocks partials in a fixed
+// order.
+static_assert(kBwdRedBlocks == kBwdReduceThreads, "one partial per thread");
+__global__ void __launch_bounds__(kBwdReduceThreads)
+gdn_prefill_bwd_reduce_kernel(const float *__restrict__ red, float *__restrict__ dA_log,
+                              float *__restrict__ ddt_bias) {
+  __shared__ float s1[kBwdReduceThreads / 32], s2[kBwdReduceThreads / 32];
+  const int hv = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float x = red[(static_cast<int64_t>(tid) * kHV + hv) * 2];
+  float y = red[(static_cast<int64_t>(tid) * kHV + hv) * 2 + 1];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -882,7 +929,7 @@ gdn_prefill_bwd_reduce_kernel(const int *__restrict__ meta, const float *__restr
 // ---------------------------------------------------------------------------
 // launcher
 // ---------------------------------------------------------------------------
-int prefill_bwd_kernel_launches() { return 6; }
+int prefill_bwd_kernel_launches() { return 7; }
 
 cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, const float *state,
                                const float *A_log, const void *a, const float *dt_bias,
@@ -985,8 +1032,12 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
   }
-  gdn_prefill_bwd_reduce_kernel<<<kHV, kBwdReduceThreads, 0, stream>>>(meta, dgg, da, T, dA_log,
-                                                                      ddt_bias);
+  float *red = reinterpret_cast<float *>(ws + w.red);
+  gdn_prefill_bwd_reduce_partial_kernel<<<kBwdRedBlocks, kBwdReduceThreads, 0, stream>>>(
+      meta, dgg, da, T, red);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  gdn_prefill_bwd_reduce_kernel<<<kHV, kBwdReduceThreads, 0, stream>>>(red, dA_log, ddt_bias);
   return cudaGetLastError();
 }
 
