@@ -103,6 +103,61 @@ def prefill_lengths(kind: str) -> np.ndarray:
     raise ValueError(kind)
 
 
+def workload_config(workload: str, world: int) -> dict:
+    """The `config` of a bench line: the workload alone, so that every arm
+    (b200, reference, triton) prints the identical dict for the same
+    workload and N.  How an arm executes it goes under `execution`."""
+    wl = WORKLOADS[workload]
+    lengths = prefill_lengths(wl["prefill"]) if wl["prefill"] else np.zeros(0, np.int64)
+    tokens = wl["decode_batch"] * wl.get("decode_tokens", 1) + int(lengths.sum())
+    return {
+        "workload": wl["desc"],
+        "decode_batch": wl["decode_batch"],
+        "decode_tokens_per_request": wl.get("decode_tokens", 1),
+        "state_dtype": "bf16" if wl.get("state_bf16") else "fp32",
+        "prefill_sequences": len(lengths),
+        "prefill_tokens": int(lengths.sum()),
+        "l2": ("inputs larger than L2 (no flush needed)" if tokens > 20000 else
+               "inputs smaller than L2 (no flush)"),
+        "parallelism": (f"shard{world}: decode request blocks, prefill LPT by sequence"
+                        if world > 1 else "one GPU"),
+    }
+
+
+# Algorithmic work of one prefill call split between its two main kernels.
+# Per 64-token chunk and v-head the path does 5 (2 C^2 D) + 3 (2 C D^2) FLOP:
+# KK^T, QK^T and the W-side product (3 x 2 C^2 D) depend only on the chunk and
+# are the preparation kernel's; U, P v_new and the three state products W S^T,
+# K^T v_new, Q S^T (2 x 2 C^2 D + 3 x 2 C D^2) need the state and are the
+# scan's.  Bytes: the preparation reads q, k, a, b; the scan reads q, k, v
+# and writes the output, plus the initial / final states.
+PREP_FLOP_PER_TOKEN = 8 * 3 * 2 * 64 * 64 * 128 // 64          # 393,216
+SCAN_FLOP_PER_TOKEN = PREFILL_FLOP_PER_TOKEN - PREP_FLOP_PER_TOKEN  # 1,048,576
+PREP_BYTES_PER_TOKEN = 2 * HQK * D * 2 + 2 * HV * 2                # 2,080
+SCAN_BYTES_PER_TOKEN = 2 * HQK * D * 2 + 2 * HV * D * 2            # 6,144
+
+
+def roofline_entry(kernel: str, flop: float, nbytes: float, seconds: float, peaks: dict,
+                   traffic=None, sustained: bool = False) -> dict:
+    """Roofline position of one timed kernel (or call): the bound is whichever
+    of FLOP / tensor peak and bytes / HBM peak is longer; achieved and peak
+    are in that bound's unit, so frac = max(t_tensor, t_hbm) / measured."""
+    tc_peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    t_tc = flop / (tc_peak * 1e12)
+    t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9)
+    if t_tc >= t_hbm:
+        bound, achieved, peak, unit = "tensor", flop / seconds / 1e12, tc_peak, "TFLOP/s"
+        src = "bf16 sustained" if sustained else "bf16 burst"
+    else:
+        bound, achieved, peak, unit = "hbm", nbytes / seconds / 1e9, peaks["hbm_gbs"], "GB/s"
+        src = "hbm copy"
+    return {"kernel": kernel, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": max(t_tc, t_hbm) / seconds, "traffic": traffic,
+            "algorithmic_flop": flop, "algorithmic_bytes": nbytes,
+            "t_tensor_ms": t_tc * 1e3, "t_hbm_ms": t_hbm * 1e3, "measured_ms": seconds * 1e3,
+            "peak_source": f"{peaks['source']} {src}"}
+
+
 # ---------------------------------------------------------------------------
 # measured peaks
 # ---------------------------------------------------------------------------
@@ -376,6 +431,11 @@ def gpu_arm(args):
     stream = torch.cuda.current_stream(dev)
 
     ev = {k: [] for k in ("s", "d", "p", "g")}
+    # per-kernel events inside each timed prefill call (recorded by the
+    # library right after each of its launches, on this stream)
+    n_pre_launch = (gdn._native.prefill_kernel_launches(pre["T"], pre["N"])
+                    if pre is not None and pre["N"] > 0 else 0)
+    ev["k"] = []
 
     # decode and prefill are independent: with overlap on, decode runs on a
     # side stream next to the prefill (its CTAs fill SMs the prefill leaves
@@ -384,14 +444,14 @@ def gpu_arm(args):
     side = torch.cuda.Stream(dev) if overlap else stream
     ev["dside"] = []
 
-    dec_dst = dec_peer.rows_for_me() if dec_peer is not None else dec_out
-    fin_dst = fin_peer.rows_for_me() if fin_peer is not None else (pre["final"] if pre else None)
-
-    def decode():
+    def decode(dec_dst):
         with torch.cuda.stream(side):
             run_decode(gdn, dec, A_log, dt_bias, dec_dst)
 
     def step(record):
+        # this step's destinations (the peer results alternate two buffers)
+        dec_dst = dec_peer.rows_for_me() if dec_peer is not None else dec_out
+        fin_dst = fin_peer.rows_for_me() if fin_peer is not None else (pre["final"] if pre else None)
         if record:
             e = torch.cuda.Event(enable_timing=True)
             e.record(stream)
@@ -399,19 +459,23 @@ def gpu_arm(args):
         if overlap:
             side.wait_stream(stream)
         if dec is not None and not overlap:
-            decode()
+            decode(dec_dst)
         if record:
             e = torch.cuda.Event(enable_timing=True)
             e.record(stream)
             ev["d"].append(e)
         if pre is not None and pre["N"] > 0:
+            kev = None
+            if record and not overlap:
+                kev = [torch.cuda.Event(enable_timing=True) for _ in range(n_pre_launch)]
+                ev["k"].append(kev)
             gdn.prefill.prefill_into(pre["q"], pre["k"], pre["v"], pre["h0"], A_log, pre["a"],
                                      dt_bias, pre["b"], pre["cu"], None, pre["out"],
-                                     fin_dst, pre["ws"])
+                                     fin_dst, pre["ws"], events=kev)
         if overlap:
             # issued after the prefill, so its CTAs take the SMs the prefill's
             # kernels leave free (their tails and the gaps between them)
-            decode()
+            decode(dec_dst)
             if record:
                 e = torch.cuda.Event(enable_timing=True)
                 e.record(side)
@@ -422,7 +486,8 @@ def gpu_arm(args):
             e.record(stream)
             ev["p"].append(e)
         if peer is not None:
-            peer.publish()  # one all-reduce closes the step for both buffers (same group, stream)
+            # one all-reduce closes the step for both results (same group, stream)
+            peer.publish(*[r for r in (dec_peer, fin_peer) if r is not None and r is not peer])
         elif world > 1:
             if dec_out is not None or max_dec:
                 t = dec_out if dec_out is not None else torch.empty(0, Tdec, HV, D, dtype=torch.bfloat16, device=dev)
@@ -473,7 +538,30 @@ def gpu_arm(args):
     if status:
         raise SystemExit(f"device status {status} after the timed region")
 
+    # per-kernel mean durations of the prefill call (CUDA events the library
+    # records after each of its launches), max over ranks
+    # (one fixed-size reduction on every rank, whatever its own launch count)
+    knames = ["meta", "prep", "scan", "compose", "scan_pass3"]
+    local = np.full(len(knames), -1.0)
+    for i in range(min(n_pre_launch, len(knames)) if ev["k"] else 0):
+        durs = [(st if i == 0 else ks[i - 1]).elapsed_time(ks[i]) for st, ks in zip(ev["d"], ev["k"])]
+        local[i] = float(np.mean(durs))
+    if world > 1:
+        t = torch.tensor(local, dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        local = t.cpu().numpy()
+    kernel_ms = {n: float(x) for n, x in zip(knames, local) if x >= 0}
+
     peaks = load_peaks()
+    execution = {
+        "streams": ("decode on a side stream next to the prefill, joined each step" if overlap
+                    else "one stream (decode, then prefill)"),
+        "results": ("kernels store decode outputs + prefill final states into rank 0's buffers "
+                    "over NVLink (CUDA IPC), one 4-byte all-reduce per step" if peer is not None else
+                    "NCCL gather of decode outputs + prefill final states to rank 0"
+                    if world > 1 else "single GPU, results stay in place"),
+        "gather": gather_mode,
+    }
     result = {
         "metric": "GDN serving throughput (decode + prefill tokens/s, max-over-ranks device time)",
         "value": total_tokens / (ms_step / 1e3),
@@ -487,28 +575,11 @@ def gpu_arm(args):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded; the benchmark configs' value distributions)",
-        "config": {
-            "workload": wl["desc"],
-            "decode_batch": B_total,
-            "decode_tokens_per_request": Tdec,
-            "state_dtype": "bf16" if wl.get("state_bf16") else "fp32",
-            "prefill_sequences": int(sum(seq_counts)) if wl["prefill"] else 0,
-            "prefill_tokens": total_prefill_tokens,
-            "l2": "inputs larger than L2 (no flush needed)" if total_tokens > 20000 else
-                  "inputs smaller than L2 (no flush)",
-            "streams": ("decode on a side stream next to the prefill, joined each step" if overlap
-                        else "one stream (decode, then prefill)"),
-            "parallelism": f"shard{world}: decode request blocks, prefill LPT by sequence; "
-                           + ("kernels store decode outputs + prefill final states into rank 0's "
-                              "buffers over NVLink (CUDA IPC), one 4-byte all-reduce per step"
-                              if peer is not None else
-                              "NCCL gather of decode outputs + prefill final states to rank 0"
-                              if world > 1 else "no collective"),
-            "gather": gather_mode,
-        },
-        "gpu_launches": args.steps * ((1 if dec is not None else 0) +
-                                      (gdn._native.prefill_kernel_launches(pre["T"], pre["N"]) if pre else 0)),
+        "config": workload_config(args.workload, world),
+        "execution": execution,
+        "gpu_launches": args.steps * ((1 if dec is not None else 0) + n_pre_launch),
         "phases_ms": {"decode": d_ms_max, "prefill": p_ms_max, "gather": g_ms_max},
+        "prefill_kernels_ms": kernel_ms,
         "clocks": clocks,
     }
     if dec is not None:
@@ -524,15 +595,31 @@ def gpu_arm(args):
     if pre is not None:
         flops = pre["T"] * PREFILL_FLOP_PER_TOKEN
         tflops = flops / (p_ms / 1e3) / 1e12
+        n_states = pre["N"] * (2 if pre["h0"] is not None else 1)   # h0 read (if given), final written
         result["prefill"] = {"tokens_per_s": total_prefill_tokens / (p_ms_max / 1e3),
                              "tflops_rank0": tflops, "tokens_rank0": pre["T"]}
-        result["roofline"] = {
-            "kernel": "prefill (meta + prep + scan launches of one prefill call)",
-            "bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops_sustained"],
-            "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops_sustained"],
-            "traffic": load_traffic(args.workload).get("prefill_bytes_per_launch"),
-            "algorithmic_bytes": pre["T"] * PREFILL_BYTES_PER_TOKEN + 2 * pre["N"] * STATE_BYTES,
-            "peak_source": peaks["source"] + " bf16 sustained"}
+        traffic = load_traffic(args.workload)
+        # the prefill call (all its launches) is the hot path's one "launch";
+        # the timed region is well under a second, so the burst peaks apply
+        result["roofline"] = roofline_entry(
+            "prefill call (meta + prep + scan" + (" + compose + scan pass 3" if n_pre_launch == 5 else "")
+            + " launches)", flops, pre["T"] * PREFILL_BYTES_PER_TOKEN + n_states * STATE_BYTES,
+            p_ms / 1e3, peaks, traffic.get("prefill_bytes_per_launch"))
+        per_kernel = {}
+        if "prep" in kernel_ms:
+            per_kernel["prep"] = roofline_entry(
+                "gdn_prefill_prep_kernel", pre["T"] * PREP_FLOP_PER_TOKEN,
+                pre["T"] * PREP_BYTES_PER_TOKEN, kernel_ms["prep"] / 1e3, peaks,
+                traffic.get("prep_bytes_per_launch"))
+        if "scan" in kernel_ms:
+            scan_s = (kernel_ms["scan"] + kernel_ms.get("scan_pass3", 0.0)) / 1e3
+            per_kernel["scan"] = roofline_entry(
+                "gdn_prefill_scan_kernel" + (" (both passes)" if "scan_pass3" in kernel_ms else ""),
+                pre["T"] * SCAN_FLOP_PER_TOKEN,
+                pre["T"] * SCAN_BYTES_PER_TOKEN + n_states * STATE_BYTES, scan_s, peaks,
+                traffic.get("scan_bytes_per_launch"))
+        if per_kernel:
+            result["roofline_kernels"] = per_kernel
     elif dec is not None:
         result["roofline"] = result.pop("roofline_decode")
 
@@ -541,6 +628,13 @@ def gpu_arm(args):
         result["e2e"] = e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world,
                                 max_over_ranks, barrier, total_tokens)
 
+    if world == 1 and not args.no_triton:
+        ours = {"step_ms": ms_step, "decode_ms": d_ms_max, "prefill_ms": p_ms_max}
+        try:
+            result["triton_reference"] = triton_reference_block(
+                torch, gdn, args, dev, A_log, dt_bias, dec, pre, ours)
+        except Exception as e:  # noqa: BLE001 -- the reference's kernels are not ours to fix
+            result["triton_reference"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_seconds)
     for res in (dec_peer, fin_peer):
@@ -848,8 +942,9 @@ def e2e_run(torch, gdn, args, dec, pre, A_log, dt_bias, dev, world, max_over_ran
 # CPU oracle (reported baseline and the reference arm)
 # ---------------------------------------------------------------------------
 def _bf16_bits(x: np.ndarray) -> np.ndarray:
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    # round to nearest even; 32-bit arithmetic cannot overflow for finite inputs
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    return ((u + np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1))) >> 16).astype(np.uint16)
 
 
 def _cpu_decode_inputs(rng, B, T=1):
@@ -879,9 +974,14 @@ def _cpu_prefill_inputs(rng, lengths, with_state):
                 if with_state else None, cu=cu, T=T)
 
 
-class CpuOracleTimer:
-    """Times the oracle on samples of a workload; extrapolates the time of one
-    full step as decode_time_per_request * B + prefill_time_per_token * T."""
+class CpuStepSampler:
+    """Times the CPU oracle (the reference recurrence restated in C, OpenMP
+    over all host threads) on sample steps of a workload.  Sample step j is
+    1/k of the workload's step with the same decode : prefill mix: decode of
+    B/k requests (T tokens each) and prefill of the sequences j mod k,
+    j mod k + k, j mod k + 2k, ... of the workload's length list.  Its tokens/s
+    is therefore that of the full step's mix, measured directly (nothing is
+    extrapolated); the full step would take about k times one sample step."""
 
     def __init__(self, workload: str):
         import oracle
@@ -889,92 +989,111 @@ class CpuOracleTimer:
         self.threads = oracle.default_threads()
         self.wl = WORKLOADS[workload]
         self.lengths = prefill_lengths(self.wl["prefill"]) if self.wl["prefill"] else None
+        B = self.wl["decode_batch"]
+        if self.lengths is not None:
+            self.k = 64 if len(self.lengths) >= 64 else 1
+        else:
+            self.k = max(1, B // 64)
+        self.dec_req = B // self.k if B else 0
+        self.dec_T = self.wl.get("decode_tokens", 1)
         self.rng = np.random.default_rng(77)
         self.A_log = (self.rng.random(HV, dtype=np.float32) * 2.7).astype(np.float32)
         self.dt = (self.rng.standard_normal(HV, dtype=np.float32) * 0.1).astype(np.float32)
-        self.dec_s = self.dec_n = self.pre_s = self.pre_n = 0.0
-        self.next_seq = 0
-        self.dec_sample = 64
-        self.dec_T = self.wl.get("decode_tokens", 1)
+        self.j = 0
+        self.times = []      # seconds per timed sample step
+        self.tokens = []     # tokens per timed sample step
+        self.seqs_seen = set()
 
-    def sample(self):
-        if self.wl["decode_batch"]:
-            inp = _cpu_decode_inputs(self.rng, self.dec_sample, self.dec_T)
-            t = time.perf_counter()
+    def step(self, record: bool = True):
+        tok, secs = 0, 0.0
+        if self.dec_req:
+            inp = _cpu_decode_inputs(self.rng, self.dec_req, self.dec_T)
             fn = self.oracle.decode if self.dec_T == 1 else self.oracle.decode_mtp
+            t = time.perf_counter()
             fn(inp["q"], inp["k"], inp["v"], inp["state"], self.A_log, inp["a"], self.dt, inp["b"],
                nthreads=self.threads)
-            self.dec_s += time.perf_counter() - t
-            self.dec_n += self.dec_sample
+            secs += time.perf_counter() - t
+            tok += self.dec_req * self.dec_T
         if self.lengths is not None:
-            L = [int(self.lengths[self.next_seq % len(self.lengths)])]
-            self.next_seq += 1
-            inp = _cpu_prefill_inputs(self.rng, L, self.wl["prefill"] == "c3")
+            idx = list(range(self.j % self.k, len(self.lengths), self.k))
+            inp = _cpu_prefill_inputs(self.rng, self.lengths[idx], self.wl["prefill"] == "c3")
             t = time.perf_counter()
             self.oracle.prefill(inp["q"], inp["k"], inp["v"], inp["state"], self.A_log, inp["a"],
                                 self.dt, inp["b"], inp["cu"], nthreads=self.threads)
-            self.pre_s += time.perf_counter() - t
-            self.pre_n += inp["T"]
+            secs += time.perf_counter() - t
+            tok += inp["T"]
+            if record:
+                self.seqs_seen.update(idx)
+        self.j += 1
+        if record:
+            self.times.append(secs)
+            self.tokens.append(tok)
 
-    def full_step_seconds(self):
-        t = 0.0
-        if self.wl["decode_batch"]:
-            t += self.dec_s / self.dec_n * self.wl["decode_batch"]
-        if self.lengths is not None:
-            t += self.pre_s / self.pre_n * float(self.lengths.sum())
-        return t
+    def value(self) -> float:
+        return float(sum(self.tokens) / sum(self.times))
 
-    def total_tokens(self):
-        return (self.wl["decode_batch"] * self.dec_T
-                + (int(self.lengths.sum()) if self.lengths is not None else 0))
+    def ms_per_step(self) -> float:
+        return float(np.mean(self.times) * 1e3)
 
-    def describe(self):
+    def describe(self) -> str:
         parts = []
-        if self.dec_n:
-            parts.append(f"decode of {int(self.dec_n)} requests x {self.dec_T} token(s)")
-        if self.pre_n:
-            parts.append(f"prefill of {int(self.pre_n)} tokens ({self.next_seq} sequences drawn "
-                         f"from the workload's length list)")
-        return ("; ".join(parts) + "; extrapolated per request / per token to the full step")
+        if self.dec_req:
+            parts.append(f"decode of {self.dec_req} requests x {self.dec_T} token(s)")
+        if self.lengths is not None:
+            per = len(range(0, len(self.lengths), self.k))
+            parts.append(f"prefill of {per} sequence(s) (every {self.k}th of the workload's "
+                         f"{len(self.lengths)}-sequence length list)")
+        frac = f"1/{self.k} of the workload's step" if self.k > 1 else "the whole workload step"
+        seen = (f"; the timed steps covered {len(self.seqs_seen)} of the {len(self.lengths)} "
+                "sequences" if self.lengths is not None else "")
+        return (f"each step = {frac} with the same decode:prefill mix: " + " + ".join(parts)
+                + f"; {len(self.times)} timed steps, {sum(self.tokens)} tokens" + seen)
 
 
 def cpu_baseline(workload: str, budget_s: float = 15.0):
-    timer = CpuOracleTimer(workload)
+    """The oracle on sample steps for about `budget_s` seconds (at least two)."""
+    sampler = CpuStepSampler(workload)
     t_start = time.perf_counter()
-    while time.perf_counter() - t_start < budget_s:
-        timer.sample()
-    step_s = timer.full_step_seconds()
-    return {"value": timer.total_tokens() / step_s, "unit": "tokens/s", "cores": timer.threads,
-            "kind": "port", "sample": timer.describe(),
+    sampler.step(record=False)  # warm-up (page-in, thread pool)
+    while len(sampler.times) < 2 or time.perf_counter() - t_start < budget_s:
+        sampler.step()
+    return {"value": sampler.value(), "unit": "tokens/s", "cores": sampler.threads,
+            "kind": "port", "sample": sampler.describe(),
+            "ms_per_sample_step": sampler.ms_per_step(),
             "wall_s": round(time.perf_counter() - t_start, 1)}
 
 
 def reference_arm(args):
+    """The reference's path on the host cores: the CPU restatement of its
+    recurrence (the reference's own code is Python/Triton and GPU-only).
+    Rank 0 alone runs; W warm-up and K timed sample steps (see
+    CpuStepSampler), so `steps` and `ms_per_step` describe exactly what was
+    timed."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    timer = CpuOracleTimer(args.workload)
+    sampler = CpuStepSampler(args.workload)
     for _ in range(args.warmup):
-        timer.sample()
-    timer.dec_s = timer.dec_n = timer.pre_s = timer.pre_n = 0.0
+        sampler.step(record=False)
     t_start = time.perf_counter()
     for _ in range(args.steps):
-        timer.sample()
-    step_s = timer.full_step_seconds()
-    value = timer.total_tokens() / step_s
-    wl = WORKLOADS[args.workload]
+        sampler.step()
+    value = sampler.value()
+    cpu = {"value": value, "unit": "tokens/s", "cores": sampler.threads, "kind": "port",
+           "sample": sampler.describe(), "wall_s": round(time.perf_counter() - t_start, 1)}
     emit({
         "impl": "reference",
         "metric": "GDN serving throughput (decode + prefill tokens/s, max-over-ranks device time)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": wl["desc"], "decode_batch": wl["decode_batch"],
-                   "prefill_tokens": int(timer.lengths.sum()) if timer.lengths is not None else 0},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": timer.threads,
-                         "kind": "port", "sample": timer.describe() + f"; {args.steps} timed samples",
-                         "wall_s": round(time.perf_counter() - t_start, 1)},
+        "warmup": args.warmup, "ms_per_step": sampler.ms_per_step(), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded; the benchmark configs' value distributions)",
+        "config": workload_config(args.workload, world),
+        "execution": {"where": f"rank 0's host cores ({sampler.threads} threads)",
+                      "step": f"1/{sampler.k} of the workload step per timed step",
+                      "full_step_ms_estimate": sampler.ms_per_step() * sampler.k},
+        "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "note": "the reference's path is Python/Triton (GPU only); its CPU implementation "
@@ -997,6 +1116,111 @@ def _load_triton_ref(definition: str):
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod
+
+
+def _flush_l2(torch, buf):
+    buf.add_(1)  # writes 256 MiB (more than the 126 MB L2)
+
+
+def _time_calls(torch, stream, fn, n, flush=None):
+    """Mean device time (ms) of `fn` over n calls, CUDA events on `stream`
+    around each call only (an L2 flush, when given, runs before each call
+    outside the events)."""
+    pairs = []
+    for _ in range(n):
+        if flush is not None:
+            flush()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        pairs.append((e0, e1))
+    torch.cuda.synchronize()
+    return float(np.mean([a.elapsed_time(b) for a, b in pairs]))
+
+
+def triton_reference_block(torch, gdn, args, dev, A_log, dt_bias, dec, pre, ours):
+    """The reference's own Triton kernels (its two solution/triton/kernel.py
+    files, unmodified, staged under baseline/_ref) timed on this GPU on the
+    same inputs as this run (N = 1): the workload's step and its phases, and
+    for the default workload also C2 (one 4,096-token sequence, the north
+    star's T >= 4096 case), against ours on the same inputs.  Speed-up =
+    reference ms / ours."""
+    dec_mod = _load_triton_ref("gdn_decode_qk4_v8_d128_k_last") if dec is not None else None
+    pre_mod = _load_triton_ref("gdn_prefill_qk4_v8_d128_k_last")
+    if (dec is not None and dec_mod is None) or pre_mod is None:
+        return {"unavailable": f"reference Triton solutions not staged under {TRITON_REF_DIR}"}
+    if dec is not None and (dec["T"] != 1 or dec.get("bf16")):
+        return {"unavailable": "the reference decode takes one fp32-state token per request; "
+                               "bench.py --impl triton times it token by token"}
+    stream = torch.cuda.current_stream(dev)
+    n = max(3, min(args.steps, 10))
+    out = {"source": "solution/triton/kernel.py (prefill) and gdn_decode_qk4_v8_d128_k_last/"
+                     "solution/triton/kernel.py (decode), unmodified, through their run() entry "
+                     "points; CUDA events, same inputs and GPU as this run",
+           "steps": n}
+
+    def ref_decode():
+        return dec_mod.run(dec["q"], dec["k"], dec["v"], dec["state"], A_log, dec["a"], dt_bias,
+                           dec["b"], None)
+
+    def ref_prefill(p):
+        return pre_mod.run(p["q"], p["k"], p["v"], p["h0"], A_log, p["a"], dt_bias, p["b"],
+                           p["cu"], None)
+
+    def entry(ref_ms, our_ms):
+        return {"reference_triton": ref_ms, "b200": our_ms, "speedup": ref_ms / our_ms}
+
+    for _ in range(3):  # warm-up, JIT compilation included
+        if dec is not None:
+            ref_decode()
+        if pre is not None and pre["N"] > 0:
+            ref_prefill(pre)
+    torch.cuda.synchronize()
+    phases = {}
+    if dec is not None:
+        phases["decode"] = _time_calls(torch, stream, ref_decode, n)
+        out[f"decode_b{dec['B']}_ms"] = entry(phases["decode"], ours["decode_ms"])
+    if pre is not None and pre["N"] > 0:
+        phases["prefill"] = _time_calls(torch, stream, lambda: ref_prefill(pre), n)
+        out["prefill_ms"] = entry(phases["prefill"], ours["prefill_ms"])
+        # parity of the two on these inputs (final states; outputs by median
+        # per-token distance, the reference's output stage being nondeterministic)
+        o_ref, s_ref = ref_prefill(pre)
+        o, s = gdn.prefill.run(pre["q"], pre["k"], pre["v"], pre["h0"], A_log, pre["a"], dt_bias,
+                               pre["b"], pre["cu"], None)
+        tok = ((o.float() - o_ref.float()).flatten(1).norm(dim=1)
+               / o_ref.float().flatten(1).norm(dim=1).clamp_min(1e-30))
+        out["prefill_parity"] = {
+            "final_state_rel_fro": float((s - s_ref).norm() / s_ref.norm().clamp_min(1e-30)),
+            "out_token_rel_median": float(tok.median())}
+        del o_ref, s_ref, o, s
+    out["step_ms"] = entry(sum(phases.values()), ours["step_ms"])
+    if args.workload == "c4":
+        # C2: T = 4096 in one sequence, zero initial state (L2 flushed before each call)
+        c2 = make_prefill_inputs(torch, prefill_lengths("c2"), False, 200, dev)
+        o2 = torch.empty(c2["T"], HV, D, dtype=torch.bfloat16, device=dev)
+        f2 = torch.empty(c2["N"], HV, D, D, dtype=torch.float32, device=dev)
+        ws2 = gdn.prefill.alloc_workspace(c2["T"], c2["N"], dev)
+        flush_buf = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+
+        def ours_c2():
+            gdn.prefill.prefill_into(c2["q"], c2["k"], c2["v"], None, A_log, c2["a"], dt_bias,
+                                     c2["b"], c2["cu"], None, o2, f2, ws2)
+
+        for _ in range(3):
+            ours_c2()
+            ref_prefill(c2)
+        flush = lambda: _flush_l2(torch, flush_buf)  # noqa: E731
+        m = max(n, 20)
+        out["c2_prefill_ms"] = entry(_time_calls(torch, stream, lambda: ref_prefill(c2), m, flush),
+                                     _time_calls(torch, stream, ours_c2, m, flush))
+        out["c2_prefill_ms"]["l2"] = "flushed before each call"
+    pre_keys = [k for k in ("prefill_ms", "c2_prefill_ms") if k in out]
+    out["prefill_faster_than_reference_at_T_ge_4096"] = (
+        all(out[k]["speedup"] > 1.0 for k in pre_keys) if pre_keys else None)
+    return out
 
 
 def triton_arm(args):
@@ -1150,6 +1374,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="device step only (profiling runs)")
+    ap.add_argument("--no-triton", action="store_true",
+                    help="N = 1: skip timing the reference's Triton kernels beside ours")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="N > 1: kernels store results into rank 0's memory (peer) or an NCCL "
                          "gather runs after the compute (nccl)")

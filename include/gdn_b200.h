@@ -7,8 +7,10 @@
  * Every entry point takes plain device pointers, element counts and a CUDA
  * stream (cudaStream_t passed as void*, NULL = legacy default stream).  Calls
  * are asynchronous on that stream, never synchronise the host, never
- * allocate, and return a gdn_status_t.  Tensors are dense row-major
- * (contiguous); bf16 tensors are passed as raw 16-bit storage.
+ * allocate device memory (outputs and workspaces are the caller's; the
+ * Python mirror in track-c-gdn_b200/ is what allocates them for its
+ * value-returning `run`s), and return a gdn_status_t.  Tensors are dense
+ * row-major (contiguous); bf16 tensors are passed as raw 16-bit storage.
  *
  * The library is built from track-c-gdn_b200/csrc/ by __graft_entry__.build()
  * into track-c-gdn_b200/libgdn_b200.so.
@@ -184,6 +186,23 @@ int gdn_prefill_qk4_v8_d128_k_last(
     const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
     float scale, void *out, float *final_state, void *workspace,
     size_t workspace_bytes, void *stream);
+
+/*
+ * gdn_prefill_qk4_v8_d128_k_last, recording CUDA events for per-kernel
+ * timing: events[i] (a cudaEvent_t passed as void*) is recorded on `stream`
+ * right after the i-th kernel this call launches, for i < num_events.  The
+ * call launches gdn_prefill_kernel_launches(T, N) kernels, in this order:
+ * metadata, chunk preparation, scan (pass 1), and with the segmented
+ * evaluation also the segment composition and the scan's pass 3.  Results
+ * are those of gdn_prefill_qk4_v8_d128_k_last bit for bit.  No counterpart
+ * in the reference (its timing is the harness's, around the whole call).
+ */
+int gdn_prefill_qk4_v8_d128_k_last_events(
+    const void *q, const void *k, const void *v, const float *state,
+    const float *A_log, const void *a, const float *dt_bias, const void *b,
+    const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+    float scale, void *out, float *final_state, void *workspace,
+    size_t workspace_bytes, void *const *events, int num_events, void *stream);
 
 /*
  * Prefill against a paged state pool: sequence n starts from

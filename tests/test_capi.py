@@ -25,7 +25,8 @@ def test_header_declares_expected_entry_points():
               "gdn_prefill_workspace_bytes", "gdn_b200_status_string",
               "gdn_prefill_backward_qk4_v8_d128_k_last",
               "gdn_prefill_backward_workspace_bytes", "gdn_prefill_backward_kernel_launches",
-              "gdn_b200_abi_version", "gdn_b200_read_device_status"):
+              "gdn_b200_abi_version", "gdn_b200_read_device_status",
+              "gdn_prefill_qk4_v8_d128_k_last_events"):
         assert n in names
 
 
@@ -35,6 +36,22 @@ def test_library_exports_every_declared_symbol(gdn):
         assert hasattr(lib, name), f"libgdn_b200.so does not export {name}"
     # and the Python binding covers each of them
     assert set(header_functions()) == set(gdn._native.SIGNATURES)
+
+
+def test_debug_entry_points_only_in_the_debug_build(gdn):
+    """include/gdn_b200_debug.h declares what libgdn_b200_debug.so alone exports."""
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "gdn_b200_debug.h").read_text(), flags=re.S)
+    names = sorted(set(re.findall(r"\b(gdn_[a-z0-9_]+)\s*\(", text)))
+    assert names == ["gdn_b200_debug_wait_timeout_probe"]
+    release = ctypes.CDLL(str(gdn._native.LIB_PATH))
+    debug_path = gdn._native.LIB_PATH.with_name("libgdn_b200_debug.so")
+    if not debug_path.exists():
+        pytest.skip("debug build not present")
+    debug = ctypes.CDLL(str(debug_path))
+    for n in names:
+        assert hasattr(debug, n) and not hasattr(release, n), n
+    for n in header_functions():
+        assert hasattr(debug, n), n
 
 
 def test_status_strings(gdn):

@@ -1,10 +1,13 @@
 """Results written in place on another process's GPU memory (shard.PeerResult).
 
-Two processes share cuda:0 (CUDA IPC works between processes on one device,
-so one GPU is enough): rank 0 owns the rank-major result buffers, rank 1
-maps them, and each rank's decode and prefill calls store their outputs
-and final states straight into them.  Rank 0 then recomputes both ranks'
-work into its own tensors: the mapped writes must equal it bit for bit.
+Two processes, on GPUs 0 and 1 when there are two (the stores then cross
+NVLink), else both on cuda:0 (CUDA IPC works between processes on one
+device): rank 0 owns the rank-major result buffers, rank 1 maps them, and
+each rank's decode and prefill calls store their outputs and final states
+straight into them, for three steps.  After each step rank 0 recomputes
+both ranks' work into its own tensors and the mapped writes must equal it
+bit for bit -- while rank 1 is already storing the next step into the other
+of the two alternating buffers.
 Rank 1's prefill is one long sequence, so its final state comes from the
 segmented evaluation's TAIL items; rank 0's is a ragged single-pass batch.
 The processes never wait on each other inside a kernel; the host joins them
@@ -24,60 +27,66 @@ pytestmark = pytest.mark.gpu
 
 DEC_ROWS = [5, 3]
 PREFILL_LENS = [[100, 300, 64, 7], [4096]]
+STEPS = 3
 
 
-def _inputs(rank):
+def _inputs(rank, step):
     import cases
     from gpu_util import decode_args, prefill_args
-    dec = decode_args(cases.decode_inputs(seed=40 + rank, B=DEC_ROWS[rank]))
-    pre = prefill_args(cases.prefill_inputs(seed=50 + rank, lens=PREFILL_LENS[rank]))
+    dec = decode_args(cases.decode_inputs(seed=40 + rank + 10 * step, B=DEC_ROWS[rank]))
+    pre = prefill_args(cases.prefill_inputs(seed=50 + rank + 10 * step, lens=PREFILL_LENS[rank]))
     return dec, pre
 
 
 def _worker(rank, world, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
+    # rank r on GPU r when there are enough GPUs (stores cross NVLink), else
+    # both ranks on GPU 0 (CUDA IPC between processes on one device)
+    dev_index = rank if torch.cuda.device_count() >= world else 0
+    torch.cuda.set_device(dev_index)
+    dev = torch.device("cuda", dev_index)
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=timedelta(seconds=120))
     try:
         gdn = importlib.import_module("track-c-gdn_b200")
         shard = importlib.import_module("track-c-gdn_b200.shard")
-        dec, pre = _inputs(rank)
         dec_res = shard.PeerResult(DEC_ROWS, (1, 8, 128), torch.bfloat16, dev)
         fin_res = shard.PeerResult([len(x) for x in PREFILL_LENS], (8, 128, 128), torch.float32, dev)
-        if rank == 0:  # poison the buffers; the other rank writes only after the barrier
-            dec_res.tensor().fill_(float("nan"))
-            fin_res.tensor().fill_(float("nan"))
+        if rank == 0:  # poison both buffers; the other rank writes only after the barrier
+            dec_res._buf.fill_(float("nan"))
+            fin_res._buf.fill_(float("nan"))
         torch.cuda.synchronize(dev)
         dist.barrier()
 
-        q_, k_, v_, st, A_log, a, dt, b = dec
-        new_state = torch.empty_like(st)
-        gdn.decode.decode_into(q_, k_, v_, st, A_log, a, dt, b, None, dec_res.rows_for_me(),
-                               new_state)
-        pq, pk, pv, h0, pA, pa, pdt, pb, cu = pre
-        T, N = pq.shape[0], cu.numel() - 1
-        out = torch.empty(T, 8, 128, dtype=torch.bfloat16, device=dev)
-        ws = gdn.prefill.alloc_workspace(T, N, dev)
-        gdn.prefill.prefill_into(pq, pk, pv, h0, pA, pa, pdt, pb, cu, None, out,
-                                 fin_res.rows_for_me(), ws)
-        dec_res.publish()
-        status = gdn._native.read_device_status()
-
         verdict = "ok"
-        if rank == 0:
-            for r in range(world):
-                (q_, k_, v_, st, A_log, a, dt, b), pre_r = _inputs(r)
-                o_ref, _ = gdn.decode.run(q_, k_, v_, st, A_log, a, dt, b, None)
-                _, f_ref = gdn.prefill.run(*pre_r, None)
-                lo, hi = dec_res.offsets[r], dec_res.offsets[r + 1]
-                if not torch.equal(dec_res.tensor()[lo:hi], o_ref.view(hi - lo, 1, 8, 128)):
-                    verdict = f"decode rows of rank {r} differ"
-                lo, hi = fin_res.offsets[r], fin_res.offsets[r + 1]
-                if not torch.equal(fin_res.tensor()[lo:hi], f_ref):
-                    verdict = f"final states of rank {r} differ"
+        for step in range(STEPS):
+            dec, pre = _inputs(rank, step)
+            q_, k_, v_, st, A_log, a, dt, b = dec
+            new_state = torch.empty_like(st)
+            gdn.decode.decode_into(q_, k_, v_, st, A_log, a, dt, b, None,
+                                   dec_res.rows_for_me(), new_state)
+            pq, pk, pv, h0, pA, pa, pdt, pb, cu = pre
+            T, N = pq.shape[0], cu.numel() - 1
+            out = torch.empty(T, 8, 128, dtype=torch.bfloat16, device=dev)
+            ws = gdn.prefill.alloc_workspace(T, N, dev)
+            gdn.prefill.prefill_into(pq, pk, pv, h0, pA, pa, pdt, pb, cu, None, out,
+                                     fin_res.rows_for_me(), ws)
+            dec_res.publish(fin_res)
+            if rank == 0:
+                # step `step` is published; the other rank may already be
+                # storing step + 1 into the other buffers while this reads
+                for r in range(world):
+                    (q_, k_, v_, st, A_log, a, dt, b), pre_r = _inputs(r, step)
+                    o_ref, _ = gdn.decode.run(q_, k_, v_, st, A_log, a, dt, b, None)
+                    _, f_ref = gdn.prefill.run(*pre_r, None)
+                    lo, hi = dec_res.offsets[r], dec_res.offsets[r + 1]
+                    if not torch.equal(dec_res.tensor()[lo:hi], o_ref.view(hi - lo, 1, 8, 128)):
+                        verdict = f"step {step}: decode rows of rank {r} differ"
+                    lo, hi = fin_res.offsets[r], fin_res.offsets[r + 1]
+                    if not torch.equal(fin_res.tensor()[lo:hi], f_ref):
+                        verdict = f"step {step}: final states of rank {r} differ"
+        status = gdn._native.read_device_status()
         dec_res.close()
         fin_res.close()
         q.put((rank, verdict, status))

@@ -133,3 +133,36 @@ def test_backward_reports_bad_seqlens(gdn):
     gdn.prefill.backward_into(q, k, v, None, A_log, a, dt, b, bad_cu, None, d_out.cuda(), None,
                               *outs, ws)
     assert gdn._native.read_device_status() == 1
+
+
+@pytest.mark.parametrize("T", [1, 255, 257, 70_001])
+def test_backward_parameter_gradient_reduction(gdn, T):
+    """dA_log and ddt_bias are reduced over tokens in two fixed-order stages
+    (256 coalesced partial sums, then one pass over them).  At T values whose
+    token ranges split unevenly over the 256 blocks (and T < 256, which
+    leaves blocks empty) the sums must equal the float64 sums of the
+    kernel's own per-token gradients -- ddt_bias = sum_t da_t and dA_log =
+    sum_t da_t softplus(x_t) / sigmoid(x_t), x = a + dt_bias, because da_t =
+    dg_t (-e^A_log sigmoid(x_t)) and dg_t/dA_log = g_t -- and two calls must
+    agree bit for bit.  Small T is also checked against autograd."""
+    args, d_out, d_final = _case(1000 + T, [T], T > 1, T > 1)
+    g1 = gdn.prefill.backward(*args, None, d_out.cuda(), None if d_final is None else d_final.cuda())
+    g2 = gdn.prefill.backward(*args, None, d_out.cuda(), None if d_final is None else d_final.cuda())
+    for name in NAMES:
+        if g1[name] is not None:
+            assert torch.equal(g1[name], g2[name]), name
+    q, k, v, state, A_log, a, dt, b, cu = args
+    da = g1["da"].double().cpu()                                  # [T, 8]
+    x = a.double().cpu() + dt.double().cpu()[None, :]
+    sp = torch.where(x > 0, x + torch.log1p(torch.exp(-x)), torch.log1p(torch.exp(x)))
+    terms = {"ddt_bias": da, "dA_log": da * sp / torch.sigmoid(x)}
+    for name, t in terms.items():
+        want = t.sum(0)
+        got = g1[name].double().cpu()
+        bound = 1e-4 * t.abs().sum(0) + 1e-6
+        assert bool(((got - want).abs() <= bound).all()), (name, got, want)
+    if T <= 257:
+        ref = autograd_ref.prefill_grads(q, k, v, state, A_log, a, dt, b, cu.cpu().tolist(), None,
+                                         d_out.float(), d_final)
+        for name in ("dA_log", "ddt_bias", "da", "db"):
+            assert _rel(g1[name], ref[name].view_as(g1[name])) < TOL, name

@@ -183,12 +183,19 @@ def _peer_protocol_worker(rank, world, port, failing_rank, q):
             q.put((rank, "raised", str(e)))
             return
         row_bytes = 2 * 4 * 4
-        mine = res.rows_for_me().data_ptr()
-        if rank == 0:
-            ok = mine == res.tensor().data_ptr() and tuple(res.tensor().shape) == (8, 2, 4)
-        else:
-            ok = mine == _FakeIpc.MAPPED + _FakeIpc.OFFSET + res.offsets[rank] * row_bytes
-        res.publish()
+        buf_bytes = (8 * row_bytes + 255) // 256 * 256  # one buffer, 256-byte rounded
+        base = res.tensor().data_ptr() if rank == 0 else _FakeIpc.MAPPED + _FakeIpc.OFFSET
+        ok = True
+        # three steps: the destination alternates between the two buffers,
+        # and dst's tensor() is the buffer of the step just published
+        for step in range(3):
+            mine = res.rows_for_me().data_ptr()
+            ok = ok and mine == base + (step % 2) * buf_bytes + res.offsets[rank] * row_bytes
+            res.publish()
+            if rank == 0:
+                t = res.tensor()
+                ok = ok and t.data_ptr() == base + (step % 2) * buf_bytes
+                ok = ok and tuple(t.shape) == (8, 2, 4)
         res.close()
         ok = ok and ipc.closed == ([] if rank == 0 else [_FakeIpc.MAPPED])
         q.put((rank, "ok" if ok else "bad addresses", None))

@@ -7,7 +7,8 @@ import pytest
 import torch
 
 import cases
-from gpu_util import bf16_dev, f32_dev, prefill_args
+import oracle
+from gpu_util import bf16_dev, f32_dev, out_err, prefill_args, rel_fro
 
 pytestmark = pytest.mark.gpu
 
@@ -72,6 +73,11 @@ def test_prefill_pool_equals_dense_prefill(gdn, lens):
     untouched = torch.ones(P, dtype=torch.bool, device="cuda")
     untouched[slots.long()] = False
     assert torch.equal(pool[untouched], before[untouched])
+    # and directly against the fp32 recurrence, from the states the slots held
+    ro, rs = oracle.prefill(inp["q"], inp["k"], inp["v"], h0.cpu().numpy(), inp["A_log"],
+                            inp["a"], inp["dt_bias"], inp["b"], inp["cu_seqlens"])
+    assert out_err(o, ro) <= 1.0
+    assert rel_fro(pool[slots.long()].cpu().numpy(), rs) < 5e-3
 
 
 def test_bad_slot_sets_device_status(gdn):

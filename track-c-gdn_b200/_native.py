@@ -39,6 +39,10 @@ SIGNATURES = {
     "gdn_prefill_qk4_v8_d128_k_last": (
         ctypes.c_int,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P, _P, ctypes.c_size_t, _P]),
+    "gdn_prefill_qk4_v8_d128_k_last_events": (
+        ctypes.c_int,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _F, _P, _P, _P, ctypes.c_size_t, _P,
+         ctypes.c_int, _P]),
     "gdn_prefill_backward_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
     "gdn_prefill_backward_kernel_launches": (ctypes.c_int, []),
     "gdn_prefill_backward_qk4_v8_d128_k_last": (

@@ -6,3 +6,4 @@
 #include "gdn_prefill_bwd.cu"
 #include "gdn_capi.cu"
 #include "gdn_prefill_noalloc.cu"
+#include "gdn_debug_probe.cu"  // compiled only with -DGDN_DEBUG_CHECKS

@@ -44,7 +44,8 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
                            const float *A_log, const void *a, const float *dt_bias, const void *b,
                            const int64_t *cu_seqlens, int64_t N, int64_t T, float scale,
                            void *out, float *final_state, void *workspace, bool allow_segments,
-                           const int32_t *slots, int64_t pool_slots, cudaStream_t stream);
+                           const int32_t *slots, int64_t pool_slots, cudaStream_t stream,
+                           const cudaEvent_t *events, int num_events);
 }  // namespace gdn
 
 namespace {
@@ -72,6 +73,39 @@ int check_device(int *num_sms) {
   }
   if (num_sms) *num_sms = cached_sms;
   return cached_ok ? GDN_OK : GDN_ERR_DEVICE;
+}
+
+
+// Argument checks of the dense prefill entry points, then the launches.
+int prefill_checked(const void *q, const void *k, const void *v, const float *state,
+                    const float *A_log, const void *a, const float *dt_bias, const void *b,
+                    const int64_t *cu_seqlens, int64_t num_seqs, int64_t total_tokens,
+                    float scale, void *out, float *final_state, void *workspace,
+                    size_t workspace_bytes, void *stream, const cudaEvent_t *events,
+                    int num_events) {
+  if (num_seqs < 0 || total_tokens < 0 || total_tokens > (int64_t{1} << 31) ||
+      num_seqs > (int64_t{1} << 24))
+    return GDN_ERR_BAD_SIZE;
+  if (num_seqs == 0) return total_tokens == 0 ? GDN_OK : GDN_ERR_BAD_SIZE;
+  if (!cu_seqlens || !A_log || !dt_bias || !final_state || !workspace) return GDN_ERR_NULL_POINTER;
+  if (total_tokens > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL_POINTER;
+  if ((q && !aligned(q, 16)) || (k && !aligned(k, 16)) || (v && !aligned(v, 16)) ||
+      (out && !aligned(out, 16)) || !aligned(final_state, 16) || (state && !aligned(state, 16)) ||
+      !aligned(cu_seqlens, 8))
+    return GDN_ERR_MISALIGNED;
+  if (!aligned(workspace, 1024) ||
+      workspace_bytes < gdn::prefill_workspace_bytes(total_tokens, num_seqs, true))
+    return GDN_ERR_WORKSPACE;
+  const size_t state_bytes = static_cast<size_t>(num_seqs) * gdn::kHV * gdn::kD * gdn::kD * 4;
+  if (state && state != final_state && overlap(state, state_bytes, final_state, state_bytes))
+    return GDN_ERR_ALIASING;
+  if (int st = check_device(nullptr)) return st;
+  if (scale == 0.0f) scale = kDefaultScale;
+  cudaError_t err = gdn::launch_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
+                                        total_tokens, scale, out, final_state, workspace, true,
+                                        nullptr, 0, static_cast<cudaStream_t>(stream), events,
+                                        num_events);
+  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
 }  // namespace
@@ -229,28 +263,22 @@ int gdn_prefill_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
                                    int64_t total_tokens, float scale, void *out,
                                    float *final_state, void *workspace, size_t workspace_bytes,
                                    void *stream) {
-  if (num_seqs < 0 || total_tokens < 0 || total_tokens > (int64_t{1} << 31) ||
-      num_seqs > (int64_t{1} << 24))
-    return GDN_ERR_BAD_SIZE;
-  if (num_seqs == 0) return total_tokens == 0 ? GDN_OK : GDN_ERR_BAD_SIZE;
-  if (!cu_seqlens || !A_log || !dt_bias || !final_state || !workspace) return GDN_ERR_NULL_POINTER;
-  if (total_tokens > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_NULL_POINTER;
-  if ((q && !aligned(q, 16)) || (k && !aligned(k, 16)) || (v && !aligned(v, 16)) ||
-      (out && !aligned(out, 16)) || !aligned(final_state, 16) || (state && !aligned(state, 16)) ||
-      !aligned(cu_seqlens, 8))
-    return GDN_ERR_MISALIGNED;
-  if (!aligned(workspace, 1024) ||
-      workspace_bytes < gdn::prefill_workspace_bytes(total_tokens, num_seqs, true))
-    return GDN_ERR_WORKSPACE;
-  const size_t state_bytes = static_cast<size_t>(num_seqs) * gdn::kHV * gdn::kD * gdn::kD * 4;
-  if (state && state != final_state && overlap(state, state_bytes, final_state, state_bytes))
-    return GDN_ERR_ALIASING;
-  if (int st = check_device(nullptr)) return st;
-  if (scale == 0.0f) scale = kDefaultScale;
-  cudaError_t err = gdn::launch_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
-                                        total_tokens, scale, out, final_state, workspace, true,
-                                        nullptr, 0, static_cast<cudaStream_t>(stream));
-  return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+  return prefill_checked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                         scale, out, final_state, workspace, workspace_bytes, stream, nullptr, 0);
+}
+
+int gdn_prefill_qk4_v8_d128_k_last_events(const void *q, const void *k, const void *v,
+                                          const float *state, const float *A_log, const void *a,
+                                          const float *dt_bias, const void *b,
+                                          const int64_t *cu_seqlens, int64_t num_seqs,
+                                          int64_t total_tokens, float scale, void *out,
+                                          float *final_state, void *workspace,
+                                          size_t workspace_bytes, void *const *events,
+                                          int num_events, void *stream) {
+  if (num_events < 0 || (num_events > 0 && events == nullptr)) return GDN_ERR_NULL_POINTER;
+  return prefill_checked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs, total_tokens,
+                         scale, out, final_state, workspace, workspace_bytes, stream,
+                         reinterpret_cast<const cudaEvent_t *>(events), num_events);
 }
 
 int gdn_decode_pool_qk4_v8_d128_k_last(const void *q, const void *k, const void *v,
@@ -333,7 +361,8 @@ int gdn_prefill_pool_qk4_v8_d128_k_last(const void *q, const void *k, const void
   if (scale == 0.0f) scale = kDefaultScale;
   cudaError_t err = gdn::launch_prefill(q, k, v, state_pool, A_log, a, dt_bias, b, cu_seqlens,
                                         num_seqs, total_tokens, scale, out, state_pool, workspace,
-                                        true, slots, pool_slots, static_cast<cudaStream_t>(stream));
+                                        true, slots, pool_slots, static_cast<cudaStream_t>(stream),
+                                        nullptr, 0);
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 

@@ -175,18 +175,31 @@ __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
-// Slow path of wait_phase: keep polling, give up after 2^33 SM cycles
-// (about 4 s at the B200's top clock, longer at lower clocks) or at once
-// when another thread of the CTA already gave up; records device status 2.
-// A CTA that gave up finishes its loop without waiting again and still
-// deallocates its TMEM.
+// Cycle budget of one bounded wait: 2^33 SM cycles (about 4 s at the B200's
+// top clock, longer at lower clocks).  The index-checked debug build reads it
+// from a device variable instead, so that a test can shorten it and make a
+// wait run out (gdn_b200_debug_wait_timeout_probe).
+#ifdef GDN_DEBUG_CHECKS
+__device__ long long g_wait_limit_cycles = 1ll << 33;
+__device__ __forceinline__ long long wait_limit_cycles() {
+  return *reinterpret_cast<volatile long long *>(&g_wait_limit_cycles);
+}
+#else
+__device__ __forceinline__ constexpr long long wait_limit_cycles() { return 1ll << 33; }
+#endif
+
+// Slow path of wait_phase: keep polling, give up after wait_limit_cycles()
+// or at once when another thread of the CTA already gave up; records device
+// status 2.  A CTA that gave up finishes its loop without waiting again and
+// still deallocates its TMEM.
 __device__ __noinline__ bool wait_phase_slow(uint32_t mbar, uint32_t parity, volatile int *broken) {
   const long long t0 = clock64();
+  const long long limit = wait_limit_cycles();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(mbar, parity)) return true;
     if (*broken) return false;
-    if (clock64() - t0 > (1ll << 33)) {
+    if (clock64() - t0 > limit) {
       *broken = 1;
       set_device_status(kDevStatusWaitTimeout);
       return false;
@@ -1544,8 +1557,16 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
                            const float *A_log, const void *a, const float *dt_bias, const void *b,
                            const int64_t *cu_seqlens, int64_t N, int64_t T, float scale,
                            void *out, float *final_state, void *workspace, bool allow_segments,
-                           const int32_t *slots, int64_t pool_slots, cudaStream_t stream) {
+                           const int32_t *slots, int64_t pool_slots, cudaStream_t stream,
+                           const cudaEvent_t *events, int num_events) {
   if (N == 0) return cudaSuccess;
+  // events[i] (when given) is recorded on the stream right after the i-th
+  // kernel launch, for per-kernel timing with CUDA events
+  int launched = 0;
+  auto mark = [&]() -> cudaError_t {
+    const int i = launched++;
+    return (events != nullptr && i < num_events) ? cudaEventRecord(events[i], stream) : cudaSuccess;
+  };
   const PrefillWs w = prefill_ws_layout(T, N, allow_segments);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   int *meta = reinterpret_cast<int *>(ws + w.meta);
@@ -1578,6 +1599,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
       static_cast<int>(w.seg_chunks), static_cast<int>(w.seg_max), items, seg_off, slots,
       pool_slots);
   cudaError_t err = cudaGetLastError();
+  if (err == cudaSuccess) err = mark();
   if (err != cudaSuccess) return err;
 
   err = cudaFuncSetAttribute(gdn_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1589,6 +1611,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
         tq, tk, A_log, static_cast<const uint16_t *>(a), dt_bias,
         static_cast<const uint16_t *>(b), cu_seqlens, meta, chunk_tab, gcum, beta, m2);
     err = cudaGetLastError();
+    if (err == cudaSuccess) err = mark();
     if (err != cudaSuccess) return err;
   }
   err = cudaFuncSetAttribute(gdn_prefill_scan_kernel<false>,
@@ -1602,6 +1625,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
       static_cast<uint16_t *>(out), final_state, items, 2, seg_tokens, seg_off, seg_ss, seg_sb,
       seg_phi, slots, nullptr, nullptr);
   err = cudaGetLastError();
+  if (err == cudaSuccess) err = mark();
   if (err != cudaSuccess || w.seg_chunks == 0) return err;
 
   err = cudaFuncSetAttribute(gdn_prefill_compose_kernel,
@@ -1611,6 +1635,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   gdn_prefill_compose_kernel<<<cgrid, kComposeThreads, kCmpSmem, stream>>>(meta, seg_off, seg_ss,
                                                                            seg_sb, seg_phi);
   err = cudaGetLastError();
+  if (err == cudaSuccess) err = mark();
   if (err != cudaSuccess) return err;
   // pass 3
   gdn_prefill_scan_kernel<false><<<static_cast<unsigned>(w.seg_max * kHV), kScanThreads,
@@ -1618,7 +1643,9 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
       tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale,
       static_cast<uint16_t *>(out), final_state, items + 2 * w.seg_max, 3, seg_tokens, seg_off,
       seg_ss, seg_sb, seg_phi, slots, nullptr, nullptr);
-  return cudaGetLastError();
+  err = cudaGetLastError();
+  if (err == cudaSuccess) err = mark();
+  return err;
 }
 
 }  // namespace gdn

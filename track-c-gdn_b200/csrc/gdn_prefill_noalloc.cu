@@ -88,7 +88,6 @@ extern "C" int gdn_prefill_qk4_v8_d128_k_last_noalloc(
   if (scale == 0.0f) scale = kDefaultScale;
   cudaError_t err = gdn::launch_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, num_seqs,
                                         total_tokens, scale, out, final_state, ws, segments,
-                                        nullptr, 0,
-                                        static_cast<cudaStream_t>(stream));
+                                        nullptr, 0, static_cast<cudaStream_t>(stream), nullptr, 0);
   return err == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }

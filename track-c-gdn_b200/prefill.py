@@ -11,8 +11,9 @@ host synchronisation at all (the same check then runs on the device).
 """
 from __future__ import annotations
 
+import ctypes
 import math
-from typing import Optional
+from typing import Optional, Sequence
 
 import torch
 
@@ -71,9 +72,14 @@ def _aligned_ptr(ws: torch.Tensor):
 
 
 def prefill_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, out, final_state,
-                 workspace: torch.Tensor, stream: Optional[int] = None) -> None:
+                 workspace: torch.Tensor, stream: Optional[int] = None,
+                 events: Optional[Sequence] = None) -> None:
     """Destination-passing prefill: writes `out` [T,8,128] bf16 and
-    `final_state` [N,8,128,128] fp32 (which may be `state`).  No host sync."""
+    `final_state` [N,8,128,128] fp32 (which may be `state`).  No host sync.
+    `events` (torch.cuda.Event objects, optional): events[i] is recorded on
+    the stream right after the call's i-th kernel launch (metadata, chunk
+    preparation, scan; with the segmented evaluation also the composition and
+    the second scan pass), for per-kernel timing."""
     T = q.shape[0]
     N = cu_seqlens.numel() - 1
     if scale is None or scale == 0.0:
@@ -81,13 +87,17 @@ def prefill_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, out, f
     if stream is None:
         stream = torch.cuda.current_stream(q.device).cuda_stream
     wptr, wbytes = _aligned_ptr(workspace)
-    st = _native.lib.gdn_prefill_qk4_v8_d128_k_last(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(),
-        None if state is None else state.data_ptr(),
-        A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
-        cu_seqlens.data_ptr(), N, T, float(scale), out.data_ptr(), final_state.data_ptr(),
-        wptr, wbytes, stream)
-    _native.check(st, "gdn_prefill_qk4_v8_d128_k_last")
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), None if state is None else state.data_ptr(),
+            A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
+            cu_seqlens.data_ptr(), N, T, float(scale), out.data_ptr(), final_state.data_ptr(),
+            wptr, wbytes)
+    if events:
+        handles = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+        st = _native.lib.gdn_prefill_qk4_v8_d128_k_last_events(*args, handles, len(events), stream)
+        _native.check(st, "gdn_prefill_qk4_v8_d128_k_last_events")
+    else:
+        st = _native.lib.gdn_prefill_qk4_v8_d128_k_last(*args, stream)
+        _native.check(st, "gdn_prefill_qk4_v8_d128_k_last")
 
 
 @torch.no_grad()

@@ -7,8 +7,11 @@ step shards with no communication during compute:
   * prefill: longest-processing-time-first (LPT) bin packing of sequences by
     cost = number of 64-token chunks + a per-sequence constant (the scan's
     per-sequence setup), which bounds the makespan by 4/3 of optimal.
-The only collective is the final gather to rank 0 of the step's results
-(decode outputs and prefill final states), over NCCL.
+The step's results (decode outputs and prefill final states) end on rank 0
+without a gather: each rank's kernels store them straight into rank 0's
+memory (PeerResult, CUDA IPC over NVLink), and one 4-byte NCCL all-reduce
+closes the step.  An NCCL gather after the compute (gather_padded) is the
+fallback when the peer mapping is not possible.
 """
 from __future__ import annotations
 
@@ -170,16 +173,25 @@ class PeerResult:
     """A step result that lives on rank `dst` and that every rank writes in
     place, so no gather runs after the step.
 
-    `dst` allocates the rank-major buffer [sum(rows), *row_shape] (rank r's
-    rows start at row_offsets(rows)[r]) and sends its CUDA IPC handle to the
-    group; every other rank maps it with lazy peer access.  A rank passes
-    `rows_for_me()` as the destination of its decode or prefill call, and the
-    kernels' stores cross NVLink while the rest of the step still computes.
-    `publish()` closes a step: a 4-byte all-reduce on the current stream
-    (NCCL), or a device sync and a barrier (other backends).  Each rank joins
-    it after its kernels, so once it returns on `dst`, every rank's kernels
-    have finished and their stores are in `tensor()`; and no rank writes the
-    next step's rows before `dst` has reached the same point.
+    `dst` allocates two rank-major buffers [sum(rows), *row_shape] (rank r's
+    rows start at row_offsets(rows)[r]), one allocation, and sends its CUDA
+    IPC handle to the group; every other rank maps it with lazy peer access.
+    Steps alternate between the two buffers.  A rank passes `rows_for_me()`
+    (this step's buffer) as the destination of its decode or prefill call,
+    and the kernels' stores cross NVLink while the rest of the step still
+    computes.  `publish()` closes a step: a 4-byte all-reduce on the current
+    stream (NCCL), or a device sync and a barrier (other backends), then the
+    next step's buffer becomes current.  Each rank joins it after its
+    kernels, so once it returns on `dst`, every rank's kernels have finished
+    and their stores are in `tensor()` (the buffer of the step just
+    published).
+
+    Ordering rule: the other ranks write step s+1 into the other buffer
+    while `dst` still reads step s, and write step s's buffer again only in
+    step s+2, after they have passed publish() of step s+1 -- which `dst`
+    joins only after whatever it queued before it on the same stream.  So
+    `dst` must consume step s's result (host reads, or reads queued on the
+    stream that publish() runs on) before it calls publish() for step s+1.
 
     Only plain stores reach the peer memory (no TMA, no multicast).  Call
     `close()` on every rank before the process group goes away."""
@@ -203,11 +215,17 @@ class PeerResult:
         self._sync()  # the device's context exists and is current before any mapping
         self._mapped = None
         self._buf = None
+        self._cur = 0       # buffer the current step writes
+        self._published = None  # buffer of the last published step
         total = self.offsets[-1]
+        # each buffer starts on a 256-byte boundary inside the allocation
+        self._rows_pad = max(total, 1)
+        per = self._rows_pad * self.row_bytes
+        self._buf_bytes = (per + 255) // 256 * 256
         payload = [None]
         if self.rank == dst:
-            self._buf = torch.empty((max(total, 1),) + self.row_shape, dtype=dtype,
-                                    device=self.device)
+            elems = 2 * self._buf_bytes // torch.empty(0, dtype=dtype).element_size()
+            self._buf = torch.empty(elems, dtype=dtype, device=self.device)
             payload = [self._ipc.export(self._buf.data_ptr())]
         dist.broadcast_object_list(payload, src=dst, group=group,
                                    device=self.device if self._nccl() else None)
@@ -241,29 +259,47 @@ class PeerResult:
         return self._dist.get_backend(self._group) == "nccl"
 
     def rows_for(self, rank: int) -> DeviceRows:
-        """Where `rank`'s first row goes, as an address valid in this process
-        (this rank's own block when rank == self.rank)."""
-        return DeviceRows(self._base + self.offsets[rank] * self.row_bytes)
+        """Where `rank`'s first row of the current step goes, as an address
+        valid in this process (this rank's own block when rank == self.rank)."""
+        return DeviceRows(self._base + self._cur * self._buf_bytes
+                          + self.offsets[rank] * self.row_bytes)
 
     def rows_for_me(self) -> DeviceRows:
         return self.rows_for(self.rank)
 
-    def publish(self) -> None:
+    def publish(self, *others: "PeerResult") -> None:
+        """Close the current step (collective) and make the other buffer the
+        next step's.  PeerResults of the same group written in the same step
+        can be passed as `others`: the one collective closes the step for
+        all of them."""
+        for o in others:
+            if o._group is not self._group or o.dst != self.dst:
+                raise ValueError("results published together must share group and dst")
         if self._flag is not None:
             self._dist.all_reduce(self._flag, group=self._group)
         else:
             self._sync()
             self._dist.barrier(group=self._group)
+        for r in (self, *others):
+            r._published = r._cur
+            r._cur ^= 1
 
     def _sync(self) -> None:
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
 
+    def _view(self, which: int) -> torch.Tensor:
+        esz = self._buf.element_size()
+        start = which * self._buf_bytes // esz
+        n = self.offsets[-1] * self.row_bytes // esz
+        return self._buf[start:start + n].view((self.offsets[-1],) + self.row_shape)
+
     def tensor(self) -> torch.Tensor:
-        """The whole rank-major result (on `dst` only)."""
+        """The whole rank-major result of the last published step (on `dst`
+        only; before the first publish(), the current step's buffer)."""
         if self._buf is None:
             raise RuntimeError("the result lives on rank %d" % self.dst)
-        return self._buf[: self.offsets[-1]]
+        return self._view(self._cur if self._published is None else self._published)
 
     def close(self) -> None:
         """Unmap (all ranks, after their last kernel), then free on `dst`."""
