@@ -297,3 +297,27 @@ def test_repeated_back_to_back_runs_are_deterministic(gdn):
     assert gdn._native.read_device_status() == 0
     for o, s in outs[1:]:
         assert torch.equal(o, outs[0][0]) and torch.equal(s, outs[0][1])
+
+
+@pytest.mark.parametrize("lens", [[300, 64, 17], [4096]])  # single-pass, segmented
+def test_prefill_events_variant_times_each_kernel(gdn, lens):
+    """prefill_into(..., events=...) records one event after each kernel the
+    call launches (gdn_prefill_qk4_v8_d128_k_last_events) and gives the same
+    results bit for bit."""
+    inp = cases.prefill_inputs(seed=sum(lens) + 3, lens=lens, with_state=True)
+    q, k, v, h0, A_log, a, dt, b, cu = prefill_args(inp)
+    T, N = q.shape[0], len(lens)
+    n = gdn._native.prefill_kernel_launches(T, N)
+    ws = gdn.prefill.alloc_workspace(T, N, "cuda")
+    o1 = torch.empty(T, 8, 128, dtype=torch.bfloat16, device="cuda")
+    s1 = torch.empty_like(h0)
+    gdn.prefill.prefill_into(q, k, v, h0, A_log, a, dt, b, cu, None, o1, s1, ws)
+    start = torch.cuda.Event(enable_timing=True)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    o2, s2 = torch.empty_like(o1), torch.empty_like(s1)
+    start.record()
+    gdn.prefill.prefill_into(q, k, v, h0, A_log, a, dt, b, cu, None, o2, s2, ws, events=evs)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    times = [(start if i == 0 else evs[i - 1]).elapsed_time(evs[i]) for i in range(n)]
+    assert all(t >= 0 for t in times) and sum(times) > 0, times

@@ -92,6 +92,9 @@ def prefill_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, out, f
             cu_seqlens.data_ptr(), N, T, float(scale), out.data_ptr(), final_state.data_ptr(),
             wptr, wbytes)
     if events:
+        for e in events:
+            if e.cuda_event == 0:  # torch creates the CUDA event on its first record
+                e.record()
         handles = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
         st = _native.lib.gdn_prefill_qk4_v8_d128_k_last_events(*args, handles, len(events), stream)
         _native.check(st, "gdn_prefill_qk4_v8_d128_k_last_events")
