@@ -83,6 +83,11 @@ WORKLOADS = {
     "decode_bf16": dict(desc="decode batch 1024 with the state stored in bf16 (opt-in format), "
                              "updated in place",
                         decode_batch=1024, prefill=None, state_bf16=True),
+    # profiling subset (not a bench line): the first 64 sequences of C4's
+    # length list, prefill only -- inputs above L2 but a few GB on the device,
+    # small enough for multi-pass ncu captures of one kernel
+    "c4_64": dict(desc="profiling subset: prefill of the first 64 sequences of the C4 length list, "
+                       "zero initial state", decode_batch=0, prefill="c4_64"),
     # training: one prefill backward over the C3 / C4 prefill shapes
     "bwd_c3": dict(desc="prefill backward over C3 (32 sequences U{17..3000}, initial states "
                         "randn*0.02, d_out and d_final_state random)",
@@ -96,6 +101,8 @@ WORKLOADS = {
 def prefill_lengths(kind: str) -> np.ndarray:
     if kind == "c4":
         return np.random.default_rng(4).integers(512, 8193, size=256)
+    if kind == "c4_64":
+        return np.random.default_rng(4).integers(512, 8193, size=256)[:64]
     if kind == "c3":
         return np.random.default_rng(3).integers(17, 3001, size=32)
     if kind == "c2":

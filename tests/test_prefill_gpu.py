@@ -321,3 +321,28 @@ def test_prefill_events_variant_times_each_kernel(gdn, lens):
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
     times = [(start if i == 0 else evs[i - 1]).elapsed_time(evs[i]) for i in range(n)]
     assert all(t >= 0 for t in times) and sum(times) > 0, times
+
+
+MANY_LENS = [3000, 1000, 700, 600, 513, 1025, 2049, 100, 64, 65, 900, 1500, 777, 1200, 333,
+             2500, 950, 1100, 640, 1900]
+
+
+@pytest.mark.parametrize("slow_decay", [False, True])
+def test_segmented_evaluation_with_many_sequences(gdn, slow_decay):
+    """20 sequences (160 scan chains, fewer than the 296 scan slots): only the
+    sequences longer than two segments (here 8 chunks each, so > 1,024
+    tokens) are cut; those of 9..16 chunks run whole inside the segmented
+    call.  Against the fp32 recurrence, with the benchmark gates and with
+    slow decay (A_log in [-5, -2]) so that the joined state maps matter."""
+    lens = MANY_LENS
+    assert gdn._native.prefill_kernel_launches(sum(lens), len(lens)) == 5
+    inp = cases.prefill_inputs(seed=sum(lens) + 21, lens=lens, with_state=True)
+    if slow_decay:
+        inp["A_log"] = (np.random.default_rng(8).random(8, dtype=np.float32) * 3.0 - 5.0).astype(
+            np.float32)
+    o, s = _run(gdn, inp)
+    ro, rs = _oracle(inp)
+    assert out_err(o, ro) <= 1.0
+    st = s.cpu().numpy()
+    assert rel_fro(st, rs) < STATE_TOL
+    assert max(rel_fro(st[i], rs[i]) for i in range(len(lens))) < STATE_TOL
