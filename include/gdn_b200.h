@@ -175,12 +175,10 @@ int gdn_prefill_kernel_launches(int64_t total_tokens, int64_t num_seqs);
  * workspace   >= gdn_prefill_workspace_bytes(T, N) bytes, 1024-byte aligned
  * No host synchronisation: unlike the reference (kernel.py:1665, :181-184)
  * the chunk metadata is built on the device.
- * When the sequences' scan chains (8 per sequence) would leave the GPU's
- * scan slots idle -- num_seqs < 37 sequences averaging >= 12 chunks, decided
- * from T and N alone -- sequences longer than two segments are evaluated in
- * segments run in parallel and then joined through the segments' affine
- * state maps; results agree with the single-pass evaluation within the
- * stated tolerances, not bit for bit.
+ * Few long sequences (num_seqs <= 16 averaging >= 12 chunks, decided from T
+ * and N alone) are evaluated in segments run in parallel and then joined
+ * through the segments' affine state maps; results agree with the
+ * single-pass evaluation within the stated tolerances, not bit for bit.
  */
 int gdn_prefill_qk4_v8_d128_k_last(
     const void *q, const void *k, const void *v, const float *state,

@@ -83,9 +83,7 @@ def test_prefill_launch_count_follows_segment_policy(gdn):
     assert n(4096, 1) == 5        # one long sequence: segmented (3 passes + compose)
     assert n(16384, 4) == 5
     assert n(269, 1) == 3         # 5 chunks: too short to segment
-    assert n(44450, 32) == 5      # 256 scan chains < 296 slots: the longest sequences are cut
-    assert n(143000, 37) == 3     # 296 chains fill the slots: single pass
-    assert n(143000, 36) == 5
+    assert n(44450, 32) == 3      # more than 16 sequences: single pass
     assert n(11 * 64 * 2, 2) == 3  # fewer than 12 chunks per sequence on average
     assert n(12 * 64 * 2, 2) == 5
 

@@ -323,16 +323,16 @@ def test_prefill_events_variant_times_each_kernel(gdn, lens):
     assert all(t >= 0 for t in times) and sum(times) > 0, times
 
 
-MANY_LENS = [3000, 1000, 700, 600, 513, 1025, 2049, 100, 64, 65, 900, 1500, 777, 1200, 333,
-             2500, 950, 1100, 640, 1900]
+MANY_LENS = [3000, 1000, 700, 5000, 513, 1025, 2049, 100, 64, 65, 900, 1500, 777, 1200, 333,
+             2500]
 
 
 @pytest.mark.parametrize("slow_decay", [False, True])
 def test_segmented_evaluation_with_many_sequences(gdn, slow_decay):
-    """20 sequences (160 scan chains, fewer than the 296 scan slots): only the
-    sequences longer than two segments (here 8 chunks each, so > 1,024
-    tokens) are cut; those of 9..16 chunks run whole inside the segmented
-    call.  Against the fp32 recurrence, with the benchmark gates and with
+    """16 sequences, the most the segmented evaluation takes, with lengths
+    from 64 to 5,000 tokens: in one call the shortest ones (at most one
+    segment) run whole in pass 1 while the others are cut into two or more
+    segments.  Against the fp32 recurrence, with the benchmark gates and with
     slow decay (A_log in [-5, -2]) so that the joined state maps matter."""
     lens = MANY_LENS
     assert gdn._native.prefill_kernel_launches(sum(lens), len(lens)) == 5

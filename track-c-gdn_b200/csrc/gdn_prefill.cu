@@ -68,13 +68,10 @@ enum ScanItemMode : int { kItemFull = 0, kItemHead, kItemZero, kItemIdent, kItem
 // checks).
 enum MetaSlot : int { kMetaChunks = 0, kMetaError, kMetaPass1, kMetaPass3, kMetaN, kMetaT };
 
+// Segmented evaluation is used for at most this many sequences.
+constexpr int kSegMaxSeqs = 16;
 // Scan CTAs that run at once on a B200 (148 SMs x 2 CTAs).
 constexpr int64_t kScanSlots = 296;
-// Up to this many sequences the segment length aims at one wave of pass 1
-// (few long sequences); above it, while the sequences' scan chains (8 per
-// sequence) still leave slots idle, segments are longer (see
-// prefill_segment_chunks).
-constexpr int kSegFewSeqs = 16;
 
 struct PrefillWs {
   size_t meta, chunk_off, seq_order, chunk_tab, gcum, beta, m2, items, seg_off, seg_ss, seg_sb,
@@ -113,31 +110,16 @@ __device__ __forceinline__ void put_state_img_row(uint8_t *img, int row, int hc,
                    pack_bf16x2(x[8 * cc + 4], x[8 * cc + 5]), pack_bf16x2(x[8 * cc + 6], x[8 * cc + 7]));
 }
 
-// Segment length Lc (chunks) chosen from T and N alone, so that the
-// workspace size is a function of (T, N).  Segmentation pays only while the
-// sequences' scan chains (8 per sequence) leave scan slots idle and the
-// sequences average at least 12 chunks; the time is then the longest chain.
-// A sequence is cut only into P >= 3 segments (more than 2 Lc chunks): with
-// two, the second segment would still wait for the first.
-//   * N <= 16 (few long sequences): pass 1 (about two CTAs per segment and
-//     v-head) should fit one wave: Lc = 16 (nt + N) / slots, at least 4;
-//   * 16 < N < slots / 8 (e.g. one rank's share of a large batch): the
-//     unsegmented time is the longest sequence (up to several times the
-//     mean), the balanced time about 8 nt / slots chunk-steps; segments of
-//     Lc = 5.5 nt / slots (at least 8) cut only the longest sequences, so
-//     the critical path (about 2 Lc) drops to the balanced time while the
-//     extra work (a middle segment runs three times: B, Phi, then with
-//     outputs) stays in slots that would idle.
+// Segment length (chunks) chosen from T and N alone, so that the workspace
+// size is a function of (T, N): segment only when there are fewer scan
+// chains (8 per sequence) than SMs and the sequences average at least 12
+// chunks; make pass 1 (about two CTAs per segment and v-head) fit one wave.
 inline int64_t prefill_segment_chunks(int64_t T, int64_t N) {
-  if (N <= 0 || 8 * N >= kScanSlots) return 0;
+  if (N <= 0 || N > kSegMaxSeqs) return 0;
   const int64_t nt = (T + kChunk - 1) / kChunk;
   if (nt < 12 * N) return 0;
-  if (N <= kSegFewSeqs) {
-    const int64_t lc = (16 * (nt + N) + kScanSlots - 1) / kScanSlots;
-    return lc < 4 ? 4 : lc;
-  }
-  const int64_t lc = (11 * nt + 2 * kScanSlots - 1) / (2 * kScanSlots);
-  return lc < 8 ? 8 : lc;
+  const int64_t lc = (16 * (nt + N) + kScanSlots - 1) / kScanSlots;
+  return lc < 4 ? 4 : lc;
 }
 
 inline PrefillWs prefill_ws_layout(int64_t T, int64_t N, bool allow_segments = true) {
@@ -355,7 +337,7 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
     }
     return;
   }
-  // Segmented (N < kScanSlots / 8): thread 0 builds the tables, longest
+  // Segmented (N <= kSegMaxSeqs): thread 0 builds the tables, longest
   // sequences first.  Pass-1 items occupy items[0, 2 seg_max), pass-3 items
   // items[2 seg_max, 3 seg_max).
   if (tid == 0) {
@@ -363,7 +345,7 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
     for (int i = 0; i < N; ++i) {
       const int nc = chunk_off[i + 1] - chunk_off[i];
       seg_off[i] = so;
-      so += nc > 2 * seg_chunks ? (nc + seg_chunks - 1) / seg_chunks : 1;  // P >= 3 or whole
+      so += nc > seg_chunks ? (nc + seg_chunks - 1) / seg_chunks : 1;
     }
     seg_off[N] = so;
     if (so > seg_max) {  // cannot happen for a valid cu_seqlens (bound of the layout)
@@ -1014,11 +996,11 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const int hqk = hv >> 1;
   const int4 it = items[item];
   const int n = it.x, seg = it.y, mode = it.z;
-  // this item's token range: segment `seg` of sequence n, or the whole
-  // sequence for a FULL item (which may be up to 2 segments long)
+  // this item's token range: segment `seg` of sequence n (the whole sequence
+  // when not segmented: seg = 0 and seg_tokens exceeds any length)
   const int64_t seg_begin = static_cast<int64_t>(seg) * seg_tokens;
   const int64_t bos = cu[n] + seg_begin;
-  const int64_t len = mode == kItemFull ? cu[n + 1] - bos : lmin(cu[n + 1] - bos, seg_tokens);
+  const int64_t len = lmin(cu[n + 1] - bos, seg_tokens);
   const int nchunks = static_cast<int>((len + kChunk - 1) / kChunk);
   const int gbase = chunk_off[n] + static_cast<int>(seg_begin / kChunk);
   GDN_DCHECK(n >= 0 && n < meta[kMetaN] && mode >= kItemFull && mode <= kItemTail);
