@@ -54,6 +54,37 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&p);
 }
 
+// Packed fp32 pairs for the sm_100 f32x2 instructions (mul/fma/add.rn.f32x2:
+// two independent round-to-nearest fp32 operations per instruction, results
+// identical to the scalar instructions on the same operands).  A pair is a
+// 64-bit register {lo, hi}.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float f2_lo(uint64_t x) {
+  float lo;
+  asm("{\n\t.reg .f32 hi;\n\tmov.b64 {%0, hi}, %1;\n\t}" : "=f"(lo) : "l"(x));
+  return lo;
+}
+__device__ __forceinline__ float f2_hi(uint64_t x) {
+  float hi;
+  asm("{\n\t.reg .f32 lo;\n\tmov.b64 {lo, %0}, %1;\n\t}" : "=f"(hi) : "l"(x));
+  return hi;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// a * b + c, each half fused (one rounding)
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
 // softplus with threshold 20 -- reference decode kernel.py:21-23.
 __device__ __forceinline__ float softplus_thr20(float x) {
   return x <= 20.0f ? logf(1.0f + expf(x)) : x;
