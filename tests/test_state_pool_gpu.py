@@ -102,3 +102,30 @@ def test_bad_slot_sets_device_status(gdn):
                          pA, pa, pdt, pb, cu, None)
     assert gdn._native.read_device_status() == 3
     assert torch.equal(pool, before)
+
+
+def test_multi_token_pool_with_bad_slot(gdn):
+    """Multi-token pool decode (the streaming kernel, T <= 16) with one slot
+    outside the pool: status 3, the other requests served exactly as the
+    dense call on their gathered states, nothing else in the pool touched."""
+    P, B, T = 40, 37, 3
+    pool = _pool(P, 123)
+    slots = _slots(P, B, 124)
+    slots[5] = P + 3  # outside the pool
+    inp = cases.decode_mtp_inputs(seed=125, B=B, T=T, with_state=False)
+    q, k, v = bf16_dev(inp["q"]), bf16_dev(inp["k"]), bf16_dev(inp["v"])
+    A_log, dt = f32_dev(inp["A_log"]), f32_dev(inp["dt_bias"])
+    a, b = bf16_dev(inp["a"]), bf16_dev(inp["b"])
+    before = pool.clone()
+    good = torch.ones(B, dtype=torch.bool, device="cuda")
+    good[5] = False
+    gslots = slots[good].long()
+    o_ref, s_ref = gdn.decode.run_mtp(q[good], k[good], v[good], pool[gslots].clone(), A_log,
+                                      a[good], dt, b[good], None)
+    o = gdn.decode.run_pool(q, k, v, pool, slots, A_log, a, dt, b, None)
+    assert gdn._native.read_device_status() == 3
+    assert torch.equal(o[good], o_ref)
+    assert torch.equal(pool[gslots], s_ref)
+    untouched = torch.ones(P, dtype=torch.bool, device="cuda")
+    untouched[gslots] = False
+    assert torch.equal(pool[untouched], before[untouched])
