@@ -479,12 +479,24 @@ __device__ __forceinline__ void solve_diag_block_column(const float *AT, float *
       xb[jp] = (r == c) ? 1.f : (r < c ? 0.f : -acc[jp]);
       const float *colp = AT + (r0 + jp) * 64 + r0;
 #pragma unroll
+      const uint64_t xx = f2_pack(xb[jp], xb[jp]);
       for (int q = (jp + 1) / 4; q < 4; ++q) {
         const float4 a = *reinterpret_cast<const float4 *>(colp + 4 * q);
-        if (4 * q + 0 > jp) acc[4 * q + 0] += a.x * xb[jp];
-        if (4 * q + 1 > jp) acc[4 * q + 1] += a.y * xb[jp];
-        if (4 * q + 2 > jp) acc[4 * q + 2] += a.z * xb[jp];
-        if (4 * q + 3 > jp) acc[4 * q + 3] += a.w * xb[jp];
+        // rows 4q .. 4q+3 below jp: one packed pair (f32x2) where both rows are
+        if (4 * q + 0 > jp) {
+          const uint64_t r = f2_fma(f2_pack(a.x, a.y), xx, f2_pack(acc[4 * q], acc[4 * q + 1]));
+          acc[4 * q] = f2_lo(r);
+          acc[4 * q + 1] = f2_hi(r);
+        } else if (4 * q + 1 > jp) {
+          acc[4 * q + 1] += a.y * xb[jp];
+        }
+        if (4 * q + 2 > jp) {
+          const uint64_t r = f2_fma(f2_pack(a.z, a.w), xx, f2_pack(acc[4 * q + 2], acc[4 * q + 3]));
+          acc[4 * q + 2] = f2_lo(r);
+          acc[4 * q + 3] = f2_hi(r);
+        } else if (4 * q + 3 > jp) {
+          acc[4 * q + 3] += a.w * xb[jp];
+        }
       }
     }
     if (bb == 0) {
@@ -654,18 +666,25 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
             dc[u] = dec;
           }
           const float *a8 = acc + 8 * cc;
+          float prod[8];  // a8 * dc on packed pairs
+#pragma unroll
+          for (int u = 0; u < 8; u += 2) {
+            const uint64_t r = f2_mul(f2_pack(a8[u], a8[u + 1]), f2_pack(dc[u], dc[u + 1]));
+            prod[u] = f2_lo(r);
+            prod[u + 1] = f2_hi(r);
+          }
           if (warp >= 2) {
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int col = 8 * cc + u;
-              AT[(j * 64 + col) * 64 + i] = (rv && col < i) ? a8[u] * dc[u] : 0.f;
+              AT[(j * 64 + col) * 64 + i] = (rv && col < i) ? prod[u] : 0.f;
             }
           } else {
             float vals[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int col = 8 * cc + u;
-              vals[u] = (rv && col <= i) ? a8[u] * dc[u] : 0.f;
+              vals[u] = (rv && col <= i) ? prod[u] : 0.f;
             }
             prow[4 * cc + 0] = pack_bf16x2(vals[0], vals[1]);
             prow[4 * cc + 1] = pack_bf16x2(vals[2], vals[3]);
@@ -905,7 +924,8 @@ struct ScanSmem {
   static constexpr int kG = 81920;     // float eG[2][64]
   static constexpr int kB = kG + 512;  // float beta[2][64]
   static constexpr int kDec = kB + 512;  // float eDec[2][64]
-  static constexpr int kGl = kDec + 512;  // float eGlast[2]
+  static constexpr int kEn = kDec + 512;  // float -eG[2][64] (the X phase's fused multiply-add)
+  static constexpr int kGl = kEn + 512;  // float eGlast[2]
   static constexpr int kBar = kGl + 16;
   static constexpr int kBarMma = kBar, kBarQ = kBar + 8, kBarV = kBar + 16, kBarM2 = kBar + 24,
                        kBarK0 = kBar + 32;  // kBarK1 = kBarK0 + 8
@@ -999,6 +1019,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   float *Eg = reinterpret_cast<float *>(smem + SM::kG);
   float *Bs = reinterpret_cast<float *>(smem + SM::kB);
   float *Ed = reinterpret_cast<float *>(smem + SM::kDec);
+  float *En = reinterpret_cast<float *>(smem + SM::kEn);
   float *Egl = reinterpret_cast<float *>(smem + SM::kGl);
   volatile int *broken = reinterpret_cast<volatile int *>(smem + SM::kBroken);
   const uint32_t s_base = smem_u32(smem);
@@ -1052,7 +1073,9 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   };
   auto store_gates = [&](const GateRegs &r, int buf) {
     const float g = r.valid ? r.g : r.g_last;
-    Eg[buf * 64 + tid] = expf(g);
+    const float eg = expf(g);
+    Eg[buf * 64 + tid] = eg;
+    En[buf * 64 + tid] = -eg;
     Bs[buf * 64 + tid] = r.beta;
     Ed[buf * 64 + tid] = r.valid ? expf(r.g_last - g) : 0.f;
     if (tid == 0) Egl[buf] = expf(r.g_last);
@@ -1192,15 +1215,21 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         tmem_wait_ld();
   #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          const float4 eg4 = *reinterpret_cast<const float4 *>(Eg + cb * 64 + tb + 4 * g);
+          // packed pairs (f32x2): x = beta * fma(-e^G, y, v), as the scalar form
+          const float4 en4 = *reinterpret_cast<const float4 *>(En + cb * 64 + tb + 4 * g);
           const float4 bt4 = *reinterpret_cast<const float4 *>(Bs + cb * 64 + tb + 4 * g);
-          const float eg[4] = {eg4.x, eg4.y, eg4.z, eg4.w};
-          const float bt[4] = {bt4.x, bt4.y, bt4.z, bt4.w};
+          const uint64_t en2[2] = {f2_pack(en4.x, en4.y), f2_pack(en4.z, en4.w)};
+          const uint64_t bt2[2] = {f2_pack(bt4.x, bt4.y), f2_pack(bt4.z, bt4.w)};
   #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int j = 4 * g + u, t = tb + j;
-            const float vv = (t < L && (kOut || !ident)) ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
-            yk[j] = bt[u] * (vv - eg[u] * yk[j]);
+          for (int h = 0; h < 2; ++h) {
+            const int j = 4 * g + 2 * h, t = tb + j;
+            const float v0 = (t < L && (kOut || !ident)) ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
+            const float v1 =
+                (t + 1 < L && (kOut || !ident)) ? bf16_to_f32(vt[(t + 1) * kD + vrow]) : 0.f;
+            const uint64_t x =
+                f2_mul(bt2[h], f2_fma(en2[h], f2_pack(yk[j], yk[j + 1]), f2_pack(v0, v1)));
+            yk[j] = f2_lo(x);
+            yk[j + 1] = f2_hi(x);
           }
         }
         // bf16 X into the Yk columns this thread has read (MMA 2's A operand)
@@ -1250,16 +1279,23 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
           tmem_ld16(tlane + SM::kColY + tb, zq);
           tmem_ld16(tlane + SM::kColOi + tb, zo);
           tmem_wait_ld();
+          const uint64_t sc2 = f2_pack(scale, scale);
   #pragma unroll
           for (int g = 0; g < 4; ++g) {
             const float4 eg4 = *reinterpret_cast<const float4 *>(Eg + cb * 64 + tb + 4 * g);
-            const float eg[4] = {eg4.x, eg4.y, eg4.z, eg4.w};
+            const uint64_t eg2[2] = {f2_pack(eg4.x, eg4.y), f2_pack(eg4.z, eg4.w)};
   #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int j = 4 * g + u, t = tb + j;
+            for (int h = 0; h < 2; ++h) {
+              const int j = 4 * g + 2 * h, t = tb + j;
+              // scale * (e^G Yq + O_intra) on a packed pair
+              const uint64_t o = f2_mul(sc2, f2_fma(eg2[h], f2_pack(zq[j], zq[j + 1]),
+                                                   f2_pack(zo[j], zo[j + 1])));
               if (t < L)
                 out[((t0 + t) * kHV + hv) * kD + vrow] =
-                    __bfloat16_as_ushort(__float2bfloat16_rn(scale * (eg[u] * zq[j] + zo[j])));
+                    __bfloat16_as_ushort(__float2bfloat16_rn(f2_lo(o)));
+              if (t + 1 < L)
+                out[((t0 + t + 1) * kHV + hv) * kD + vrow] =
+                    __bfloat16_as_ushort(__float2bfloat16_rn(f2_hi(o)));
             }
           }
         }
@@ -1273,17 +1309,17 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
           for (int j = 0; j < 16; ++j) put_tok_img(img, tb + j, vrow, tb + j < L ? zv[j] : 0.f);
         }
+        // V_dec = e^{G_last - G_t} V_new (0 past the end), on packed pairs, then
+        // bf16 into the V_new columns this thread has read (MMA 3's A operand)
+        uint32_t pk[8];
   #pragma unroll
         for (int g = 0; g < 4; ++g) {
           const float4 ed4 = *reinterpret_cast<const float4 *>(Ed + cb * 64 + tb + 4 * g);
-          const float ed[4] = {ed4.x, ed4.y, ed4.z, ed4.w};
-  #pragma unroll
-          for (int u = 0; u < 4; ++u) zv[4 * g + u] *= ed[u];  // e^{G_last - G_t}, 0 past the end
+          const uint64_t a = f2_mul(f2_pack(zv[4 * g], zv[4 * g + 1]), f2_pack(ed4.x, ed4.y));
+          const uint64_t b = f2_mul(f2_pack(zv[4 * g + 2], zv[4 * g + 3]), f2_pack(ed4.z, ed4.w));
+          pk[2 * g] = pack_bf16x2(f2_lo(a), f2_hi(a));
+          pk[2 * g + 1] = pack_bf16x2(f2_lo(b), f2_hi(b));
         }
-        // bf16 V_dec into the V_new columns this thread has read (MMA 3's A operand)
-        uint32_t pk[8];
-  #pragma unroll
-        for (int j = 0; j < 8; ++j) pk[j] = pack_bf16x2(zv[2 * j], zv[2 * j + 1]);
         tmem_st8(tlane + SM::kColVn + 32 * hc + 8 * p, pk);
       }
       tmem_wait_st();
@@ -1313,8 +1349,14 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
           float ds[32];
           tmem_ld32(tlane + SM::kColY + 64 * hc + 32 * p, ds);
           tmem_wait_ld();
+          const uint64_t gl2 = f2_pack(eg_last, eg_last);
   #pragma unroll
-          for (int j = 0; j < 32; ++j) s[32 * p + j] = eg_last * s[32 * p + j] + ds[j];
+          for (int j = 0; j < 32; j += 2) {  // e^{G_last} S + dS on packed pairs
+            const uint64_t x =
+                f2_fma(gl2, f2_pack(s[32 * p + j], s[32 * p + j + 1]), f2_pack(ds[j], ds[j + 1]));
+            s[32 * p + j] = f2_lo(x);
+            s[32 * p + j + 1] = f2_hi(x);
+          }
         }
         uint32_t pk[32];
   #pragma unroll
