@@ -478,8 +478,8 @@ __device__ __forceinline__ void solve_diag_block_column(const float *AT, float *
       const int r = r0 + jp;
       xb[jp] = (r == c) ? 1.f : (r < c ? 0.f : -acc[jp]);
       const float *colp = AT + (r0 + jp) * 64 + r0;
-#pragma unroll
       const uint64_t xx = f2_pack(xb[jp], xb[jp]);
+#pragma unroll
       for (int q = (jp + 1) / 4; q < 4; ++q) {
         const float4 a = *reinterpret_cast<const float4 *>(colp + 4 * q);
         // rows 4q .. 4q+3 below jp: one packed pair (f32x2) where both rows are
@@ -516,6 +516,11 @@ __device__ __forceinline__ void solve_diag_block_column(const float *AT, float *
   }
 }
 
+// kPA: the image is [P Ainv ; Ainv] (the backward's recompute and gradient
+// kernels use P Ainv); otherwise [P ; Ainv] (the forward scan forms its
+// intra-chunk output from P itself), and the P rows go to the workspace
+// straight from the A/P phase, with no P Ainv product.
+template <bool kPA>
 __global__ void __launch_bounds__(kPrepThreads, 4)
 gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         const __grid_constant__ CUtensorMap tmap_k,
@@ -697,7 +702,18 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
           for (int k = 16; k < 32; ++k) prow[k] = 0u;
         }
         // D's columns 0..63 were read above; lanes 0..63 now keep P_0 | P_1
-        if (warp < 2) tmem_st32(trow + 32 * j, prow);
+        if (warp < 2) {
+          if constexpr (kPA) {
+            tmem_st32(trow + 32 * j, prow);
+          } else {
+            // row i of P_j -> row i of the workspace image of v-head 2 hqk + j
+            uint8_t *img = m2_ws + ((static_cast<size_t>(gchunk) * kHV + 2 * hqk + j) * kM2Bytes);
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc)
+              *reinterpret_cast<uint4 *>(img + sw128(i, cc)) =
+                  make_uint4(prow[4 * cc], prow[4 * cc + 1], prow[4 * cc + 2], prow[4 * cc + 3]);
+          }
+        }
       }
     };
     if (warp & 1)
@@ -813,6 +829,22 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   tc_fence_before();
   __syncthreads();  // every column solved: the A region is free
   tc_fence_after();
+  uint8_t *img0 = m2_ws + (static_cast<size_t>(gchunk) * kHV + 2 * hqk) * kM2Bytes;
+  if constexpr (!kPA) {
+    // [P ; Ainv]: the P rows are already out; Ainv halves -> rows 64..127
+    for (int idx = tid; idx < 2 * 512; idx += kPrepThreads) {
+      const int j = idx >> 9, o = idx & 511;
+      reinterpret_cast<uint4 *>(img0 + j * kM2Bytes + 8192)[o] =
+          reinterpret_cast<const uint4 *>(ai + j * 8192)[o];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+      tc_fence_after();
+      tmem_dealloc(tmem, kPrepTmemCols);
+    }
+    return;
+  }
   if (warp < 2) {
     const int i = warp * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
@@ -849,7 +881,6 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     umma_commit(bar);
   }
   // Ainv halves -> rows 64..127 of the workspace images while the MMA runs.
-  uint8_t *img0 = m2_ws + (static_cast<size_t>(gchunk) * kHV + 2 * hqk) * kM2Bytes;
   for (int idx = tid; idx < 2 * 512; idx += kPrepThreads) {
     const int j = idx >> 9, o = idx & 511;
     reinterpret_cast<uint4 *>(img0 + j * kM2Bytes + 8192)[o] =
@@ -917,7 +948,7 @@ struct ScanSmem {
   static constexpr int kQ = 0;         // Q tile: 2 d-blocks x 64 t x 128 B, 128-byte swizzle
   static constexpr int kK0 = 16384;    // K tiles, same layout, double buffered
   static constexpr int kK1 = 32768;
-  static constexpr int kM2 = 49152;    // [PA ; Ainv] image, 128 rows x 128 B
+  static constexpr int kM2 = 49152;    // [P ; Ainv] image, 128 rows x 128 B
   static constexpr int kV = 65536;     // V tile: 64 t rows x 128 v bf16, unswizzled (16 KB)
   // per-token gate factors of the current / next chunk, computed once per
   // chunk: e^{G_t}, beta_t, e^{G_last - G_t} (0 past the end), e^{G_last}
@@ -931,13 +962,18 @@ struct ScanSmem {
                        kBarK0 = kBar + 32;  // kBarK1 = kBarK0 + 8
   static constexpr int kTmem = kBar + 48;
   static constexpr int kBroken = kBar + 52;
+  static constexpr int kBarO = kBar + 56;  // the output MMA (O += bf16(V_new) P^T)
   static constexpr int kBytes = kBar + 64 + 1024;  // + base alignment slack
   static constexpr uint32_t kTmemCols = 256;
-  static constexpr uint32_t kColSb = 0, kColOi = 64, kColY = 128;
-  // bf16 operand images that MMA 2 and MMA 3 read from TMEM: X over the Yk
-  // columns (thread half hc: columns kColX + 32 hc .. + 15, two tokens per
-  // column), V_new and then V_dec over the bf16(S) columns
-  static constexpr uint32_t kColX = kColY + 64, kColVn = kColSb;
+  // kColO: e^G Yq = S Q~^T (MMA 1), then + bf16(V_new) P^T (the output MMA):
+  // scale * that is the output.  kColY: Yk (MMA 1), then dS (MMA 3, 128
+  // columns).
+  static constexpr uint32_t kColSb = 0, kColO = 64, kColY = 128, kColYk = kColY;
+  // bf16 operand images read from TMEM: X over the Yk columns (thread half
+  // hc: columns kColX + 32 hc .. + 15, two tokens per column; MMA 2), then
+  // bf16(V_new) in the same columns (the output MMA); V_new and then V_dec
+  // (MMA 3) over the bf16(S) columns
+  static constexpr uint32_t kColX = kColYk, kColVnb = kColX, kColVn = kColSb;
 };
 // the epilogue stages one 64 KB (n, hv) state over the Q, K and [PA;Ainv] tiles
 static_assert(ScanSmem::kQ == 0 && ScanSmem::kV >= 65536, "state staging region");
@@ -1025,7 +1061,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar_mma = s_base + SM::kBarMma, bar_q = s_base + SM::kBarQ,
                  bar_v = s_base + SM::kBarV, bar_m2 = s_base + SM::kBarM2,
-                 bar_k0 = s_base + SM::kBarK0;
+                 bar_k0 = s_base + SM::kBarK0, bar_o = s_base + SM::kBarO;
 
   // Items without outputs (ZERO, IDENT) need neither Q nor the Q-side MMAs;
   // IDENT treats V as zero and needs no V either.
@@ -1087,6 +1123,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   if (tid == 0) {
     *broken = 0;
     for (int i = 0; i < 6; ++i) mbar_init(bar_mma + 8 * i, 1);
+    mbar_init(bar_o, 1);
     mbar_init_fence();
     if (nchunks > 0) {
       if (need_q) issue_qk(false, 0, s_base + SM::kQ, bar_q);
@@ -1132,7 +1169,8 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 
   const uint32_t idesc_n64 = umma_idesc_bf16(128, 64, false, false);
   const uint32_t idesc_ds = umma_idesc_bf16(128, 128, false, true);
-  uint32_t ph_mma = 0, ph_q = 0, ph_v = 0, ph_m2 = 0, ph_k = 0;  // ph_k: bit b = parity of K buffer b
+  uint32_t ph_mma = 0, ph_q = 0, ph_v = 0, ph_m2 = 0, ph_o = 0;
+  uint32_t ph_k = 0;  // bit b = parity of K buffer b
 
   // The chunk loop, instantiated twice: with outputs (FULL, HEAD, MID, TAIL)
   // and state only (ZERO, IDENT).  Compile-time flags keep the loop free of
@@ -1176,23 +1214,51 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         __syncthreads();
       }
 
-      // ---- MMA 1: Yk = S K^T (committed first: X needs it), then Yq = S Q^T
-      // (read only after MMA 2, whose commit also covers it) ----
+      // ---- MMA 1: Yk = S K^T (committed: X needs it); then, with the Q tile
+      // scaled in place to Q~ = e^G Q while Yk computes, e^G Yq = S Q~^T into
+      // the output columns (read only after MMA 2, whose commit covers it) ----
       if (tid == 0) {
         tc_fence_after();
   #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
-          umma_bf16_ts(tmem + SM::kColY + 64, tmem + SM::kColSb + 8 * ks,
+          umma_bf16_ts(tmem + SM::kColYk, tmem + SM::kColSb + 8 * ks,
                        umma_desc_sw128(kbuf + boff, 16, 1024), idesc_n64, ks > 0);
         }
         umma_commit(bar_mma);
-        if constexpr (kOut) {
-          if (!tail) wait_phase(bar_q, ph_q, broken);
+      }
+      if constexpr (kOut) {
+        // every thread waits for the Q tile here (thread 0 re-arms its barrier
+        // only after MMA 2, which all threads reach after the barrier below)
+        if (!tail) wait_phase(bar_q, ph_q, broken);
+        // row t of both 64-column blocks times e^{G_t}: 4 of the tile's 1,024
+        // 16-byte pieces per thread (a piece lies in one row; the swizzle only
+        // permutes pieces within a row), on packed pairs
+  #pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int piece = tid + kScanThreads * m;
+          const int db = piece >> 9, t = (piece >> 3) & 63;
+          uint4 *ptr = reinterpret_cast<uint4 *>(smem + SM::kQ + db * 8192 + t * 128 + (piece & 7) * 16);
+          const uint4 w = *ptr;
+          const float e = Eg[cb * 64 + t];
+          const uint64_t ee = f2_pack(e, e);
+          const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+          uint32_t o[4];
+  #pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const uint64_t r = f2_mul(f2_pack(bf16_lo(in[h]), bf16_hi(in[h])), ee);
+            o[h] = pack_bf16x2(f2_lo(r), f2_hi(r));
+          }
+          *ptr = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+          tc_fence_after();
   #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
-            umma_bf16_ts(tmem + SM::kColY, tmem + SM::kColSb + 8 * ks,
+            umma_bf16_ts(tmem + SM::kColO, tmem + SM::kColSb + 8 * ks,
                          umma_desc_sw128(s_base + SM::kQ + boff, 16, 1024), idesc_n64, ks > 0);
           }
         }
@@ -1211,7 +1277,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       for (int p = 0; p < 2; ++p) {
         const int tb = 32 * hc + 16 * p;
         float yk[16];
-        tmem_ld16(tlane + SM::kColY + 64 + tb, yk);
+        tmem_ld16(tlane + SM::kColYk + tb, yk);
         tmem_wait_ld();
   #pragma unroll
         for (int g = 0; g < 4; ++g) {
@@ -1244,21 +1310,15 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tc_fence_after();
       if (tid == 0 && (kOut || need_v) && c + 1 < nchunks) issue_v(c + 1);
 
-      // ---- MMA 2: O_intra = X PA^T (free columns 64..127), V_new = X Ainv^T ----
+      // ---- MMA 2: V_new = X Ainv^T ----
+      const uint32_t m2buf = s_base + SM::kM2;
       if (tid == 0) {
         wait_phase(bar_m2, ph_m2, broken);
         tc_fence_after();
-        if constexpr (kOut) {
-  #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_bf16_ts(tmem + SM::kColOi, tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
-                         umma_desc_sw128(s_base + SM::kM2 + ks * 32, 16, 1024), idesc_n64, ks > 0);
-        }
   #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
           umma_bf16_ts(tmem + SM::kColVn, tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
-                       umma_desc_sw128(s_base + SM::kM2 + 8192 + ks * 32, 16, 1024), idesc_n64,
-                       ks > 0);
+                       umma_desc_sw128(m2buf + 8192 + ks * 32, 16, 1024), idesc_n64, ks > 0);
         umma_commit(bar_mma);
       }
       ph_m2 ^= 1;
@@ -1266,39 +1326,16 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       ph_mma ^= 1;
       tc_fence_after();
       if (tid == 0 && c + 1 < nchunks) {
-        issue_m2(c + 1);
+        // the output MMA still reads this chunk's P rows: with outputs the next
+        // image is issued once that MMA has completed
+        if constexpr (!kOut) issue_m2(c + 1);
         if constexpr (kOut) issue_qk(false, c + 1, s_base + SM::kQ, bar_q);  // MMA 1's Q reads are done too
       }
 
-      // ---- outputs O = scale (e^G Yq + O_intra) and V_dec ----
+      // ---- V_dec (the outputs wait until MMA 3 runs) ----
   #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const int tb = 32 * hc + 16 * p;
-        if constexpr (kOut) {
-          float zq[16], zo[16];
-          tmem_ld16(tlane + SM::kColY + tb, zq);
-          tmem_ld16(tlane + SM::kColOi + tb, zo);
-          tmem_wait_ld();
-          const uint64_t sc2 = f2_pack(scale, scale);
-  #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const float4 eg4 = *reinterpret_cast<const float4 *>(Eg + cb * 64 + tb + 4 * g);
-            const uint64_t eg2[2] = {f2_pack(eg4.x, eg4.y), f2_pack(eg4.z, eg4.w)};
-  #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int j = 4 * g + 2 * h, t = tb + j;
-              // scale * (e^G Yq + O_intra) on a packed pair
-              const uint64_t o = f2_mul(sc2, f2_fma(eg2[h], f2_pack(zq[j], zq[j + 1]),
-                                                   f2_pack(zo[j], zo[j + 1])));
-              if (t < L)
-                out[((t0 + t) * kHV + hv) * kD + vrow] =
-                    __bfloat16_as_ushort(__float2bfloat16_rn(f2_lo(o)));
-              if (t + 1 < L)
-                out[((t0 + t + 1) * kHV + hv) * kD + vrow] =
-                    __bfloat16_as_ushort(__float2bfloat16_rn(f2_hi(o)));
-            }
-          }
-        }
         float zv[16];
         tmem_ld16(tlane + SM::kColVn + tb, zv);
         tmem_wait_ld();
@@ -1312,6 +1349,13 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         // V_dec = e^{G_last - G_t} V_new (0 past the end), on packed pairs, then
         // bf16 into the V_new columns this thread has read (MMA 3's A operand)
         uint32_t pk[8];
+        if constexpr (kOut) {
+          // bf16(V_new) into the X columns (MMA 2 has read them): the output
+          // MMA's A operand
+  #pragma unroll
+          for (int j = 0; j < 8; ++j) pk[j] = pack_bf16x2(zv[2 * j], zv[2 * j + 1]);
+          tmem_st8(tlane + SM::kColVnb + 32 * hc + 8 * p, pk);
+        }
   #pragma unroll
         for (int g = 0; g < 4; ++g) {
           const float4 ed4 = *reinterpret_cast<const float4 *>(Ed + cb * 64 + tb + 4 * g);
@@ -1327,8 +1371,16 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       __syncthreads();
       tc_fence_after();
 
-      // ---- MMA 3: dS = V_dec K ----
+      // ---- output MMA: O += bf16(V_new) P^T (onto e^G Yq; before MMA 3, which
+      // overwrites its A operand), then MMA 3: dS = V_dec K ----
       if (tid == 0) {
+        if constexpr (kOut) {
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16_ts(tmem + SM::kColO, tmem + SM::kColVnb + 32 * (ks >> 1) + 8 * (ks & 1),
+                         umma_desc_sw128(m2buf + ks * 32, 16, 1024), idesc_n64, 1);
+          umma_commit(bar_o);
+        }
   #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
           umma_bf16_ts(tmem + SM::kColY, tmem + SM::kColVn + 32 * (ks >> 1) + 8 * (ks & 1),
@@ -1336,6 +1388,34 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         umma_commit(bar_mma);
       }
       if (tid < 64 && c + 1 < nchunks) store_gates(next_gates, cb ^ 1);
+      if constexpr (kOut) {
+        // ---- outputs O = scale (e^G Yq + bf16(V_new) P^T), while MMA 3 runs
+        // (it writes columns kColY.., these are kColO..); then this chunk's
+        // image is no longer read and the next one can come in ----
+        wait_phase(bar_o, ph_o, broken);
+        ph_o ^= 1;
+        tc_fence_after();
+        if (tid == 0 && c + 1 < nchunks) issue_m2(c + 1);
+        const uint64_t sc2 = f2_pack(scale, scale);
+  #pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const int tb = 32 * hc + 16 * p;
+          float zo[16];
+          tmem_ld16(tlane + SM::kColO + tb, zo);
+          tmem_wait_ld();
+  #pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const int t = tb + j;
+            const uint64_t o = f2_mul(sc2, f2_pack(zo[j], zo[j + 1]));
+            if (t < L)
+              out[((t0 + t) * kHV + hv) * kD + vrow] =
+                  __bfloat16_as_ushort(__float2bfloat16_rn(f2_lo(o)));
+            if (t + 1 < L)
+              out[((t0 + t + 1) * kHV + hv) * kD + vrow] =
+                  __bfloat16_as_ushort(__float2bfloat16_rn(f2_hi(o)));
+          }
+        }
+      }
       wait_phase(bar_mma, ph_mma, broken);
       ph_mma ^= 1;
       tc_fence_after();
@@ -1604,12 +1684,12 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   if (err == cudaSuccess) err = mark();
   if (err != cudaSuccess) return err;
 
-  err = cudaFuncSetAttribute(gdn_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kPrepSmem);
+  err = cudaFuncSetAttribute(gdn_prefill_prep_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem);
   if (err != cudaSuccess) return err;
   if (w.nt_max > 0) {
     dim3 grid(static_cast<unsigned>(w.nt_max), kHQK);
-    gdn_prefill_prep_kernel<<<grid, kPrepThreads, kPrepSmem, stream>>>(
+    gdn_prefill_prep_kernel<false><<<grid, kPrepThreads, kPrepSmem, stream>>>(
         tq, tk, A_log, static_cast<const uint16_t *>(a), dt_bias,
         static_cast<const uint16_t *>(b), cu_seqlens, meta, chunk_tab, gcum, beta, m2);
     err = cudaGetLastError();

@@ -981,12 +981,12 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
       items, seg_off, nullptr, 0);
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
-  err = cudaFuncSetAttribute(gdn_prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  err = cudaFuncSetAttribute(gdn_prefill_prep_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kPrepSmem);
   if (err != cudaSuccess) return err;
   if (f.nt_max > 0) {
     dim3 grid(static_cast<unsigned>(f.nt_max), kHQK);
-    gdn_prefill_prep_kernel<<<grid, kPrepThreads, kPrepSmem, stream>>>(
+    gdn_prefill_prep_kernel<true><<<grid, kPrepThreads, kPrepSmem, stream>>>(
         tq, tk, A_log, static_cast<const uint16_t *>(a), dt_bias,
         static_cast<const uint16_t *>(b), cu_seqlens, meta, chunk_tab, gcum, beta, m2);
     err = cudaGetLastError();
