@@ -85,6 +85,27 @@ struct PrefillWs {
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 constexpr size_t kM2Bytes = 128 * 128;  // [PA ; Ainv] 128 rows x 64 bf16
+// The forward's [P ; Ainv] image keeps only what can be nonzero.  P and Ainv
+// are lower triangular (column s <= row t), so the 16 columns of K-step ks
+// (s = 16 ks .. 16 ks + 15) are nonzero only in rows t >= 16 ks: K-step ks is
+// stored as rows 16 ks .. 63 in the no-swizzle K-major operand layout (core
+// matrices of 8 rows x 16 bytes; 8-row groups 256 B apart, the two 8-column
+// halves 128 B apart) and the scan's MMAs over it have N = 64 - 16 ks.
+// One matrix is 5 KiB (5/8 of the full 8 KiB), the image 10 KiB.
+constexpr size_t kTriBytes = 5120;
+constexpr size_t kImgFwdBytes = 2 * kTriBytes;
+constexpr uint32_t kTriSbo = 256, kTriLbo = 128;
+// byte offset of K-step ks (0..4) inside one matrix
+__host__ __device__ constexpr uint32_t tri_step_off(int ks) {
+  return static_cast<uint32_t>(2048 * ks - 256 * ks * (ks - 1));
+}
+static_assert(tri_step_off(4) == kTriBytes, "K-step offsets");
+// byte offset of the 16-byte piece cc (columns 8 cc .. 8 cc + 7) of row t;
+// stored only for cc / 2 <= t / 16
+__device__ __forceinline__ uint32_t tri_off(int t, int cc) {
+  const int ks = cc >> 1, r = t - 16 * ks;
+  return tri_step_off(ks) + static_cast<uint32_t>((r >> 3) * kTriSbo + (cc & 1) * kTriLbo + (r & 7) * 16);
+}
 constexpr size_t kStateBytes = static_cast<size_t>(kHV) * kD * kD * sizeof(float);
 // a 128 x 128 state (one v-head) as a bf16 tensor-core operand image
 constexpr size_t kStateImgBytes = static_cast<size_t>(kD) * kD * 2;
@@ -706,12 +727,14 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
           if constexpr (kPA) {
             tmem_st32(trow + 32 * j, prow);
           } else {
-            // row i of P_j -> row i of the workspace image of v-head 2 hqk + j
-            uint8_t *img = m2_ws + ((static_cast<size_t>(gchunk) * kHV + 2 * hqk + j) * kM2Bytes);
+            // row i of P_j -> row i of the compact image of v-head 2 hqk + j
+            // (the K-steps ks <= i / 16)
+            uint8_t *img = m2_ws + ((static_cast<size_t>(gchunk) * kHV + 2 * hqk + j) * kImgFwdBytes);
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc)
-              *reinterpret_cast<uint4 *>(img + sw128(i, cc)) =
-                  make_uint4(prow[4 * cc], prow[4 * cc + 1], prow[4 * cc + 2], prow[4 * cc + 3]);
+            for (int cc = 0; cc < kGroups; ++cc)
+              if ((cc >> 1) <= (i >> 4))
+                *reinterpret_cast<uint4 *>(img + tri_off(i, cc)) =
+                    make_uint4(prow[4 * cc], prow[4 * cc + 1], prow[4 * cc + 2], prow[4 * cc + 3]);
           }
         }
       }
@@ -829,13 +852,19 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   tc_fence_before();
   __syncthreads();  // every column solved: the A region is free
   tc_fence_after();
-  uint8_t *img0 = m2_ws + (static_cast<size_t>(gchunk) * kHV + 2 * hqk) * kM2Bytes;
   if constexpr (!kPA) {
-    // [P ; Ainv]: the P rows are already out; Ainv halves -> rows 64..127
-    for (int idx = tid; idx < 2 * 512; idx += kPrepThreads) {
-      const int j = idx >> 9, o = idx & 511;
-      reinterpret_cast<uint4 *>(img0 + j * kM2Bytes + 8192)[o] =
-          reinterpret_cast<const uint4 *>(ai + j * 8192)[o];
+    // [P ; Ainv]: the P rows are already out; the stored K-steps of Ainv_j
+    // (128-byte-swizzled rows in shared memory) -> the compact image's second
+    // matrix, one 16-byte piece per iteration, consecutive in global memory
+    uint8_t *img0 = m2_ws + (static_cast<size_t>(gchunk) * kHV + 2 * hqk) * kImgFwdBytes + kTriBytes;
+    constexpr int kPieces = static_cast<int>(kTriBytes / 16);  // 320 per matrix
+    for (int idx = tid; idx < 2 * kPieces; idx += kPrepThreads) {
+      const int j = idx >= kPieces, q = idx - j * kPieces;
+      const int ks = q < 128 ? 0 : q < 224 ? 1 : q < 288 ? 2 : 3;
+      const int qb = q - static_cast<int>(tri_step_off(ks) >> 4);
+      const int t = 16 * ks + (qb >> 4) * 8 + (qb & 7), cc = 2 * ks + ((qb >> 3) & 1);
+      reinterpret_cast<uint4 *>(img0 + j * kImgFwdBytes)[q] =
+          *reinterpret_cast<const uint4 *>(ai + j * 8192 + sw128(t, cc));
     }
     tc_fence_before();
     __syncthreads();
@@ -845,6 +874,7 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
     return;
   }
+  uint8_t *img0 = m2_ws + (static_cast<size_t>(gchunk) * kHV + 2 * hqk) * kM2Bytes;
   if (warp < 2) {
     const int i = warp * 32 + lane;
     const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
@@ -1080,10 +1110,13 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     mbar_arrive_expect_tx(bar_v, 16384);
     tma_load_2d(s_base + SM::kV, &tmap_v, hv * kD, static_cast<int>(bos + static_cast<int64_t>(c) * kChunk), bar_v);
   };
+  // the backward's recompute reads the full [PA ; Ainv] image, the forward
+  // the compact [P ; Ainv] one
+  constexpr uint32_t kImgBytes = static_cast<uint32_t>(kSave ? kM2Bytes : kImgFwdBytes);
   auto issue_m2 = [&](int c) {
-    mbar_arrive_expect_tx(bar_m2, static_cast<uint32_t>(kM2Bytes));
-    bulk_load(s_base + SM::kM2, m2_ws + (static_cast<int64_t>(gbase + c) * kHV + hv) * kM2Bytes,
-              static_cast<uint32_t>(kM2Bytes), bar_m2);
+    mbar_arrive_expect_tx(bar_m2, kImgBytes);
+    bulk_load(s_base + SM::kM2, m2_ws + (static_cast<int64_t>(gbase + c) * kHV + hv) * kImgBytes,
+              kImgBytes, bar_m2);
   };
   // Gates of chunk c for token `tid` (threads 0..63): fetched into registers
   // a chunk ahead, turned into the per-token factors when the buffer is free.
@@ -1315,10 +1348,20 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       if (tid == 0) {
         wait_phase(bar_m2, ph_m2, broken);
         tc_fence_after();
+        if constexpr (kSave) {
   #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          umma_bf16_ts(tmem + SM::kColVn, tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
-                       umma_desc_sw128(m2buf + 8192 + ks * 32, 16, 1024), idesc_n64, ks > 0);
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16_ts(tmem + SM::kColVn, tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
+                         umma_desc_sw128(m2buf + 8192 + ks * 32, 16, 1024), idesc_n64, ks > 0);
+        } else {
+          // K-step ks only reaches tokens t >= 16 ks (N = 64 - 16 ks)
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16_ts(tmem + SM::kColVn + 16 * ks,
+                         tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
+                         umma_desc_noswz(m2buf + kTriBytes + tri_step_off(ks), kTriLbo, kTriSbo),
+                         umma_idesc_bf16(128, 64 - 16 * ks, false, false), ks > 0);
+        }
         umma_commit(bar_mma);
       }
       ph_m2 ^= 1;
@@ -1377,8 +1420,10 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         if constexpr (kOut) {
   #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
-            umma_bf16_ts(tmem + SM::kColO, tmem + SM::kColVnb + 32 * (ks >> 1) + 8 * (ks & 1),
-                         umma_desc_sw128(m2buf + ks * 32, 16, 1024), idesc_n64, 1);
+            umma_bf16_ts(tmem + SM::kColO + 16 * ks,
+                         tmem + SM::kColVnb + 32 * (ks >> 1) + 8 * (ks & 1),
+                         umma_desc_noswz(m2buf + tri_step_off(ks), kTriLbo, kTriSbo),
+                         umma_idesc_bf16(128, 64 - 16 * ks, false, false), 1);
           umma_commit(bar_o);
         }
   #pragma unroll
@@ -1449,10 +1494,15 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tc_fence_after();
     }
   };
-  if (write_out && !kSave)
-    chunk_loop(std::true_type{});
-  else
+  // (the recompute has no outputs: its kernel has no output loop at all)
+  if constexpr (!kSave) {
+    if (write_out)
+      chunk_loop(std::true_type{});
+    else
+      chunk_loop(std::false_type{});
+  } else {
     chunk_loop(std::false_type{});
+  }
 
   if (fin != nullptr) {
     // The (n, hv) state is one contiguous 64 KB block.  It goes out through

@@ -41,6 +41,21 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// Shared-memory matrix descriptor for the canonical no-swizzle K-major
+// layout: the operand is a grid of core matrices of 8 rows x 16 bytes (8
+// bf16 of K), each 128 contiguous bytes; lbo_bytes = distance between core
+// matrices adjacent in K, sbo_bytes = between core matrices adjacent in M/N.
+// [61,64) layout = 0 (no swizzle).
+__device__ __forceinline__ uint64_t umma_desc_noswz(uint32_t saddr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 accumulation:
 //   [4,6) D format = 1 (f32)   [7,10) A format = 1 (bf16)  [10,13) B format = 1
 //   [15] A major (1 = MN)      [16] B major (1 = MN)
