@@ -949,64 +949,82 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // ---------------------------------------------------------------------------
 // 3. sequential inter-chunk scan
 // ---------------------------------------------------------------------------
-// One CTA per (sequence, v-head), 256 threads.  The 128 v-rows of the state
-// sit on the 128 TMEM lanes: thread (quad q = warp % 4, lane l, half h =
-// warp / 4) owns row v = 32 q + l and column half h of every [v x 64] tile
-// (k-half h of the state).
+// One CTA per (sequence, v-head), 256 threads, two CTAs per SM.  The 128
+// v-rows of the state sit on the 128 TMEM lanes: thread (quad q = warp % 4,
+// lane l, half h = warp / 4) owns row v = 32 q + l and column half h of every
+// [v x 64] tile (k-half h of the state, or token half h of a chunk).
 //   S      fp32 S[v][k] in registers (64 k per thread)
-//   TMEM   cols [0, 64)    bf16(S): A operand of MMA 1 (two bf16 per column);
-//                          then V_new, then bf16 V_dec (A operand of MMA 3)
-//          cols [64, 128)  O_intra = X PA^T
-//          cols [128, 256) Yq | Yk, then Yq | bf16 X (A operand of MMA 2), then dS
-// Every A operand is read from TMEM (the TS form), so no intermediate goes
-// through shared memory; B operands (Q, K, [PA;Ainv]) are in shared memory.
-// Per chunk (t = token of the chunk, L valid tokens):
-//   MMA 1   Yq = S Q^T, Yk = S K^T                    M=128, N=64+64, K=128
+//   TMEM   cols [0, 64)    bf16(S): A operand of MMA 1; then V_new, then
+//                          bf16 V_dec (A operand of MMA 3)
+//          cols [64, 128)  O: e^G Yq = S Q~^T (MMA 1), + bf16(V_new) P^T
+//          cols [128, 256) Yk (MMA 1), then bf16 X (A operand of MMA 2) and
+//                          bf16 V_new (A operand of the output MMA); then dS
+// Every A operand is read from TMEM (the TS form); B operands (Q~ and K, the
+// [P ; Ainv] image) are in shared memory.  Per chunk (t = token of the
+// chunk, L valid tokens, G the within-chunk cumulative gate):
+//   MMA 1   [e^G Yq | Yk] = S [Q~ ; K]^T, Q~ = e^G Q   M=128, N=128, K=128
 //           X[v][t] = beta_t (V[t][v] - e^{G_t} Yk[v][t])
-//   MMA 2   O_intra = X PA^T,  V_new = X Ainv^T       M=128, N=64+64, K=64
-//           out[t][v] = scale (e^{G_t} Yq[v][t] + O_intra[v][t]);
+//   MMA 2   V_new = X Ainv^T                          M=128, N=64..16, K=64
 //           V_dec[v][t] = e^{G_last - G_t} V_new[v][t]
+//   output  O += bf16(V_new) P^T;  out[t][v] = scale O[v][t]
 //   MMA 3   dS = V_dec K                               M=128, N=128,   K=64
 //           S = e^{G_last} S + dS,  bf16(S) -> TMEM
-// Operands arrive by TMA (Q and K tiles with 128-byte swizzle, V tile plain)
-// and a bulk copy (the [PA;Ainv] image), each on its own mbarrier, issued as
-// soon as its buffer is free: Q after MMA 1, V after X, [PA;Ainv] after
-// MMA 2, K two chunks ahead (double buffered).
+// Thread 0 issues the MMAs; lane 0 of warp 1 the copies; warps 2 and 3 turn
+// the gates into per-token factors.  Operands arrive by TMA (Q and K tiles,
+// 128-byte swizzle, double buffered and loaded two chunks ahead, on one
+// mbarrier per buffer; the V tile plain) and a bulk copy (the image), each
+// issued as soon as its buffer is free.  Q~ of chunk c + 1 is formed in
+// place while MMA 3 of chunk c runs, so that MMA 1 finds it ready.
 constexpr int kScanThreads = 256;
+constexpr int kCopyThread = 32;  // lane 0 of warp 1
 
 struct ScanSmem {
-  static constexpr int kQ = 0;         // Q tile: 2 d-blocks x 64 t x 128 B, 128-byte swizzle
-  static constexpr int kK0 = 16384;    // K tiles, same layout, double buffered
-  static constexpr int kK1 = 32768;
-  static constexpr int kM2 = 49152;    // [P ; Ainv] image, 128 rows x 128 B
-  static constexpr int kV = 65536;     // V tile: 64 t rows x 128 v bf16, unswizzled (16 KB)
+  // Q and K tiles of a chunk, double buffered: [Q.d0 | K.d0 | Q.d1 | K.d1],
+  // each 64 t rows x 128 B (64 bf16 of d), 128-byte swizzle.  Rows 0..63 of
+  // [Q.db ; K.db] are the 128 N rows of MMA 1's B operand for d-block db.
+  static constexpr int kQK0 = 0;
+  static constexpr int kQK1 = 32768;
+  static constexpr int kM2 = 65536;    // [P ; Ainv] image (the backward's full one: 16 KB)
+  // V tile: 2 v-blocks x 64 t rows x 128 B, 128-byte swizzle (the MN-major
+  // A operand of the V MMA)
+  static constexpr int kV = 81920;
   // per-token gate factors of the current / next chunk, computed once per
   // chunk: e^{G_t}, beta_t, e^{G_last - G_t} (0 past the end), e^{G_last}
-  static constexpr int kG = 81920;     // float eG[2][64]
-  static constexpr int kB = kG + 512;  // float beta[2][64]
-  static constexpr int kDec = kB + 512;  // float eDec[2][64]
-  static constexpr int kEn = kDec + 512;  // float -eG[2][64] (the X phase's fused multiply-add)
-  static constexpr int kGl = kEn + 512;  // float eGlast[2]
-  static constexpr int kBar = kGl + 16;
-  static constexpr int kBarMma = kBar, kBarQ = kBar + 8, kBarV = kBar + 16, kBarM2 = kBar + 24,
-                       kBarK0 = kBar + 32;  // kBarK1 = kBarK0 + 8
-  static constexpr int kTmem = kBar + 48;
-  static constexpr int kBroken = kBar + 52;
-  static constexpr int kBarO = kBar + 56;  // the output MMA (O += bf16(V_new) P^T)
-  static constexpr int kBytes = kBar + 64 + 1024;  // + base alignment slack
+  // (three chunks' worth: the current one, and the next two, whose factors
+  // are stored a chunk ahead so that Q~ of the next chunk can be formed at
+  // the start of this one)
+  static constexpr int kG = 98304;     // float eG[3][64]
+  static constexpr int kB = kG + 768;  // float beta[3][64]
+  static constexpr int kDec = kB + 768;  // float eDec[3][64]
+  static constexpr int kEn = kDec + 768;  // float -eG[3][64] (the X phase's fused multiply-add)
+  static constexpr int kGl = kEn + 768;  // float eGlast[3]
+  // 16 x 16 bf16 identity, no-swizzle K-major (B operand of the V MMA)
+  static constexpr int kI = kGl + 16;
+  static constexpr int kBar = kI + 512;
+  static constexpr int kBarMma = kBar, kBarV = kBar + 8, kBarM2 = kBar + 16,
+                       kBarK0 = kBar + 24,  // K tile of buffer b: kBarK0 + 8 b
+                       kBarQ0 = kBar + 40;  // Q tile of buffer b: kBarQ0 + 8 b
+  static constexpr int kBarO = kBar + 56;   // the output MMA (O += bf16(V_new) P^T)
+  static constexpr int kTmem = kBar + 64;
+  static constexpr int kBroken = kBar + 68;
+  static constexpr int kBytes = kBar + 72 + 1024;  // + base alignment slack
   static constexpr uint32_t kTmemCols = 256;
   // kColO: e^G Yq = S Q~^T (MMA 1), then + bf16(V_new) P^T (the output MMA):
-  // scale * that is the output.  kColY: Yk (MMA 1), then dS (MMA 3, 128
-  // columns).
+  // scale * that is the output.  kColY: Yk (MMA 1, the 64 columns right after
+  // kColO, as MMA 1's N = 128 result), then dS (MMA 3, 128 columns).
   static constexpr uint32_t kColSb = 0, kColO = 64, kColY = 128, kColYk = kColY;
   // bf16 operand images read from TMEM: X over the Yk columns (thread half
   // hc: columns kColX + 32 hc .. + 15, two tokens per column; MMA 2), then
   // bf16(V_new) in the same columns (the output MMA); V_new and then V_dec
   // (MMA 3) over the bf16(S) columns
   static constexpr uint32_t kColX = kColYk, kColVnb = kColX, kColVn = kColSb;
+  // V[t][v] in fp32 (the V MMA), read by the X phase; free until MMA 3's dS
+  static constexpr uint32_t kColV = 192;
 };
-// the epilogue stages one 64 KB (n, hv) state over the Q, K and [PA;Ainv] tiles
-static_assert(ScanSmem::kQ == 0 && ScanSmem::kV >= 65536, "state staging region");
+// the epilogue stages one 64 KB (n, hv) state over the two Q/K tile buffers
+static_assert(ScanSmem::kQK0 == 0 && ScanSmem::kQK1 + 32768 <= ScanSmem::kM2, "state staging region");
+static_assert(ScanSmem::kColO + 64 == ScanSmem::kColYk, "MMA 1 writes [e^G Yq | Yk] in one pass");
+static_assert(2 * ScanSmem::kBytes <= 227 * 1024, "two CTAs per SM");
 
 // kSave = true is the backward pass's recompute: FULL items only, no outputs
 // and no final state; instead the state at the start of every chunk goes to
@@ -1081,7 +1099,6 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   else if (mode == kItemIdent)
     fin = seg_state(seg_phi, seg);
 
-  const uint16_t *vt = reinterpret_cast<const uint16_t *>(smem + SM::kV);
   float *Eg = reinterpret_cast<float *>(smem + SM::kG);
   float *Bs = reinterpret_cast<float *>(smem + SM::kB);
   float *Ed = reinterpret_cast<float *>(smem + SM::kDec);
@@ -1089,26 +1106,37 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   float *Egl = reinterpret_cast<float *>(smem + SM::kGl);
   volatile int *broken = reinterpret_cast<volatile int *>(smem + SM::kBroken);
   const uint32_t s_base = smem_u32(smem);
-  const uint32_t bar_mma = s_base + SM::kBarMma, bar_q = s_base + SM::kBarQ,
-                 bar_v = s_base + SM::kBarV, bar_m2 = s_base + SM::kBarM2,
-                 bar_k0 = s_base + SM::kBarK0, bar_o = s_base + SM::kBarO;
+  const uint32_t bar_mma = s_base + SM::kBarMma, bar_v = s_base + SM::kBarV,
+                 bar_m2 = s_base + SM::kBarM2, bar_k0 = s_base + SM::kBarK0,
+                 bar_q0 = s_base + SM::kBarQ0, bar_o = s_base + SM::kBarO;
 
   // Items without outputs (ZERO, IDENT) need neither Q nor the Q-side MMAs;
   // IDENT treats V as zero and needs no V either.
   const bool need_q = write_out && !kSave;
   const bool need_v = !ident;
 
-  // Chunk operand loads, all issued by thread 0.
-  auto issue_qk = [&](bool is_k, int c, uint32_t dst, uint32_t bar) {
+  // Chunk operand loads: the first ones by thread 0 at the start, then each
+  // next one by lane 0 of warp 1 (kCopyThread) as soon as its buffer is free,
+  // so that thread 0, which issues every MMA, has no copies to issue.  Each
+  // barrier still has one re-arming thread, and only the waits that happen
+  // before its re-arm poll it.
+  // The Q (where outputs are formed) or the K tile of chunk c into tile
+  // buffer b, each on its own barrier: a buffer's Q half is free once MMA 1
+  // has run, its K half only after MMA 3.
+  auto issue_tile = [&](bool is_k, int c, int b) {
     const int y = static_cast<int>(bos + static_cast<int64_t>(c) * kChunk);
-    mbar_arrive_expect_tx(bar, 16384);
+    const uint32_t dst = s_base + (b ? SM::kQK1 : SM::kQK0) + (is_k ? 8192 : 0);
+    const uint32_t bar = (is_k ? bar_k0 : bar_q0) + 8 * b;
     const void *tm = is_k ? static_cast<const void *>(&tmap_k) : static_cast<const void *>(&tmap_q);
+    mbar_arrive_expect_tx(bar, 16384u);
     tma_load_2d(dst, tm, hqk * kD, y, bar);
-    tma_load_2d(dst + 8192, tm, hqk * kD + 64, y, bar);
+    tma_load_2d(dst + 16384, tm, hqk * kD + 64, y, bar);
   };
   auto issue_v = [&](int c) {
+    const int y = static_cast<int>(bos + static_cast<int64_t>(c) * kChunk);
     mbar_arrive_expect_tx(bar_v, 16384);
-    tma_load_2d(s_base + SM::kV, &tmap_v, hv * kD, static_cast<int>(bos + static_cast<int64_t>(c) * kChunk), bar_v);
+    tma_load_2d(s_base + SM::kV, &tmap_v, hv * kD, y, bar_v);
+    tma_load_2d(s_base + SM::kV + 8192, &tmap_v, hv * kD + 64, y, bar_v);
   };
   // the backward's recompute reads the full [PA ; Ainv] image, the forward
   // the compact [P ; Ainv] one
@@ -1118,8 +1146,12 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     bulk_load(s_base + SM::kM2, m2_ws + (static_cast<int64_t>(gbase + c) * kHV + hv) * kImgBytes,
               kImgBytes, bar_m2);
   };
-  // Gates of chunk c for token `tid` (threads 0..63): fetched into registers
-  // a chunk ahead, turned into the per-token factors when the buffer is free.
+  // Gates of chunk c for token gt = tid - 64 (threads 64..127, warps 2 and 3:
+  // thread 0, which issues the MMAs and copies, has no part in them): fetched
+  // into registers a chunk ahead, turned into the per-token factors when the
+  // buffer is free.
+  const int gt = tid - 64;
+  const bool gate_thread = static_cast<unsigned>(gt) < 64u;
   struct GateRegs {
     float g, g_last, beta;
     bool valid;
@@ -1130,24 +1162,51 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
     const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
     GateRegs r;
-    r.valid = tid < L;
+    r.valid = gt < L;
     r.g_last = gcum_ws[(t0 + L - 1) * kHV + hv];
     r.g = 0.f;
     r.beta = 0.f;
     if (r.valid) {
-      r.g = gcum_ws[(t0 + tid) * kHV + hv];
-      r.beta = beta_ws[(t0 + tid) * kHV + hv];
+      r.g = gcum_ws[(t0 + gt) * kHV + hv];
+      r.beta = beta_ws[(t0 + gt) * kHV + hv];
     }
     return r;
   };
   auto store_gates = [&](const GateRegs &r, int buf) {
     const float g = r.valid ? r.g : r.g_last;
     const float eg = expf(g);
-    Eg[buf * 64 + tid] = eg;
-    En[buf * 64 + tid] = -eg;
-    Bs[buf * 64 + tid] = r.beta;
-    Ed[buf * 64 + tid] = r.valid ? expf(r.g_last - g) : 0.f;
-    if (tid == 0) Egl[buf] = expf(r.g_last);
+    Eg[buf * 64 + gt] = eg;
+    En[buf * 64 + gt] = -eg;
+    Bs[buf * 64 + gt] = r.beta;
+    Ed[buf * 64 + gt] = r.valid ? expf(r.g_last - g) : 0.f;
+    if (gt == 0) Egl[buf] = expf(r.g_last);
+  };
+  // Q~ = e^{G_t} Q in place in tile buffer b with the factors of gate buffer
+  // gb: row t of both d-blocks times e^{G_t}, the tile's 1,024 16-byte pieces
+  // spread over nt threads (this one is number ti; a piece lies in one row,
+  // the swizzle only permutes pieces within a row), on packed pairs.  The
+  // caller waits for the tile first and fences (async proxy) and
+  // synchronises before MMA 1 reads it.
+  auto scale_q = [&](int b, int gb, int ti, int nt) {
+    uint8_t *qt = smem + (b ? SM::kQK1 : SM::kQK0);
+#pragma unroll
+    for (int m = 0; m < 5; ++m) {  // nt >= 224 threads: at most 5 pieces each
+      const int piece = ti + nt * m;
+      if (piece >= 1024) break;
+      const int db = piece >> 9, t = (piece >> 3) & 63;
+      uint4 *ptr = reinterpret_cast<uint4 *>(qt + db * 16384 + t * 128 + (piece & 7) * 16);
+      const uint4 w = *ptr;
+      const float e = Eg[gb * 64 + t];
+      const uint64_t ee = f2_pack(e, e);
+      const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint64_t r = f2_mul(f2_pack(bf16_lo(in[h]), bf16_hi(in[h])), ee);
+        o[h] = pack_bf16x2(f2_lo(r), f2_hi(r));
+      }
+      *ptr = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   };
 
   // Barriers first, then the first chunk's operand loads and gates, so their
@@ -1155,19 +1214,22 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   if (warp == 0) tmem_alloc(s_base + SM::kTmem, SM::kTmemCols);
   if (tid == 0) {
     *broken = 0;
-    for (int i = 0; i < 6; ++i) mbar_init(bar_mma + 8 * i, 1);
-    mbar_init(bar_o, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(bar_mma + 8 * i, 1);  // mma, v, m2, k0/1, q0/1, o
     mbar_init_fence();
     if (nchunks > 0) {
-      if (need_q) issue_qk(false, 0, s_base + SM::kQ, bar_q);
-      issue_qk(true, 0, s_base + SM::kK0, bar_k0);
-      if (nchunks > 1) issue_qk(true, 1, s_base + SM::kK1, bar_k0 + 8);
+      if (need_q) issue_tile(false, 0, 0);
+      issue_tile(true, 0, 0);
+      if (nchunks > 1) {
+        if (need_q) issue_tile(false, 1, 1);
+        issue_tile(true, 1, 1);
+      }
       if (need_v) issue_v(0);
       issue_m2(0);
     }
   }
-  GateRegs gates0;
-  if (tid < 64 && nchunks > 0) gates0 = fetch_gates(0);
+  GateRegs gates0, gates1;
+  if (gate_thread && nchunks > 0) gates0 = fetch_gates(0);
+  if (gate_thread && nchunks > 1) gates1 = fetch_gates(1);
 
   // fp32 state row slice S[v][64 hc .. 64 hc + 63].
   float s[64];
@@ -1184,7 +1246,16 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
     for (int i = 0; i < 64; ++i) s[i] = (ident && vrow == 64 * hc + i) ? 1.f : 0.f;
   }
-  __syncthreads();  // barriers initialised, TMEM address published
+  if (tid < 32) {
+    // the 16 x 16 identity: row r, K half kh (columns 8 kh .. 8 kh + 7) is
+    // the core-matrix row at (r / 8) * 256 + kh * 128 + (r % 8) * 16
+    const int r = tid >> 1, kh = tid & 1, wi = (r >> 3) == kh ? (r & 7) >> 1 : -1;
+    const uint32_t one = (r & 1) ? 0x3F800000u : 0x00003F80u;  // bf16 1.0 in word wi
+    *reinterpret_cast<uint4 *>(smem + SM::kI + (r >> 3) * 256 + kh * 128 + (r & 7) * 16) =
+        make_uint4(wi == 0 ? one : 0u, wi == 1 ? one : 0u, wi == 2 ? one : 0u, wi == 3 ? one : 0u);
+    fence_async_smem();
+  }
+  __syncthreads();  // barriers initialised, TMEM address published, identity written
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + SM::kTmem);
   const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * quad) << 16);
@@ -1194,16 +1265,28 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     for (int j = 0; j < 32; ++j) pk[j] = pack_bf16x2(s[2 * j], s[2 * j + 1]);
     tmem_st32(tlane + SM::kColSb + 32 * hc, pk);
   }
-  if (tid < 64 && nchunks > 0) store_gates(gates0, 0);
+  if (gate_thread && nchunks > 0) store_gates(gates0, 0);
+  if (gate_thread && nchunks > 1) store_gates(gates1, 1);
   tmem_wait_st();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Q~ of the first chunk (every later one is formed a chunk ahead)
+  uint32_t ph_q = 0;  // bit b = parity of Q barrier b
+  if (need_q && nchunks > 0) {
+    wait_phase(bar_q0, 0, broken);
+    ph_q ^= 1u;
+    scale_q(0, 0, tid, kScanThreads);
+    fence_async_smem();
+    __syncthreads();
+  }
 
   const uint32_t idesc_n64 = umma_idesc_bf16(128, 64, false, false);
+  const uint32_t idesc_n128 = umma_idesc_bf16(128, 128, false, false);
+  const uint32_t idesc_v = umma_idesc_bf16(128, 16, true, false);  // A MN-major
   const uint32_t idesc_ds = umma_idesc_bf16(128, 128, false, true);
-  uint32_t ph_mma = 0, ph_q = 0, ph_v = 0, ph_m2 = 0, ph_o = 0;
-  uint32_t ph_k = 0;  // bit b = parity of K buffer b
+  uint32_t ph_mma = 0, ph_v = 0, ph_m2 = 0, ph_o = 0;
+  uint32_t ph_k = 0;  // bit b = parity of tile buffer b
 
   // The chunk loop, instantiated twice: with outputs (FULL, HEAD, MID, TAIL)
   // and state only (ZERO, IDENT).  Compile-time flags keep the loop free of
@@ -1211,122 +1294,136 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
   auto chunk_loop = [&](auto out_tag) {
     constexpr bool kOut = decltype(out_tag)::value;
     for (int c = 0; c < nchunks; ++c) {
-      const int cb = c & 1;
+      const int cb = c & 1, gs = c % 3;
       const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
       const int L = static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk));
-      const uint32_t kbuf = s_base + (cb ? SM::kK1 : SM::kK0);
+      const uint32_t kbuf = s_base + (cb ? SM::kQK1 : SM::kQK0);
       const uint32_t bar_k = bar_k0 + 8 * cb;
+      // gate buffers rotate over three chunks: gs (this chunk), gs1 (next),
+      // gs2 (the one after, fetched now and stored before the V barrier)
+      const int gs1 = gs == 2 ? 0 : gs + 1, gs2 = gs1 == 2 ? 0 : gs1 + 1;
       GateRegs next_gates;
-      if (tid < 64 && c + 1 < nchunks) next_gates = fetch_gates(c + 1);
+      if (gate_thread && c + 2 < nchunks) next_gates = fetch_gates(c + 2);
       if constexpr (kSave)
         put_state_img_row(save_states + (static_cast<int64_t>(gbase + c) * kHV + hv) * kStateImgBytes,
                           vrow, hc, s);
 
-      // Q, K and [PA;Ainv] are read only by the tensor core, so only the MMA
-      // thread waits for them: thread 0 re-arms each barrier for the next chunk
-      // right after the MMA that consumed it, and a thread still polling the
-      // old phase could otherwise see two completions and wait forever.  The
-      // one exception is the tail chunk (always the last, so never re-armed):
+      // The tiles and the image are read only by the tensor core, so only the
+      // MMA thread waits for them here: the copy thread re-arms each barrier
+      // for a later chunk right after the MMA that consumed it, and a thread
+      // still polling the old phase could otherwise see two completions and
+      // wait forever.  (Every thread already waited for this buffer's tiles
+      // before forming Q~, a chunk earlier, long before that re-arm.)  The
+      // tail chunk (always the last, so never re-armed) is the exception:
       // every thread must see its tiles landed before zeroing rows.
       const bool tail = L < kChunk;
-      if (tid == 0 || tail) {
-        wait_phase(bar_k, (ph_k >> cb) & 1, broken);
-        if (tail && kOut) wait_phase(bar_q, ph_q, broken);
-      }
+      if (tid == 0 || tail) wait_phase(bar_k, (ph_k >> cb) & 1, broken);
+      if (tail && (kOut || need_v)) wait_phase(bar_v, ph_v, broken);
       ph_k ^= 1u << cb;
       if (tail) {
         // tail chunk: zero the rows past the sequence end (TMA brought in the
-        // next sequence's tokens there)
+        // next sequence's tokens there; Q~ rows included), and the V rows, so
+        // that nothing of the next sequence reaches this one's state (a row
+        // of the swizzled tiles keeps its 8 pieces: zero them all)
         for (int idx = tid; idx < 2 * 2 * (kChunk - L) * 8; idx += kScanThreads) {
           const int ch = idx & 7, r = L + ((idx >> 3) % (kChunk - L)), blk = (idx >> 3) / (kChunk - L);
-          const int which = blk >> 1, dblk = blk & 1;
-          uint8_t *tile = smem + (which ? (cb ? SM::kK1 : SM::kK0) : SM::kQ);
-          *reinterpret_cast<uint4 *>(tile + dblk * 8192 + r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+          const int which = blk >> 1, dblk = blk & 1;  // which: 0 Q, 1 K
+          *reinterpret_cast<uint4 *>(smem + (cb ? SM::kQK1 : SM::kQK0) + dblk * 16384 + which * 8192 +
+                                     r * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+        }
+        if (kOut || need_v) {
+          for (int idx = tid; idx < 2 * (kChunk - L) * 8; idx += kScanThreads) {
+            const int ch = idx & 7, r = L + ((idx >> 3) % (kChunk - L)), vb = (idx >> 3) / (kChunk - L);
+            *reinterpret_cast<uint4 *>(smem + SM::kV + vb * 8192 + r * 128 + ch * 16) =
+                make_uint4(0, 0, 0, 0);
+          }
         }
         fence_async_smem();
         __syncthreads();
       }
 
-      // ---- MMA 1: Yk = S K^T (committed: X needs it); then, with the Q tile
-      // scaled in place to Q~ = e^G Q while Yk computes, e^G Yq = S Q~^T into
-      // the output columns (read only after MMA 2, whose commit covers it) ----
+      // ---- MMA 1: [e^G Yq | Yk] = S [Q~ ; K]^T with outputs (B = the two
+      // 64-row tiles of d-block db, adjacent: N = 128), Yk = S K^T without ----
       if (tid == 0) {
         tc_fence_after();
+        if constexpr (kOut) {
+          const uint64_t dqk = umma_desc_sw128(kbuf, 16, 1024);
   #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
-          umma_bf16_ts(tmem + SM::kColYk, tmem + SM::kColSb + 8 * ks,
-                       umma_desc_sw128(kbuf + boff, 16, 1024), idesc_n64, ks > 0);
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t boff = (ks >> 2) * 16384 + (ks & 3) * 32;
+            umma_bf16_ts(tmem + SM::kColO, tmem + SM::kColSb + 8 * ks, umma_desc_advance(dqk, boff),
+                         idesc_n128, ks > 0);
+          }
+        } else {
+          const uint64_t dk = umma_desc_sw128(kbuf + 8192, 16, 1024);
+  #pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t boff = (ks >> 2) * 16384 + (ks & 3) * 32;
+            umma_bf16_ts(tmem + SM::kColYk, tmem + SM::kColSb + 8 * ks, umma_desc_advance(dk, boff),
+                         idesc_n64, ks > 0);
+          }
+        }
+        if (kOut || need_v) {
+          // ---- V MMA: V[t][v] in fp32 (exact) into kColV, for the X phase:
+          // A = the V tile (MN-major, v = M), B = the 16 x 16 identity;
+          // K-step ks gives tokens 16 ks .. 16 ks + 15 (N = 16) ----
+          wait_phase(bar_v, ph_v, broken);
+          tc_fence_after();
+          const uint64_t dv = umma_desc_sw128(s_base + SM::kV, 8192, 1024);
+          const uint64_t di = umma_desc_noswz(s_base + SM::kI, 128, 256);
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16(tmem + SM::kColV + 16 * ks, umma_desc_advance(dv, ks * 2048), di, idesc_v, 0);
         }
         umma_commit(bar_mma);
       }
       if constexpr (kOut) {
-        // every thread waits for the Q tile here (thread 0 re-arms its barrier
-        // only after MMA 2, which all threads reach after the barrier below)
-        if (!tail) wait_phase(bar_q, ph_q, broken);
-        // row t of both 64-column blocks times e^{G_t}: 4 of the tile's 1,024
-        // 16-byte pieces per thread (a piece lies in one row; the swizzle only
-        // permutes pieces within a row), on packed pairs
-  #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const int piece = tid + kScanThreads * m;
-          const int db = piece >> 9, t = (piece >> 3) & 63;
-          uint4 *ptr = reinterpret_cast<uint4 *>(smem + SM::kQ + db * 8192 + t * 128 + (piece & 7) * 16);
-          const uint4 w = *ptr;
-          const float e = Eg[cb * 64 + t];
-          const uint64_t ee = f2_pack(e, e);
-          const uint32_t in[4] = {w.x, w.y, w.z, w.w};
-          uint32_t o[4];
-  #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const uint64_t r = f2_mul(f2_pack(bf16_lo(in[h]), bf16_hi(in[h])), ee);
-            o[h] = pack_bf16x2(f2_lo(r), f2_hi(r));
+        // ---- Q~ of the next chunk, in the other tile buffer, by warps 1..7
+        // while thread 0 issues MMA 1 (the factors were stored a chunk ago;
+        // the X barrier below orders the writes before MMA 1 of the next
+        // chunk) ----
+        if (c + 1 < nchunks) {
+          if (warp != 0) {
+            wait_phase(bar_q0 + 8 * (cb ^ 1), (ph_q >> (cb ^ 1)) & 1, broken);
+            scale_q(cb ^ 1, gs1, tid - 32, kScanThreads - 32);
+            fence_async_smem();
           }
-          *ptr = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-          tc_fence_after();
-  #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
-            umma_bf16_ts(tmem + SM::kColO, tmem + SM::kColSb + 8 * ks,
-                         umma_desc_sw128(s_base + SM::kQ + boff, 16, 1024), idesc_n64, ks > 0);
-          }
+          ph_q ^= 1u << (cb ^ 1);
         }
       }
-      ph_q ^= 1;
       wait_phase(bar_mma, ph_mma, broken);
       ph_mma ^= 1;
       tc_fence_after();
-      if (kOut || need_v) {
-        wait_phase(bar_v, ph_v, broken);
-        ph_v ^= 1;
-      }
+      // MMA 1 has read Q~ of this chunk: the Q tile two chunks ahead can come
+      if (kOut && tid == kCopyThread && c + 2 < nchunks) issue_tile(false, c + 2, cb);
+      if (kOut || need_v) ph_v ^= 1;
 
       // ---- X = beta (V - e^G Yk) -> TMEM ----
   #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const int tb = 32 * hc + 16 * p;
-        float yk[16];
+        float yk[16], vv[16];
         tmem_ld16(tlane + SM::kColYk + tb, yk);
+        if (kOut || need_v) {
+          tmem_ld16(tlane + SM::kColV + tb, vv);
+        } else {
+  #pragma unroll
+          for (int j = 0; j < 16; ++j) vv[j] = 0.f;  // IDENT: V is zero
+        }
         tmem_wait_ld();
   #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          // packed pairs (f32x2): x = beta * fma(-e^G, y, v), as the scalar form
-          const float4 en4 = *reinterpret_cast<const float4 *>(En + cb * 64 + tb + 4 * g);
-          const float4 bt4 = *reinterpret_cast<const float4 *>(Bs + cb * 64 + tb + 4 * g);
+          // packed pairs (f32x2): x = beta * fma(-e^G, y, v), as the scalar
+          // form; past the sequence end beta = 0 (and the V rows are zero)
+          const float4 en4 = *reinterpret_cast<const float4 *>(En + gs * 64 + tb + 4 * g);
+          const float4 bt4 = *reinterpret_cast<const float4 *>(Bs + gs * 64 + tb + 4 * g);
           const uint64_t en2[2] = {f2_pack(en4.x, en4.y), f2_pack(en4.z, en4.w)};
           const uint64_t bt2[2] = {f2_pack(bt4.x, bt4.y), f2_pack(bt4.z, bt4.w)};
   #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int j = 4 * g + 2 * h, t = tb + j;
-            const float v0 = (t < L && (kOut || !ident)) ? bf16_to_f32(vt[t * kD + vrow]) : 0.f;
-            const float v1 =
-                (t + 1 < L && (kOut || !ident)) ? bf16_to_f32(vt[(t + 1) * kD + vrow]) : 0.f;
+            const int j = 4 * g + 2 * h;
             const uint64_t x =
-                f2_mul(bt2[h], f2_fma(en2[h], f2_pack(yk[j], yk[j + 1]), f2_pack(v0, v1)));
+                f2_mul(bt2[h], f2_fma(en2[h], f2_pack(yk[j], yk[j + 1]), f2_pack(vv[j], vv[j + 1])));
             yk[j] = f2_lo(x);
             yk[j + 1] = f2_hi(x);
           }
@@ -1341,7 +1438,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
-      if (tid == 0 && (kOut || need_v) && c + 1 < nchunks) issue_v(c + 1);
+      if (tid == kCopyThread && (kOut || need_v) && c + 1 < nchunks) issue_v(c + 1);
 
       // ---- MMA 2: V_new = X Ainv^T ----
       const uint32_t m2buf = s_base + SM::kM2;
@@ -1349,17 +1446,19 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         wait_phase(bar_m2, ph_m2, broken);
         tc_fence_after();
         if constexpr (kSave) {
+          const uint64_t da = umma_desc_sw128(m2buf + 8192, 16, 1024);
   #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             umma_bf16_ts(tmem + SM::kColVn, tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
-                         umma_desc_sw128(m2buf + 8192 + ks * 32, 16, 1024), idesc_n64, ks > 0);
+                         umma_desc_advance(da, ks * 32), idesc_n64, ks > 0);
         } else {
           // K-step ks only reaches tokens t >= 16 ks (N = 64 - 16 ks)
+          const uint64_t da = umma_desc_noswz(m2buf + kTriBytes, kTriLbo, kTriSbo);
   #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             umma_bf16_ts(tmem + SM::kColVn + 16 * ks,
                          tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
-                         umma_desc_noswz(m2buf + kTriBytes + tri_step_off(ks), kTriLbo, kTriSbo),
+                         umma_desc_advance(da, tri_step_off(ks)),
                          umma_idesc_bf16(128, 64 - 16 * ks, false, false), ks > 0);
         }
         umma_commit(bar_mma);
@@ -1368,12 +1467,13 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       wait_phase(bar_mma, ph_mma, broken);
       ph_mma ^= 1;
       tc_fence_after();
-      if (tid == 0 && c + 1 < nchunks) {
-        // the output MMA still reads this chunk's P rows: with outputs the next
-        // image is issued once that MMA has completed
-        if constexpr (!kOut) issue_m2(c + 1);
-        if constexpr (kOut) issue_qk(false, c + 1, s_base + SM::kQ, bar_q);  // MMA 1's Q reads are done too
-      }
+      // the output MMA still reads this chunk's P rows: with outputs the next
+      // image is issued once that MMA has completed
+      if (!kOut && tid == kCopyThread && c + 1 < nchunks) issue_m2(c + 1);
+      // the gate factors of chunk c + 2 (their buffer's last reader was the
+      // previous chunk), visible to all after the barrier below: Q~ of chunk
+      // c + 2 is formed with them at the start of the next chunk
+      if (gate_thread && c + 2 < nchunks) store_gates(next_gates, gs2);
 
       // ---- V_dec (the outputs wait until MMA 3 runs) ----
   #pragma unroll
@@ -1401,7 +1501,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         }
   #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          const float4 ed4 = *reinterpret_cast<const float4 *>(Ed + cb * 64 + tb + 4 * g);
+          const float4 ed4 = *reinterpret_cast<const float4 *>(Ed + gs * 64 + tb + 4 * g);
           const uint64_t a = f2_mul(f2_pack(zv[4 * g], zv[4 * g + 1]), f2_pack(ed4.x, ed4.y));
           const uint64_t b = f2_mul(f2_pack(zv[4 * g + 2], zv[4 * g + 3]), f2_pack(ed4.z, ed4.w));
           pk[2 * g] = pack_bf16x2(f2_lo(a), f2_hi(a));
@@ -1418,21 +1518,24 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       // overwrites its A operand), then MMA 3: dS = V_dec K ----
       if (tid == 0) {
         if constexpr (kOut) {
+          const uint64_t dp = umma_desc_noswz(m2buf, kTriLbo, kTriSbo);
   #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             umma_bf16_ts(tmem + SM::kColO + 16 * ks,
                          tmem + SM::kColVnb + 32 * (ks >> 1) + 8 * (ks & 1),
-                         umma_desc_noswz(m2buf + tri_step_off(ks), kTriLbo, kTriSbo),
+                         umma_desc_advance(dp, tri_step_off(ks)),
                          umma_idesc_bf16(128, 64 - 16 * ks, false, false), 1);
           umma_commit(bar_o);
         }
+        // B = K MN-major (rows = K index t): the two 64-wide k blocks K.d0,
+        // K.d1 are 16 KB apart
+        const uint64_t dkm = umma_desc_sw128(kbuf + 8192, 16384, 1024);
   #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
           umma_bf16_ts(tmem + SM::kColY, tmem + SM::kColVn + 32 * (ks >> 1) + 8 * (ks & 1),
-                       umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), idesc_ds, ks > 0);
+                       umma_desc_advance(dkm, ks * 2048), idesc_ds, ks > 0);
         umma_commit(bar_mma);
       }
-      if (tid < 64 && c + 1 < nchunks) store_gates(next_gates, cb ^ 1);
       if constexpr (kOut) {
         // ---- outputs O = scale (e^G Yq + bf16(V_new) P^T), while MMA 3 runs
         // (it writes columns kColY.., these are kColO..); then this chunk's
@@ -1440,7 +1543,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         wait_phase(bar_o, ph_o, broken);
         ph_o ^= 1;
         tc_fence_after();
-        if (tid == 0 && c + 1 < nchunks) issue_m2(c + 1);
+        if (tid == kCopyThread && c + 1 < nchunks) issue_m2(c + 1);
         const uint64_t sc2 = f2_pack(scale, scale);
   #pragma unroll
         for (int p = 0; p < 2; ++p) {
@@ -1464,11 +1567,12 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       wait_phase(bar_mma, ph_mma, broken);
       ph_mma ^= 1;
       tc_fence_after();
-      if (tid == 0 && c + 2 < nchunks) issue_qk(true, c + 2, kbuf, bar_k);
+      // MMA 3 is done with this chunk's K tile
+      if (tid == kCopyThread && c + 2 < nchunks) issue_tile(true, c + 2, cb);
 
       // ---- S = e^{G_last} S + dS ;  bf16(S) -> TMEM ----
       {
-        const float eg_last = Egl[cb];
+        const float eg_last = Egl[gs];
   #pragma unroll
         for (int p = 0; p < 2; ++p) {
           float ds[32];
@@ -1509,10 +1613,10 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // shared memory so that each warp store covers 512 contiguous bytes (one
     // state row) rather than 16 bytes of 32 rows: the same bytes, but whole
     // lines, which is what matters when `fin` is another GPU's memory and
-    // every store crosses NVLink as its own request.  The Q/K/[PA;Ainv] tiles
-    // (first 64 KB) are free: every MMA and TMA load has completed.  Chunk c
+    // every store crosses NVLink as its own request.  The two Q/K tile
+    // buffers (first 64 KB) are free: every MMA and TMA load has completed.  Chunk c
     // of row r is kept at c ^ (r & 7), conflict-free on both sides.
-    float4 *stage = reinterpret_cast<float4 *>(smem + SM::kQ);
+    float4 *stage = reinterpret_cast<float4 *>(smem + SM::kQK0);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int c = 16 * hc + i;
@@ -1722,7 +1826,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   if (T > 0) {
     if (!make_tmap_2d(&tq, q, kHQK * kD, T, 64, 64, true) ||
         !make_tmap_2d(&tk, k, kHQK * kD, T, 64, 64, true) ||
-        !make_tmap_2d(&tv, v, kHV * kD, T, kD, 64, false))
+        !make_tmap_2d(&tv, v, kHV * kD, T, 64, 64, true))
       return cudaErrorInvalidValue;
   }
 

@@ -964,7 +964,7 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
   if (T > 0) {
     if (!make_tmap_2d(&tq, q, kHQK * kD, T, 64, 64, true) ||
         !make_tmap_2d(&tk, k, kHQK * kD, T, 64, 64, true) ||
-        !make_tmap_2d(&tv, v, kHV * kD, T, kD, 64, false))
+        !make_tmap_2d(&tv, v, kHV * kD, T, 64, 64, true))
       return cudaErrorInvalidValue;
   }
   cudaError_t err;
@@ -1019,9 +1019,7 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
 
   // chunk-parallel gradients
   if (f.nt_max > 0 && T > 0) {
-    CUtensorMap tvs;  // V with 128-byte swizzle, 64-wide boxes (the forward's map is unswizzled)
-    memset(&tvs, 0, sizeof(tvs));
-    if (!make_tmap_2d(&tvs, v, kHV * kD, T, 64, 64, true)) return cudaErrorInvalidValue;
+    const CUtensorMap &tvs = tv;  // V with 128-byte swizzle, 64-wide boxes
     err = cudaFuncSetAttribute(gdn_prefill_bwd_chunk_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, BwdTcSmem::kBytes);
     if (err != cudaSuccess) return err;

@@ -56,6 +56,14 @@ __device__ __forceinline__ uint64_t umma_desc_noswz(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// The descriptor of the operand `bytes` further on in shared memory (bytes a
+// multiple of 16): shared-memory addresses stay below 2^18, so the 14-bit
+// start-address field (address >> 4) never carries and the offset adds
+// directly -- one add per MMA instead of rebuilding the descriptor.
+__device__ __forceinline__ uint64_t umma_desc_advance(uint64_t desc, uint32_t bytes) {
+  return desc + (bytes >> 4);
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 accumulation:
 //   [4,6) D format = 1 (f32)   [7,10) A format = 1 (bf16)  [10,13) B format = 1
 //   [15] A major (1 = MN)      [16] B major (1 = MN)
