@@ -158,7 +158,7 @@ inline PrefillWs prefill_ws_layout(int64_t T, int64_t N, bool allow_segments = t
   w.seq_order = off;
   off = align_up(off + N * sizeof(int), 256);
   w.chunk_tab = off;
-  off = align_up(off + w.nt_max * sizeof(int2), 256);
+  off = align_up(off + w.nt_max * sizeof(int4), 256);
   w.items = off;
   off = align_up(off + n_items * sizeof(int4), 256);
   w.seg_off = off;
@@ -205,7 +205,7 @@ constexpr int kLptMaxSeqs = 2048;
 
 __global__ void __launch_bounds__(kMetaThreads)
 gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_t nt_max,
-                        int *meta, int *chunk_off, int *seq_order, int2 *chunk_tab,
+                        int *meta, int *chunk_off, int *seq_order, int4 *chunk_tab,
                         int seg_chunks, int seg_max, int4 *items, int *seg_off,
                         const int32_t *__restrict__ slots, int64_t pool_slots) {
   __shared__ int s_wtot[32];
@@ -287,9 +287,14 @@ gdn_prefill_meta_kernel(const int64_t *__restrict__ cu, int N, int64_t T, int64_
   }
   if (nt > nt_max) return;
   __syncthreads();
+  // chunk table: (sequence, chunk of it, first token, tokens), so that a
+  // chunk's kernels find its place with one load (T < 2^31 tokens)
   for (int i = tid; i < N; i += kMetaThreads) {
     const int off = chunk_off[i], nc = chunk_off[i + 1] - off;
-    for (int c = 0; c < nc; ++c) chunk_tab[off + c] = make_int2(i, c);
+    const int64_t b0 = cu[i], len = cu[i + 1] - b0;
+    for (int c = 0; c < nc; ++c)
+      chunk_tab[off + c] = make_int4(i, c, static_cast<int>(b0 + static_cast<int64_t>(c) * kChunk),
+                                     static_cast<int>(lmin(kChunk, len - static_cast<int64_t>(c) * kChunk)));
   }
   // Longest-first order of sequences (ties by index) so that the scan's
   // longest recurrences start first.
@@ -548,20 +553,21 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         const float *__restrict__ A_log, const uint16_t *__restrict__ a,
                         const float *__restrict__ dt_bias, const uint16_t *__restrict__ b,
                         const int64_t *__restrict__ cu, const int *__restrict__ meta,
-                        const int2 *__restrict__ chunk_tab, float *__restrict__ gcum_ws,
+                        const int4 *__restrict__ chunk_tab, float *__restrict__ gcum_ws,
                         float *__restrict__ beta_ws, uint8_t *__restrict__ m2_ws) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_align<1024>(smem_raw);
   const int gchunk = blockIdx.x, hqk = blockIdx.y;
+  // the chunk's entry is read alongside the count (the grid covers the
+  // table's nt_max entries; one past the count is never used)
+  const int4 e = chunk_tab[gchunk];
   if (meta[1] != 0 || gchunk >= meta[0]) return;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int2 e = chunk_tab[gchunk];
   GDN_DCHECK(e.x >= 0 && e.x < meta[kMetaN] && e.y >= 0);
-  const int64_t bos = cu[e.x];
-  const int64_t t0 = bos + static_cast<int64_t>(e.y) * kChunk;
-  const int L = static_cast<int>(lmin(kChunk, cu[e.x + 1] - t0));
-  GDN_DCHECK(L > 0 && t0 + L <= meta[kMetaT]);
+  const int64_t t0 = e.z;
+  const int L = e.w;
+  GDN_DCHECK(t0 == cu[e.x] + static_cast<int64_t>(e.y) * kChunk && L > 0 && t0 + L <= meta[kMetaT]);
 
   uint8_t *qk = smem + kPrepQK;
   uint8_t *pp = smem + kPrepQK;  // P image, written only once A is no longer read
@@ -700,10 +706,12 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
             prod[u + 1] = f2_hi(r);
           }
           if (warp >= 2) {
+            // only the strictly lower triangle: nothing reads A at col >= i
+            // (the solve masks the entries it loads there)
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int col = 8 * cc + u;
-              AT[(j * 64 + col) * 64 + i] = (rv && col < i) ? prod[u] : 0.f;
+              if (col < i) AT[(j * 64 + col) * 64 + i] = rv ? prod[u] : 0.f;
             }
           } else {
             float vals[8];
@@ -1470,10 +1478,6 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       // the output MMA still reads this chunk's P rows: with outputs the next
       // image is issued once that MMA has completed
       if (!kOut && tid == kCopyThread && c + 1 < nchunks) issue_m2(c + 1);
-      // the gate factors of chunk c + 2 (their buffer's last reader was the
-      // previous chunk), visible to all after the barrier below: Q~ of chunk
-      // c + 2 is formed with them at the start of the next chunk
-      if (gate_thread && c + 2 < nchunks) store_gates(next_gates, gs2);
 
       // ---- V_dec (the outputs wait until MMA 3 runs) ----
   #pragma unroll
@@ -1544,7 +1548,13 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         ph_o ^= 1;
         tc_fence_after();
         if (tid == kCopyThread && c + 1 < nchunks) issue_m2(c + 1);
+        // Lanes 2m and 2m + 1 (rows v, v + 1) swap one value per token pair
+        // so that each stores a bf16 pair of adjacent v: the even lane token
+        // t, the odd lane token t + 1 -- half the store instructions.
         const uint64_t sc2 = f2_pack(scale, scale);
+        const bool odd = lane & 1;
+        uint32_t *orow = reinterpret_cast<uint32_t *>(
+            out + ((t0 + 32 * hc + (odd ? 1 : 0)) * kHV + hv) * kD + (vrow & ~1));
   #pragma unroll
         for (int p = 0; p < 2; ++p) {
           const int tb = 32 * hc + 16 * p;
@@ -1553,16 +1563,19 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
           tmem_wait_ld();
   #pragma unroll
           for (int j = 0; j < 16; j += 2) {
-            const int t = tb + j;
             const uint64_t o = f2_mul(sc2, f2_pack(zo[j], zo[j + 1]));
-            if (t < L)
-              out[((t0 + t) * kHV + hv) * kD + vrow] =
-                  __bfloat16_as_ushort(__float2bfloat16_rn(f2_lo(o)));
-            if (t + 1 < L)
-              out[((t0 + t + 1) * kHV + hv) * kD + vrow] =
-                  __bfloat16_as_ushort(__float2bfloat16_rn(f2_hi(o)));
+            const float oe = f2_lo(o), oo = f2_hi(o);  // tokens tb + j, tb + j + 1
+            const float got = __shfl_xor_sync(0xffffffffu, odd ? oe : oo, 1);
+            const uint32_t pair = odd ? pack_bf16x2(got, oo) : pack_bf16x2(oe, got);
+            if (tb + j + (odd ? 1 : 0) < L) orow[(16 * p + j) * (kHV * kD / 2)] = pair;
           }
         }
+        // the gate factors of chunk c + 2, while MMA 3 runs (their buffer's
+        // last reader was the previous chunk; the barrier ending this chunk
+        // makes them visible before Q~ of chunk c + 2 is formed)
+        if (gate_thread && c + 2 < nchunks) store_gates(next_gates, gs2);
+      } else {
+        if (gate_thread && c + 2 < nchunks) store_gates(next_gates, gs2);
       }
       wait_phase(bar_mma, ph_mma, broken);
       ph_mma ^= 1;
@@ -1808,7 +1821,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   int *meta = reinterpret_cast<int *>(ws + w.meta);
   int *chunk_off = reinterpret_cast<int *>(ws + w.chunk_off);
   int *seq_order = reinterpret_cast<int *>(ws + w.seq_order);
-  int2 *chunk_tab = reinterpret_cast<int2 *>(ws + w.chunk_tab);
+  int4 *chunk_tab = reinterpret_cast<int4 *>(ws + w.chunk_tab);
   float *gcum = reinterpret_cast<float *>(ws + w.gcum);
   float *beta = reinterpret_cast<float *>(ws + w.beta);
   uint8_t *m2 = ws + w.m2;

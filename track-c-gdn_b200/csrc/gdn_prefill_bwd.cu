@@ -509,7 +509,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
                              const float *__restrict__ A_log,
                              const uint16_t *__restrict__ a, const float *__restrict__ dt_bias,
                              const int64_t *__restrict__ cu, const int *__restrict__ meta,
-                             const int2 *__restrict__ chunk_tab, const float *__restrict__ gcum_ws,
+                             const int4 *__restrict__ chunk_tab, const float *__restrict__ gcum_ws,
                              const float *__restrict__ beta_ws,
                              const uint8_t *__restrict__ states_ws,
                              const uint8_t *__restrict__ dsc_ws,
@@ -524,9 +524,9 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const int g = blockIdx.x, hv = blockIdx.y, hqk = hv >> 1;
   if (meta[kMetaError] != 0 || g >= meta[kMetaChunks]) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int2 e = chunk_tab[g];
-  const int64_t t0 = cu[e.x] + static_cast<int64_t>(e.y) * kChunk;
-  const int L = static_cast<int>(lmin(kChunk, cu[e.x + 1] - t0));
+  const int4 e = chunk_tab[g];
+  const int64_t t0 = e.z;
+  const int L = e.w;
   GDN_DCHECK(e.x >= 0 && e.x < meta[kMetaN] && L > 0 && t0 + L <= meta[kMetaT]);
   const int64_t soff = (static_cast<int64_t>(g) * kHV + hv) * kStateImgBytes;
   const int64_t toff = (static_cast<int64_t>(g) * kHV + hv) * kTokImgBytes;
@@ -945,7 +945,7 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
   int *meta = reinterpret_cast<int *>(ws + f.meta);
   int *chunk_off = reinterpret_cast<int *>(ws + f.chunk_off);
   int *seq_order = reinterpret_cast<int *>(ws + f.seq_order);
-  int2 *chunk_tab = reinterpret_cast<int2 *>(ws + f.chunk_tab);
+  int4 *chunk_tab = reinterpret_cast<int4 *>(ws + f.chunk_tab);
   float *gcum = reinterpret_cast<float *>(ws + f.gcum);
   float *beta = reinterpret_cast<float *>(ws + f.beta);
   uint8_t *m2 = ws + f.m2;
