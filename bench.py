@@ -625,6 +625,18 @@ def gpu_arm(args):
                 pre["T"] * SCAN_FLOP_PER_TOKEN,
                 pre["T"] * SCAN_BYTES_PER_TOKEN + n_states * STATE_BYTES, scan_s, peaks,
                 traffic.get("scan_bytes_per_launch"))
+        # tensor-pipe utilisation (sm__pipe_tensor_cycles_active, % of active
+        # cycles) of each kernel from its one-kernel ncu capture; the call's
+        # figure is their average weighted by this run's kernel times
+        tc = {k: traffic.get(f"{k}_tensor_pipe_active_pct") for k in per_kernel}
+        for k, v in tc.items():
+            per_kernel[k]["tensor_pipe_active_pct"] = v
+        if per_kernel and all(v is not None for v in tc.values()):
+            w = {k: per_kernel[k]["measured_ms"] for k in per_kernel}
+            result["roofline"]["tensor_pipe_active_pct"] = (
+                sum(tc[k] * w[k] for k in w) / sum(w.values()))
+            result["roofline"]["tensor_pipe_source"] = (
+                "ncu one-kernel captures (profiles/traffic.json), weighted by this run's kernel times")
         if per_kernel:
             result["roofline_kernels"] = per_kernel
     elif dec is not None:
