@@ -986,22 +986,29 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
 constexpr int kScanThreads = 256;
 constexpr int kCopyThread = 32;  // lane 0 of warp 1
 
-struct ScanSmem {
+template <bool kSave>
+struct ScanSmemT {
   // Q and K tiles of a chunk, double buffered: [Q.d0 | K.d0 | Q.d1 | K.d1],
   // each 64 t rows x 128 B (64 bf16 of d), 128-byte swizzle.  Rows 0..63 of
   // [Q.db ; K.db] are the 128 N rows of MMA 1's B operand for d-block db.
   static constexpr int kQK0 = 0;
   static constexpr int kQK1 = 32768;
-  static constexpr int kM2 = 65536;    // [P ; Ainv] image (the backward's full one: 16 KB)
+  // [P ; Ainv] image: the forward's compact 10 KiB, the backward's full 16 KiB
+  static constexpr int kM2 = 65536;
+  static constexpr int kM2Size = kSave ? 16384 : 10240;
   // V tile: 2 v-blocks x 64 t rows x 128 B, 128-byte swizzle (the MN-major
   // A operand of the V MMA)
-  static constexpr int kV = 81920;
+  static constexpr int kV = kM2 + kM2Size;
+  // bf16 output tile of a full chunk, [64 t][128 v] (256-byte rows), for one
+  // TMA store (the forward only)
+  static constexpr int kOst = kV + 16384;
+  static constexpr int kOstSize = kSave ? 0 : 16384;
   // per-token gate factors of the current / next chunk, computed once per
   // chunk: e^{G_t}, beta_t, e^{G_last - G_t} (0 past the end), e^{G_last}
   // (three chunks' worth: the current one, and the next two, whose factors
   // are stored a chunk ahead so that Q~ of the next chunk can be formed at
   // the start of this one)
-  static constexpr int kG = 98304;     // float eG[3][64]
+  static constexpr int kG = kOst + kOstSize;  // float eG[3][64]
   static constexpr int kB = kG + 768;  // float beta[3][64]
   static constexpr int kDec = kB + 768;  // float eDec[3][64]
   static constexpr int kEn = kDec + 768;  // float -eG[3][64] (the X phase's fused multiply-add)
@@ -1029,10 +1036,14 @@ struct ScanSmem {
   // V[t][v] in fp32 (the V MMA), read by the X phase; free until MMA 3's dS
   static constexpr uint32_t kColV = 192;
 };
+using ScanSmem = ScanSmemT<false>;
 // the epilogue stages one 64 KB (n, hv) state over the two Q/K tile buffers
 static_assert(ScanSmem::kQK0 == 0 && ScanSmem::kQK1 + 32768 <= ScanSmem::kM2, "state staging region");
 static_assert(ScanSmem::kColO + 64 == ScanSmem::kColYk, "MMA 1 writes [e^G Yq | Yk] in one pass");
-static_assert(2 * ScanSmem::kBytes <= 227 * 1024, "two CTAs per SM");
+static_assert(ScanSmem::kV % 1024 == 0 && ScanSmemT<true>::kV % 1024 == 0, "swizzled V tile alignment");
+// two CTAs per SM: 228 KB per SM, 1 KB of it reserved per CTA
+static_assert(2 * (ScanSmem::kBytes + 1024) <= 228 * 1024 &&
+              2 * (ScanSmemT<true>::kBytes + 1024) <= 228 * 1024, "two CTAs per SM");
 
 // kSave = true is the backward pass's recompute: FULL items only, no outputs
 // and no final state; instead the state at the start of every chunk goes to
@@ -1044,7 +1055,8 @@ template <bool kSave>
 __global__ void __launch_bounds__(kScanThreads, 2)
 gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         const __grid_constant__ CUtensorMap tmap_k,
-                        const __grid_constant__ CUtensorMap tmap_v, const float *h0,
+                        const __grid_constant__ CUtensorMap tmap_v,
+                        const __grid_constant__ CUtensorMap tmap_o, const float *h0,
                         const int64_t *__restrict__ cu, const int *__restrict__ meta,
                         const int *__restrict__ chunk_off,
                         const float *__restrict__ gcum_ws, const float *__restrict__ beta_ws,
@@ -1054,7 +1066,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
                         const int *__restrict__ seg_off, float *seg_ss, float *seg_sb,
                         float *seg_phi, const int32_t *__restrict__ slots,
                         uint8_t *__restrict__ save_states, uint8_t *__restrict__ save_delta) {
-  using SM = ScanSmem;
+  using SM = ScanSmemT<kSave>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_align<1024>(smem_raw);
   if (meta[1] != 0) return;
@@ -1442,6 +1454,11 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         for (int j = 0; j < 8; ++j) pk[j] = pack_bf16x2(yk[2 * j], yk[2 * j + 1]);
         tmem_st8(tlane + SM::kColX + 32 * hc + 8 * p, pk);
       }
+      // the previous chunk's output store has read its tile before this
+      // barrier, so the output phase below may overwrite it
+      if constexpr (kOut) {
+        if (tid == kCopyThread) bulk_wait_read_all();
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncthreads();
@@ -1552,22 +1569,44 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         // so that each stores a bf16 pair of adjacent v: the even lane token
         // t, the odd lane token t + 1 -- half the store instructions.
         const uint64_t sc2 = f2_pack(scale, scale);
-        const bool odd = lane & 1;
-        uint32_t *orow = reinterpret_cast<uint32_t *>(
-            out + ((t0 + 32 * hc + (odd ? 1 : 0)) * kHV + hv) * kD + (vrow & ~1));
+        if (L == kChunk) {
+          // a full chunk: the bf16 tile [t][v] in shared memory (a warp's
+          // stores for one token cover 64 contiguous bytes), sent by one TMA
+          // store after the barrier that ends the chunk
+          uint16_t *ost = reinterpret_cast<uint16_t *>(smem + SM::kOst) + vrow;
   #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const int tb = 32 * hc + 16 * p;
-          float zo[16];
-          tmem_ld16(tlane + SM::kColO + tb, zo);
-          tmem_wait_ld();
+          for (int p = 0; p < 2; ++p) {
+            const int tb = 32 * hc + 16 * p;
+            float zo[16];
+            tmem_ld16(tlane + SM::kColO + tb, zo);
+            tmem_wait_ld();
   #pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            const uint64_t o = f2_mul(sc2, f2_pack(zo[j], zo[j + 1]));
-            const float oe = f2_lo(o), oo = f2_hi(o);  // tokens tb + j, tb + j + 1
-            const float got = __shfl_xor_sync(0xffffffffu, odd ? oe : oo, 1);
-            const uint32_t pair = odd ? pack_bf16x2(got, oo) : pack_bf16x2(oe, got);
-            if (tb + j + (odd ? 1 : 0) < L) orow[(16 * p + j) * (kHV * kD / 2)] = pair;
+            for (int j = 0; j < 16; j += 2) {
+              const uint64_t o = f2_mul(sc2, f2_pack(zo[j], zo[j + 1]));
+              ost[(tb + j) * kD] = __bfloat16_as_ushort(__float2bfloat16_rn(f2_lo(o)));
+              ost[(tb + j + 1) * kD] = __bfloat16_as_ushort(__float2bfloat16_rn(f2_hi(o)));
+            }
+          }
+          fence_async_smem();
+        } else {
+          // the tail chunk: direct stores of the first L tokens only
+          const bool odd = lane & 1;
+          uint32_t *orow = reinterpret_cast<uint32_t *>(
+              out + ((t0 + 32 * hc + (odd ? 1 : 0)) * kHV + hv) * kD + (vrow & ~1));
+  #pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            const int tb = 32 * hc + 16 * p;
+            float zo[16];
+            tmem_ld16(tlane + SM::kColO + tb, zo);
+            tmem_wait_ld();
+  #pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+              const uint64_t o = f2_mul(sc2, f2_pack(zo[j], zo[j + 1]));
+              const float oe = f2_lo(o), oo = f2_hi(o);  // tokens tb + j, tb + j + 1
+              const float got = __shfl_xor_sync(0xffffffffu, odd ? oe : oo, 1);
+              const uint32_t pair = odd ? pack_bf16x2(got, oo) : pack_bf16x2(oe, got);
+              if (tb + j + (odd ? 1 : 0) < L) orow[(16 * p + j) * (kHV * kD / 2)] = pair;
+            }
           }
         }
         // the gate factors of chunk c + 2, while MMA 3 runs (their buffer's
@@ -1609,6 +1648,15 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
+      // every thread's part of a full chunk's output tile is written (and
+      // fenced for the async proxy): one TMA store (x = v-head column,
+      // 256-byte aligned; y = the chunk's first token)
+      if constexpr (kOut) {
+        if (L == kChunk && tid == kCopyThread) {
+          tma_store_2d(&tmap_o, hv * kD, static_cast<int>(t0), s_base + SM::kOst);
+          bulk_commit_group();
+        }
+      }
     }
   };
   // (the recompute has no outputs: its kernel has no output loop at all)
@@ -1645,6 +1693,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
   }
 
+  if (tid == kCopyThread) bulk_wait_all();  // the last output store has completed
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -1832,14 +1881,18 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   float *seg_phi = reinterpret_cast<float *>(ws + w.seg_phi);
   const int64_t seg_tokens = w.seg_chunks ? w.seg_chunks * kChunk : (int64_t{1} << 40);
 
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   memset(&tq, 0, sizeof(tq));
   memset(&tk, 0, sizeof(tk));
   memset(&tv, 0, sizeof(tv));
+  memset(&to, 0, sizeof(to));
   if (T > 0) {
+    // to: the output as [T][8 * 128] bf16, one (64 token x 128 v) box per
+    // full chunk and v-head (the scan's TMA store)
     if (!make_tmap_2d(&tq, q, kHQK * kD, T, 64, 64, true) ||
         !make_tmap_2d(&tk, k, kHQK * kD, T, 64, 64, true) ||
-        !make_tmap_2d(&tv, v, kHV * kD, T, 64, 64, true))
+        !make_tmap_2d(&tv, v, kHV * kD, T, 64, 64, true) ||
+        !make_tmap_2d(&to, out, kHV * kD, T, kD, 64, false))
       return cudaErrorInvalidValue;
   }
 
@@ -1870,7 +1923,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   const int64_t n1 = w.seg_chunks ? 2 * w.seg_max : N;
   gdn_prefill_scan_kernel<false><<<static_cast<unsigned>(n1 * kHV), kScanThreads,
                                    ScanSmem::kBytes, stream>>>(
-      tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale,
+      tq, tk, tv, to, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale,
       static_cast<uint16_t *>(out), final_state, items, 2, seg_tokens, seg_off, seg_ss, seg_sb,
       seg_phi, slots, nullptr, nullptr);
   err = cudaGetLastError();
@@ -1889,7 +1942,7 @@ cudaError_t launch_prefill(const void *q, const void *k, const void *v, const fl
   // pass 3
   gdn_prefill_scan_kernel<false><<<static_cast<unsigned>(w.seg_max * kHV), kScanThreads,
                                    ScanSmem::kBytes, stream>>>(
-      tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale,
+      tq, tk, tv, to, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale,
       static_cast<uint16_t *>(out), final_state, items + 2 * w.seg_max, 3, seg_tokens, seg_off,
       seg_ss, seg_sb, seg_phi, slots, nullptr, nullptr);
   err = cudaGetLastError();

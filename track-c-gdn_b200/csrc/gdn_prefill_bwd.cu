@@ -993,11 +993,12 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
     if (err != cudaSuccess) return err;
   }
   err = cudaFuncSetAttribute(gdn_prefill_scan_kernel<true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, ScanSmem::kBytes);
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, ScanSmemT<true>::kBytes);
   if (err != cudaSuccess) return err;
-  gdn_prefill_scan_kernel<true><<<static_cast<unsigned>(N * kHV), kScanThreads, ScanSmem::kBytes,
+  gdn_prefill_scan_kernel<true><<<static_cast<unsigned>(N * kHV), kScanThreads, ScanSmemT<true>::kBytes,
                                   stream>>>(
-      tq, tk, tv, state, cu_seqlens, meta, chunk_off, gcum, beta, m2, scale, nullptr, nullptr,
+      tq, tk, tv, tv /* no outputs: the store map is never used */, state, cu_seqlens, meta,
+      chunk_off, gcum, beta, m2, scale, nullptr, nullptr,
       items, kMetaPass1, int64_t{1} << 40, seg_off, nullptr, nullptr, nullptr, nullptr, states,
       delta);
   err = cudaGetLastError();

@@ -245,6 +245,27 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int 
       : "memory");
 }
 
+// 2D tiled TMA store of one box from shared memory to this GPU's global
+// memory, tracked by the issuing thread's bulk async-group.
+__device__ __forceinline__ void tma_store_2d(const void *tmap, int x, int y, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               :
+               : "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until this thread's committed bulk stores have read their shared-memory
+// source (the buffer may be rewritten) ...
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// ... or have completed (their writes are done).
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Contiguous global -> shared bulk copy (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
                                           uint32_t mbar) {
