@@ -521,7 +521,11 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   using SM = BwdTcSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_align<1024>(smem_raw);
-  const int g = blockIdx.x, hv = blockIdx.y, hqk = hv >> 1;
+  // one CTA per (chunk, v-head), the v-head fastest: the eight CTAs of a
+  // chunk run side by side, so the two that add into the same dq / dk rows
+  // (the v-heads of one q/k head) and share its Q/K tiles meet in L2
+  const int g = static_cast<int>(blockIdx.x / kHV), hv = static_cast<int>(blockIdx.x % kHV);
+  const int hqk = hv >> 1;
   if (meta[kMetaError] != 0 || g >= meta[kMetaChunks]) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int4 e = chunk_tab[g];
@@ -1024,7 +1028,7 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
     err = cudaFuncSetAttribute(gdn_prefill_bwd_chunk_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, BwdTcSmem::kBytes);
     if (err != cudaSuccess) return err;
-    dim3 grid(static_cast<unsigned>(f.nt_max), kHV);
+    const unsigned grid = static_cast<unsigned>(f.nt_max * kHV);
     gdn_prefill_bwd_chunk_kernel<<<grid, kBwdTcThreads, BwdTcSmem::kBytes, stream>>>(
         tq, tk, tdo, tvs, A_log, static_cast<const uint16_t *>(a), dt_bias, cu_seqlens, meta,
         chunk_tab, gcum, beta, states, dsc, delta, dx, scale, dq, dk, da, db, dgg);
