@@ -667,8 +667,6 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   // (no per-entry exponential; exact to fp32 rounding, never overflows).
   float *AT = reinterpret_cast<float *>(smem + kPrepQK);
   {
-    const int i = (warp & 1) * 32 + lane;
-    const bool rv = i < L;
     const uint32_t trow = tmem + (static_cast<uint32_t>(32 * warp) << 16);
     // Rows 0..31 (warps 0 and 2) have no nonzero entry right of column 31:
     // their P rows are zero there and their A rows are not stored there (that
@@ -676,6 +674,11 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     auto rows = [&](auto upper_tag) {
       constexpr bool kUpper = decltype(upper_tag)::value;
       constexpr int kGroups = kUpper ? 4 : 8;  // 8-column groups that can be nonzero
+      // row i of this thread, as an expression the compiler can bound: the
+      // lower rows' column tests in groups 0..3 (columns 0..31 < 32 <= i)
+      // then fold to true
+      const int i = kUpper ? lane : 32 + lane;
+      const bool rv = i < L;
       float acc[8 * kGroups];  // row i of Q K^T (warps 0,1) or K K^T (warps 2,3)
       tmem_ld32(trow, *reinterpret_cast<float(*)[32]>(acc));
       if constexpr (!kUpper) tmem_ld32(trow + 32, *reinterpret_cast<float(*)[32]>(acc + 32));
