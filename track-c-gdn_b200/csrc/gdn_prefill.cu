@@ -683,6 +683,13 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tmem_ld32(trow, *reinterpret_cast<float(*)[32]>(acc));
       if constexpr (!kUpper) tmem_ld32(trow + 32, *reinterpret_cast<float(*)[32]>(acc + 32));
       tmem_wait_ld();
+      // a row past the sequence end (tail chunks only) is zero in A and P:
+      // zero its products once here (0 times a finite, non-negative decay
+      // factor is +0, the value the masks below would have written)
+      if (!rv) {
+#pragma unroll
+        for (int u = 0; u < 8 * kGroups; ++u) acc[u] = 0.f;
+      }
 #pragma unroll 1
       for (int j = 0; j < 2; ++j) {
         // e^{G_i - G_c} for the current column c (1 for c >= i), times beta_i
@@ -714,14 +721,14 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int col = 8 * cc + u;
-              if (col < i) AT[(j * 64 + col) * 64 + i] = rv ? prod[u] : 0.f;
+              if (col < i) AT[(j * 64 + col) * 64 + i] = prod[u];
             }
           } else {
             float vals[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int col = 8 * cc + u;
-              vals[u] = (rv && col <= i) ? prod[u] : 0.f;
+              vals[u] = col <= i ? prod[u] : 0.f;
             }
             prow[4 * cc + 0] = pack_bf16x2(vals[0], vals[1]);
             prow[4 * cc + 1] = pack_bf16x2(vals[2], vals[3]);
