@@ -647,12 +647,11 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   // D[128 x 64] = [Q;K] K^T : rows 0..63 Q K^T, rows 64..127 K K^T.
   if (tid == 0) {
     const uint32_t idesc = umma_idesc_bf16(128, 64, false, false);
-    const uint32_t base = smem_u32(qk);
+    const uint64_t dqk = umma_desc_sw128(smem_u32(qk), 16, 1024);
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-      umma_bf16(tmem, umma_desc_sw128(base + off, 16, 1024),
-                umma_desc_sw128(base + 8192 + off, 16, 1024), idesc, ks > 0);
+      umma_bf16(tmem, umma_desc_advance(dqk, off), umma_desc_advance(dqk, 8192 + off), idesc, ks > 0);
     }
     umma_commit(bar);
   }
@@ -917,14 +916,14 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
   // reusing TMEM columns 64 j .. 64 j + 63.
   if (tid == 0) {
     const uint32_t idesc = umma_idesc_bf16(128, 64, false, true);
-    const uint32_t pbase = smem_u32(pp);
+    const uint64_t dp = umma_desc_sw128(smem_u32(pp), 16, 1024);
+    const uint64_t dai = umma_desc_sw128(smem_u32(ai), 8192, 1024);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const uint32_t bbase = smem_u32(ai + j * 8192);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(tmem + 64 * j, umma_desc_sw128(pbase + ks * 32, 16, 1024),
-                  umma_desc_sw128(bbase + ks * 2048, 8192, 1024), idesc, ks > 0);
+        umma_bf16(tmem + 64 * j, umma_desc_advance(dp, ks * 32),
+                  umma_desc_advance(dai, j * 8192 + ks * 2048), idesc, ks > 0);
     }
     umma_commit(bar);
   }

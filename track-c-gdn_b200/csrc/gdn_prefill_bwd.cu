@@ -281,11 +281,12 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 
     // ---- MMA a: Zr = dS K^T ----
     if (tid == 0) {
+      const uint64_t dk = umma_desc_sw128(kbuf, 16, 1024);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t boff = (ks >> 2) * 8192 + (ks & 3) * 32;
-        umma_bf16_ts(tmem + SM::kColA, tmem + SM::kColSb + 8 * ks,
-                     umma_desc_sw128(kbuf + boff, 16, 1024), id_a, ks > 0);
+        umma_bf16_ts(tmem + SM::kColA, tmem + SM::kColSb + 8 * ks, umma_desc_advance(dk, boff), id_a,
+                     ks > 0);
       }
       umma_commit(bar_mma);
     }
@@ -326,14 +327,15 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 
     // ---- MMA b: dX / scale = dO^T (P Ainv) + (Z / scale) Ainv ----
     if (tid == 0) {
+      const uint64_t dmn = umma_desc_sw128(s_base, 8192, 1024);  // MN-major, 8 KB between blocks
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(tmem + SM::kColB, umma_desc_sw128(s_base + SM::kDO + ks * 2048, 8192, 1024),
-                  umma_desc_sw128(s_base + SM::kImg + ks * 2048, 8192, 1024), id_b1, ks > 0);
+        umma_bf16(tmem + SM::kColB, umma_desc_advance(dmn, SM::kDO + ks * 2048),
+                  umma_desc_advance(dmn, SM::kImg + ks * 2048), id_b1, ks > 0);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         umma_bf16_ts(tmem + SM::kColB, tmem + SM::kColZX + 32 * (ks >> 1) + 8 * (ks & 1),
-                     umma_desc_sw128(s_base + SM::kImg + 8192 + ks * 2048, 8192, 1024), id_b2, 1);
+                     umma_desc_advance(dmn, SM::kImg + 8192 + ks * 2048), id_b2, 1);
       umma_commit(bar_mma);
     }
     wait_phase(bar_mma, ph_mma, broken);
@@ -370,14 +372,16 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 
     // ---- MMA c: dS' = dO^T Q' - (beta e^G dX) K ----
     if (tid == 0) {
+      const uint64_t dmn = umma_desc_sw128(s_base, 8192, 1024);
+      const uint64_t dkm = umma_desc_sw128(kbuf, 8192, 1024);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(tmem + SM::kColA, umma_desc_sw128(s_base + SM::kDO + ks * 2048, 8192, 1024),
-                  umma_desc_sw128(s_base + SM::kQ + ks * 2048, 8192, 1024), id_c1, ks > 0);
+        umma_bf16(tmem + SM::kColA, umma_desc_advance(dmn, SM::kDO + ks * 2048),
+                  umma_desc_advance(dmn, SM::kQ + ks * 2048), id_c1, ks > 0);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         umma_bf16_ts(tmem + SM::kColA, tmem + SM::kColZX + 32 * (ks >> 1) + 8 * (ks & 1),
-                     umma_desc_sw128(kbuf + ks * 2048, 8192, 1024), id_c2, 1);
+                     umma_desc_advance(dkm, ks * 2048), id_c2, 1);
       umma_commit(bar_mma);
     }
     wait_phase(bar_mma, ph_mma, broken);
@@ -622,24 +626,26 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const uint32_t id_kk = umma_idesc_bf16(128, 64, false, false);
     const uint32_t id_kk2 = umma_idesc_bf16(128, 128, false, false);
     const uint32_t id_mn = umma_idesc_bf16(128, 64, true, false);
+    // one descriptor per layout, advanced by each operand's byte offset
+    const uint64_t dk16 = umma_desc_sw128(s_base, 16, 1024);      // K-major
+    const uint64_t dmn16k = umma_desc_sw128(s_base, 16384, 1024);  // MN-major, 16 KB between blocks
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-      umma_bf16(tmem + kTcA, umma_desc_sw128(s_base + SM::kQK + off, 16, 1024),
-                umma_desc_sw128(s_base + SM::kQK + 8192 + off, 16, 1024), id_kk, ks > 0);
-      umma_bf16(tmem + kTcB, umma_desc_sw128(s_base + SM::kOX + off, 16, 1024),
-                umma_desc_sw128(s_base + SM::kDV + off, 16, 1024), id_kk2, ks > 0);
+      umma_bf16(tmem + kTcA, umma_desc_advance(dk16, SM::kQK + off),
+                umma_desc_advance(dk16, SM::kQK + 8192 + off), id_kk, ks > 0);
+      umma_bf16(tmem + kTcB, umma_desc_advance(dk16, SM::kOX + off),
+                umma_desc_advance(dk16, SM::kDV + off), id_kk2, ks > 0);
     }
     umma_commit(bar_m1);
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {  // K = v, 16 rows of the MN-major tiles per step
       const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-      const uint64_t s0 = umma_desc_sw128(s_base + SM::kS0 + ks * 2048, 16384, 1024);
-      umma_bf16(tmem + kTcP1, s0, umma_desc_sw128(s_base + SM::kOX + off, 16, 1024), id_mn, ks > 0);
-      umma_bf16(tmem + kTcP2, s0, umma_desc_sw128(s_base + SM::kOX + 8192 + off, 16, 1024), id_mn,
-                ks > 0);
-      umma_bf16(tmem + kTcP3, umma_desc_sw128(s_base + SM::kDS + ks * 2048, 16384, 1024),
-                umma_desc_sw128(s_base + SM::kDV + off, 16, 1024), id_mn, ks > 0);
+      const uint64_t s0 = umma_desc_advance(dmn16k, SM::kS0 + ks * 2048);
+      umma_bf16(tmem + kTcP1, s0, umma_desc_advance(dk16, SM::kOX + off), id_mn, ks > 0);
+      umma_bf16(tmem + kTcP2, s0, umma_desc_advance(dk16, SM::kOX + 8192 + off), id_mn, ks > 0);
+      umma_bf16(tmem + kTcP3, umma_desc_advance(dmn16k, SM::kDS + ks * 2048),
+                umma_desc_advance(dk16, SM::kDV + off), id_mn, ks > 0);
     }
     umma_commit(bar_m2);
   }
@@ -725,19 +731,20 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   if (tid == 0) {
     const uint32_t id_f = umma_idesc_bf16(128, 64, true, false);
     const uint32_t id_g = umma_idesc_bf16(128, 64, true, true);
+    const uint64_t dk16 = umma_desc_sw128(s_base, 16, 1024);
+    const uint64_t dmn16k = umma_desc_sw128(s_base, 16384, 1024);
+    const uint64_t dmn8k = umma_desc_sw128(s_base, 8192, 1024);
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {  // K = 64 tokens
-      const uint64_t kt = umma_desc_sw128(s_base + SM::kQK + 8192 + ks * 2048, 16384, 1024);
-      const uint64_t qt = umma_desc_sw128(s_base + SM::kQK + ks * 2048, 16384, 1024);
-      umma_bf16(tmem + kTcF, kt, umma_desc_sw128(s_base + SM::kMQ + ks * 32, 16, 1024), id_f,
-                ks > 0);
-      umma_bf16(tmem + kTcGH, qt, umma_desc_sw128(s_base + SM::kMQ + ks * 2048, 8192, 1024), id_g,
-                ks > 0);
+      const uint64_t kt = umma_desc_advance(dmn16k, SM::kQK + 8192 + ks * 2048);
+      const uint64_t qt = umma_desc_advance(dmn16k, SM::kQK + ks * 2048);
+      umma_bf16(tmem + kTcF, kt, umma_desc_advance(dk16, SM::kMQ + ks * 32), id_f, ks > 0);
+      umma_bf16(tmem + kTcGH, qt, umma_desc_advance(dmn8k, SM::kMQ + ks * 2048), id_g, ks > 0);
     }
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks)
-      umma_bf16(tmem + kTcGH, umma_desc_sw128(s_base + SM::kQK + 8192 + ks * 2048, 16384, 1024),
-                umma_desc_sw128(s_base + SM::kMS + ks * 32, 16, 1024), id_f, 1);
+      umma_bf16(tmem + kTcGH, umma_desc_advance(dmn16k, SM::kQK + 8192 + ks * 2048),
+                umma_desc_advance(dk16, SM::kMS + ks * 32), id_f, 1);
     umma_commit(bar_m3);
   }
 
