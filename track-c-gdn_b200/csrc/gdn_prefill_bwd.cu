@@ -22,7 +22,7 @@
 //               dS <- e^{G_C} dS + scale (e^G dO)^T Q - (beta e^G dX)^T K
 //             and stores dS (chunk end) per chunk, dX per token (a bf16
 //             operand image) and dv = beta dX;
-//   bwd_chunk (one CTA per (chunk, v-head), all chunks at once):
+//   bwd_chunk (persistent; per (chunk, v-head), all chunks at once):
 //               dq = scale e^G (dO S_0) + Mq K
 //               dk = Mq^T Q + (Ma + Ma^T) K + e^{G_C-G} (delta dS_C) - beta e^G (dX S_0)
 //               dbeta,  dG -> dg (reverse cumsum in the chunk) -> da, db
@@ -33,9 +33,9 @@
 // Both kernels run their products on the tensor cores (bf16 operands, fp32
 // accumulators, as the forward) and the rest in fp32; the state gradient
 // itself is carried in fp32.  Every sum has a
-// fixed order; dq and dk (shared by the two v-heads of a q/k head) are the
-// sum of exactly two fp32 atomic additions onto zero, which is
-// order-independent, so the whole backward is deterministic.
+// fixed order; dq and dk (shared by the two v-heads of a q/k head) are one
+// fp32 addition of the two v-heads' contributions, exchanged between the two
+// CTAs of a cluster, so the whole backward is deterministic.
 
 namespace gdn {
 
@@ -431,8 +431,11 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // ---------------------------------------------------------------------------
 // chunk-parallel gradients (tcgen05)
 // ---------------------------------------------------------------------------
-// One CTA (128 threads, the whole TMEM) per (chunk, v-head).  Eight MMAs on
-// bf16 operands, fp32 accumulators in TMEM:
+// Persistent clusters of two CTAs (256 threads and the whole TMEM each, one
+// CTA per SM): a cluster takes the (chunk, q/k head) pairs in turn, its rank
+// r the v-head 2 hqk + r, and each CTA fetches the next pair's operands into
+// its buffers as they retire.  Per (chunk, v-head), eight MMAs on bf16
+// operands, fp32 accumulators in TMEM:
 //   (a) [Q;K] K^T      -> QK (lanes 0-63), KK (lanes 64-127)      M=128 N=64 K=128
 //   (b) [dO;dX] [delta;V]^T -> dO.delta (lanes 0-63), dX.delta and dX.v
 //                          (lanes 64-127; the diagonal of dX.v is dX_t.v_t)  N=128
@@ -444,7 +447,9 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // S_0, dS_C ([v][k] in memory) and the Q and K tiles ([t][k]) enter (c)-(h)
 // as MN-major A operands (k contiguous), so nothing is transposed by hand.
 // Every input arrives by TMA (Q, K, dO, V tiles) or bulk copy (the S_0,
-// dS_C, delta and dX images the recompute and the reverse scan wrote).
+// dS_C, delta and dX images the recompute and the reverse scan wrote): the
+// images and the dO / V tiles as soon as batch 2 is done with the previous
+// pair's, the Q / K tiles once batch 3 and the dot products are.
 // Mq and Msym come from (a) and (b) by element-wise work on the CUDA cores
 // between the two MMA batches.
 constexpr int kBwdTcThreads = 256;  // warps w and w + 4 share TMEM lanes 32 (w & 3) ..
@@ -461,9 +466,9 @@ struct BwdTcSmem {
   static constexpr int kVec = kMA + 64 * 65 * 4;     // per-token vectors: 16 x 64 fp32
   static constexpr int kRed = kVec + 16 * 64 * 4;    // partials [4 lane quadrants][5][64] fp32
   static constexpr int kRow = kRed + 4 * 5 * 64 * 4;  // row-sum halves [2][3][64] fp32
-  static constexpr int kBar = kRow + 2 * 3 * 64 * 4;  // 4 mbarriers
-  static constexpr int kTmem = kBar + 32;
-  static constexpr int kBroken = kBar + 36;
+  static constexpr int kBar = kRow + 2 * 3 * 64 * 4;  // 5 mbarriers: qk, rest, m1, m2, m3
+  static constexpr int kTmem = kBar + 40;
+  static constexpr int kBroken = kBar + 44;
   static constexpr int kScal = kBar + 64;            // 16 fp32 scalars
   static constexpr int kBytes = kScal + 64 + 1024;   // + base alignment slack
 };
@@ -518,343 +523,430 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
                              const uint8_t *__restrict__ states_ws,
                              const uint8_t *__restrict__ dsc_ws,
                              const uint8_t *__restrict__ delta_ws,
-                             const uint8_t *__restrict__ dx_ws, float scale,
+                             const uint8_t *__restrict__ dx_ws, float scale, int npairs,
                              float *__restrict__ dq, float *__restrict__ dk,
                              float *__restrict__ da, float *__restrict__ db,
                              float *__restrict__ dgg_ws) {
   using SM = BwdTcSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_align<1024>(smem_raw);
-  // one CTA per (chunk, v-head), the v-head fastest: the eight CTAs of a
-  // chunk run side by side, so the two that add into the same dq / dk rows
-  // (the v-heads of one q/k head) and share its Q/K tiles meet in L2
-  const int g = static_cast<int>(blockIdx.x / kHV), hv = static_cast<int>(blockIdx.x % kHV);
-  const int hqk = hv >> 1;
-  if (meta[kMetaError] != 0 || g >= meta[kMetaChunks]) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int4 e = chunk_tab[g];
-  const int64_t t0 = e.z;
-  const int L = e.w;
-  GDN_DCHECK(e.x >= 0 && e.x < meta[kMetaN] && L > 0 && t0 + L <= meta[kMetaT]);
-  const int64_t soff = (static_cast<int64_t>(g) * kHV + hv) * kStateImgBytes;
-  const int64_t toff = (static_cast<int64_t>(g) * kHV + hv) * kTokImgBytes;
+  // Persistent: a cluster of two CTAs walks the pairs p = (chunk p / 4, q/k
+  // head p % 4), p = cluster, cluster + clusters, ...; rank r of the cluster
+  // takes v-head 2 hqk + r.  Both ranks walk the same pairs, so every cluster
+  // barrier below is reached by both or by neither.
+  const int crank = static_cast<int>(cluster_ctarank());
+  const int ncl = static_cast<int>(gridDim.x >> 1);
+  const int nchunks = meta[kMetaChunks];
+  const bool meta_ok = meta[kMetaError] == 0;
+  auto live = [&](int p) { return meta_ok && p < npairs && p / kHQK < nchunks; };
 
   float *VEC = reinterpret_cast<float *>(smem + SM::kVec);
   float *RED = reinterpret_cast<float *>(smem + SM::kRed);
   float *SC = reinterpret_cast<float *>(smem + SM::kScal);
   float *MA = reinterpret_cast<float *>(smem + SM::kMA);
+  float *ROW = reinterpret_cast<float *>(smem + SM::kRow);  // [hh][Wq | Wa | dbA][i]
   volatile int *broken = reinterpret_cast<volatile int *>(smem + SM::kBroken);
   auto vec = [&](int slot) { return VEC + slot * 64; };
   auto red = [&](int w, int f) { return RED + (w * 5 + f) * 64; };
   const uint32_t s_base = smem_u32(smem);
-  const uint32_t bar_tma = s_base + SM::kBar, bar_m1 = bar_tma + 8, bar_m2 = bar_tma + 16,
-                 bar_m3 = bar_tma + 24;
+  const uint32_t bar_qk = s_base + SM::kBar, bar_rest = bar_qk + 8, bar_m1 = bar_qk + 16,
+                 bar_m2 = bar_qk + 24, bar_m3 = bar_qk + 32;
 
-  // ---- TMA of the Q, K, dO and V tiles, bulk copies of the images; TMEM ----
+  // the copies of one pair's operands: the Q and K tiles (bar_qk); the dO and
+  // V tiles and the S_0, dS_C, delta and dX images (bar_rest)
+  auto issue_qk = [&](int hqk, int64_t t0) {
+    mbar_arrive_expect_tx(bar_qk, 32768);
+    for (int blk = 0; blk < 2; ++blk) {
+      const int y = static_cast<int>(t0);
+      tma_load_2d(s_base + SM::kQK + blk * 16384, &tmap_q, hqk * kD + 64 * blk, y, bar_qk);
+      tma_load_2d(s_base + SM::kQK + blk * 16384 + 8192, &tmap_k, hqk * kD + 64 * blk, y, bar_qk);
+    }
+  };
+  auto issue_rest = [&](int g, int hv, int64_t t0) {
+    const int64_t soff = (static_cast<int64_t>(g) * kHV + hv) * kStateImgBytes;
+    const int64_t toff = (static_cast<int64_t>(g) * kHV + hv) * kTokImgBytes;
+    mbar_arrive_expect_tx(bar_rest, 32768 + 2 * static_cast<uint32_t>(kStateImgBytes) +
+                                        2 * static_cast<uint32_t>(kTokImgBytes));
+    bulk_load(s_base + SM::kS0, states_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_rest);
+    bulk_load(s_base + SM::kDS, dsc_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_rest);
+    for (int blk = 0; blk < 2; ++blk) {
+      const int y = static_cast<int>(t0);
+      tma_load_2d(s_base + SM::kOX + blk * 16384, &tmap_do, hv * kD + 64 * blk, y, bar_rest);
+      tma_load_2d(s_base + SM::kDV + blk * 16384 + 8192, &tmap_v, hv * kD + 64 * blk, y, bar_rest);
+      bulk_load(s_base + SM::kOX + blk * 16384 + 8192, dx_ws + toff + blk * 8192, 8192, bar_rest);
+      bulk_load(s_base + SM::kDV + blk * 16384, delta_ws + toff + blk * 8192, 8192, bar_rest);
+    }
+  };
+  // gate inputs of the next pair, loaded a pair ahead into registers (token
+  // tid < 64; zero past the chunk's end)
+  float nx_g = 0.f, nx_b = 0.f, nx_gc = 0.f;
+  auto fetch_gates = [&](const int4 &en, int hvn) {
+    if (tid < 64) {
+      nx_gc = gcum_ws[(en.z + en.w - 1) * kHV + hvn];
+      nx_g = 0.f;
+      nx_b = 0.f;
+      if (tid < en.w) {
+        nx_g = gcum_ws[(en.z + tid) * kHV + hvn];
+        nx_b = beta_ws[(en.z + tid) * kHV + hvn];
+      }
+    }
+  };
+
+  // ---- TMEM, barriers and the first pair's copies ----
+  int p = static_cast<int>(blockIdx.x >> 1);
+  bool have = live(p);
+  int4 e = have ? chunk_tab[p / kHQK] : make_int4(0, 0, 0, 0);
   if (warp == 0) tmem_alloc(s_base + SM::kTmem, kTcCols);
   if (tid == 0) {
     *broken = 0;
-    for (int i = 0; i < 4; ++i) mbar_init(bar_tma + 8 * i, 1);
+    for (int i = 0; i < 5; ++i) mbar_init(bar_qk + 8 * i, 1);
     mbar_init_fence();
-    mbar_arrive_expect_tx(bar_tma, 65536 + 2 * static_cast<uint32_t>(kStateImgBytes) +
-                                       2 * static_cast<uint32_t>(kTokImgBytes));
-    bulk_load(s_base + SM::kS0, states_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_tma);
-    bulk_load(s_base + SM::kDS, dsc_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_tma);
-    for (int blk = 0; blk < 2; ++blk) {
-      const int y = static_cast<int>(t0);
-      tma_load_2d(s_base + SM::kQK + blk * 16384, &tmap_q, hqk * kD + 64 * blk, y, bar_tma);
-      tma_load_2d(s_base + SM::kQK + blk * 16384 + 8192, &tmap_k, hqk * kD + 64 * blk, y, bar_tma);
-      tma_load_2d(s_base + SM::kOX + blk * 16384, &tmap_do, hv * kD + 64 * blk, y, bar_tma);
-      tma_load_2d(s_base + SM::kDV + blk * 16384 + 8192, &tmap_v, hv * kD + 64 * blk, y, bar_tma);
-      bulk_load(s_base + SM::kOX + blk * 16384 + 8192, dx_ws + toff + blk * 8192, 8192, bar_tma);
-      bulk_load(s_base + SM::kDV + blk * 16384, delta_ws + toff + blk * 8192, 8192, bar_tma);
+    if (have) {
+      issue_qk(p % kHQK, e.z);
+      issue_rest(p / kHQK, 2 * (p % kHQK) + crank, e.z);
     }
   }
-  // ---- gates ----
-  if (tid < 64) {
-    const float gC = gcum_ws[(t0 + L - 1) * kHV + hv];
-    float gg = 0.f, eg = 0.f, bt = 0.f, ed = 0.f;
-    if (tid < L) {
-      gg = gcum_ws[(t0 + tid) * kHV + hv];
-      eg = expf(gg);
-      bt = beta_ws[(t0 + tid) * kHV + hv];
-      ed = expf(gC - gg);
-    }
-    vec(kVG)[tid] = gg;
-    vec(kVEG)[tid] = eg;
-    vec(kVBT)[tid] = bt;
-    vec(kVED)[tid] = ed;
-    if (tid == 0) SC[0] = expf(gC);
-  }
-  __syncthreads();
-
-  // ---- operands written by the threads (bf16, 128-byte swizzle) ----
-  // tiles and images landed; rows past the sequence end of the TMA tiles
-  // hold the next sequence's tokens: zero them (the images are zero there)
-  wait_phase(bar_tma, 0, broken);
-  {  // <dS_C, S_0> (the images share one layout)
-    float sds = 0.f;
-    for (int idx = tid; idx < static_cast<int>(kStateImgBytes / 16); idx += kBwdTcThreads) {
-      float x[8], y[8];
-      unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kS0 + 16 * idx), x);
-      unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kDS + 16 * idx), y);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) sds += x[u] * y[u];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sds += __shfl_xor_sync(0xffffffffu, sds, o);
-    if (lane == 0) SC[4 + warp] = sds;  // SC[4..11]
-  }
-  if (L < kChunk) {
-    const int nz = kChunk - L;
-    for (int idx = tid; idx < 8 * nz * 8; idx += kBwdTcThreads) {
-      const int ch = idx & 7, r = L + (idx >> 3) % nz, which = (idx >> 3) / nz;  // 0..7
-      const int base = which < 4   ? SM::kQK + (which >> 1) * 16384 + (which & 1) * 8192
-                       : which < 6 ? SM::kOX + (which - 4) * 16384
-                                   : SM::kDV + (which - 6) * 16384 + 8192;
-      *reinterpret_cast<uint4 *>(smem + base + r * 128 + ch * 16) = make_uint4(0u, 0u, 0u, 0u);
-    }
-  }
-  fence_async_smem();
+  if (have) fetch_gates(e, 2 * (p % kHQK) + crank);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + SM::kTmem);
-
-  // ---- MMA batch 1: (a), (b); batch 2: (c), (d), (e) ----
-  if (tid == 0) {
-    const uint32_t id_kk = umma_idesc_bf16(128, 64, false, false);
-    const uint32_t id_kk2 = umma_idesc_bf16(128, 128, false, false);
-    const uint32_t id_mn = umma_idesc_bf16(128, 64, true, false);
-    // one descriptor per layout, advanced by each operand's byte offset
-    const uint64_t dk16 = umma_desc_sw128(s_base, 16, 1024);      // K-major
-    const uint64_t dmn16k = umma_desc_sw128(s_base, 16384, 1024);  // MN-major, 16 KB between blocks
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-      umma_bf16(tmem + kTcA, umma_desc_advance(dk16, SM::kQK + off),
-                umma_desc_advance(dk16, SM::kQK + 8192 + off), id_kk, ks > 0);
-      umma_bf16(tmem + kTcB, umma_desc_advance(dk16, SM::kOX + off),
-                umma_desc_advance(dk16, SM::kDV + off), id_kk2, ks > 0);
-    }
-    umma_commit(bar_m1);
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {  // K = v, 16 rows of the MN-major tiles per step
-      const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-      const uint64_t s0 = umma_desc_advance(dmn16k, SM::kS0 + ks * 2048);
-      umma_bf16(tmem + kTcP1, s0, umma_desc_advance(dk16, SM::kOX + off), id_mn, ks > 0);
-      umma_bf16(tmem + kTcP2, s0, umma_desc_advance(dk16, SM::kOX + 8192 + off), id_mn, ks > 0);
-      umma_bf16(tmem + kTcP3, umma_desc_advance(dmn16k, SM::kDS + ks * 2048),
-                umma_desc_advance(dk16, SM::kDV + off), id_mn, ks > 0);
-    }
-    umma_commit(bar_m2);
-  }
-
-  // ---- Mq, Ma and their gate terms: row i = TMEM lane, columns 32 hh.. ----
-  wait_phase(bar_m1, 0, broken);
-  tc_fence_after();
   const int quad = warp & 3, hh = warp >> 2;
   const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-  float *ROW = reinterpret_cast<float *>(smem + SM::kRow);  // [hh][Wq | Wa | dbA][i]
-  {
-    const bool qside = quad < 2;  // lanes 0-63: QK, dO.delta; lanes 64-127: KK, dX.delta
-    const int i = 32 * (quad & 1) + lane;
-    const float gi = vec(kVG)[i], bi = vec(kVBT)[i];
-    float rsum = 0.f, dba = 0.f;
-    float m[32], w[32];
-    tmem_ld32(tl + kTcA + 32 * hh, m);  // QK or KK
-    tmem_ld32(tl + kTcB + 32 * hh, w);  // dO.delta or dX.delta
-    tmem_wait_ld();
+  const int kk = 32 * quad + lane;  // k index of this thread's TMEM lane (dots, dq, dk)
+
+  uint32_t par = 0;  // each of the five barriers completes once per pair
+  while (have) {
+    const int g = p / kHQK, hqk = p % kHQK, hv = 2 * hqk + crank;
+    const int64_t t0 = e.z;
+    const int L = e.w;
+    GDN_DCHECK(e.x >= 0 && e.x < meta[kMetaN] && L > 0 && t0 + L <= meta[kMetaT]);
+    const int pn = p + ncl;
+    const bool have_n = live(pn);
+    const int4 en = have_n ? chunk_tab[pn / kHQK] : make_int4(0, 0, 0, 0);
+    const int hv_n = 2 * (pn % kHQK) + crank;
+
+    // ---- gates (inputs fetched a pair ahead) ----
+    if (tid < 64) {
+      const float gg = nx_g, bt = nx_b;
+      vec(kVG)[tid] = gg;
+      vec(kVEG)[tid] = tid < L ? expf(gg) : 0.f;
+      vec(kVBT)[tid] = bt;
+      vec(kVED)[tid] = tid < L ? expf(nx_gc - gg) : 0.f;
+      if (tid == 0) SC[0] = expf(nx_gc);
+    }
+    __syncthreads();
+
+    // ---- operands written by the threads (bf16, 128-byte swizzle) ----
+    // tiles and images landed; rows past the sequence end of the TMA tiles
+    // hold the next sequence's tokens: zero them (the images are zero there)
+    wait_phase(bar_qk, par, broken);
+    wait_phase(bar_rest, par, broken);
+    {  // <dS_C, S_0> (the images share one layout)
+      float sds = 0.f;
+      for (int idx = tid; idx < static_cast<int>(kStateImgBytes / 16); idx += kBwdTcThreads) {
+        float x[8], y[8];
+        unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kS0 + 16 * idx), x);
+        unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kDS + 16 * idx), y);
 #pragma unroll
-    for (int u = 0; u < 32; ++u) {
-      const int j = 32 * hh + u;
-      const float dec = expf(gi - vec(kVG)[j]);
-      float x;
-      if (qside) {
-        x = (i < L && j <= i) ? scale * dec * w[u] : 0.f;  // Mq
+        for (int u = 0; u < 8; ++u) sds += x[u] * y[u];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sds += __shfl_xor_sync(0xffffffffu, sds, o);
+      if (lane == 0) SC[4 + warp] = sds;  // SC[4..11]
+    }
+    if (L < kChunk) {
+      const int nz = kChunk - L;
+      for (int idx = tid; idx < 8 * nz * 8; idx += kBwdTcThreads) {
+        const int ch = idx & 7, r = L + (idx >> 3) % nz, which = (idx >> 3) / nz;  // 0..7
+        const int base = which < 4   ? SM::kQK + (which >> 1) * 16384 + (which & 1) * 8192
+                         : which < 6 ? SM::kOX + (which - 4) * 16384
+                                     : SM::kDV + (which - 6) * 16384 + 8192;
+        *reinterpret_cast<uint4 *>(smem + base + r * 128 + ch * 16) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    // ---- MMA batch 1: (a), (b); batch 2: (c), (d), (e) ----
+    if (tid == 0) {
+      const uint32_t id_kk = umma_idesc_bf16(128, 64, false, false);
+      const uint32_t id_kk2 = umma_idesc_bf16(128, 128, false, false);
+      const uint32_t id_mn = umma_idesc_bf16(128, 64, true, false);
+      // one descriptor per layout, advanced by each operand's byte offset
+      const uint64_t dk16 = umma_desc_sw128(s_base, 16, 1024);      // K-major
+      const uint64_t dmn16k = umma_desc_sw128(s_base, 16384, 1024);  // MN-major, 16 KB between blocks
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+        umma_bf16(tmem + kTcA, umma_desc_advance(dk16, SM::kQK + off),
+                  umma_desc_advance(dk16, SM::kQK + 8192 + off), id_kk, ks > 0);
+        umma_bf16(tmem + kTcB, umma_desc_advance(dk16, SM::kOX + off),
+                  umma_desc_advance(dk16, SM::kDV + off), id_kk2, ks > 0);
+      }
+      umma_commit(bar_m1);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {  // K = v, 16 rows of the MN-major tiles per step
+        const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+        const uint64_t s0 = umma_desc_advance(dmn16k, SM::kS0 + ks * 2048);
+        umma_bf16(tmem + kTcP1, s0, umma_desc_advance(dk16, SM::kOX + off), id_mn, ks > 0);
+        umma_bf16(tmem + kTcP2, s0, umma_desc_advance(dk16, SM::kOX + 8192 + off), id_mn, ks > 0);
+        umma_bf16(tmem + kTcP3, umma_desc_advance(dmn16k, SM::kDS + ks * 2048),
+                  umma_desc_advance(dk16, SM::kDV + off), id_mn, ks > 0);
+      }
+      umma_commit(bar_m2);
+    }
+
+    // ---- Mq, Ma and their gate terms: row i = TMEM lane, columns 32 hh.. ----
+    wait_phase(bar_m1, par, broken);
+    tc_fence_after();
+    {
+      const bool qside = quad < 2;  // lanes 0-63: QK, dO.delta; lanes 64-127: KK, dX.delta
+      const int i = 32 * (quad & 1) + lane;
+      const float gi = vec(kVG)[i], bi = vec(kVBT)[i];
+      float rsum = 0.f, dba = 0.f;
+      float m[32], w[32];
+      tmem_ld32(tl + kTcA + 32 * hh, m);  // QK or KK
+      tmem_ld32(tl + kTcB + 32 * hh, w);  // dO.delta or dX.delta
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int j = 32 * hh + u;
+        const float dec = expf(gi - vec(kVG)[j]);
+        float x;
+        if (qside) {
+          x = (i < L && j <= i) ? scale * dec * w[u] : 0.f;  // Mq
+        } else {
+          const float dA = -w[u];
+          x = (i < L && j < i) ? dA * bi * dec : 0.f;  // Ma
+          if (i < L && j < i) dba += dA * dec * m[u];
+          MA[i * 65 + j] = x;
+        }
+        w[u] = x;
+        m[u] *= x;  // W = M o (QK or KK)
+        rsum += m[u];
+      }
+      if (qside) {  // row i of Mq, columns 32 hh .. 32 hh + 31, as bf16
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          *reinterpret_cast<uint4 *>(smem + SM::kMQ + i * 128 + (((4 * hh + cc) ^ i) & 7) * 16) =
+              make_uint4(pack_bf16x2(w[8 * cc], w[8 * cc + 1]), pack_bf16x2(w[8 * cc + 2], w[8 * cc + 3]),
+                         pack_bf16x2(w[8 * cc + 4], w[8 * cc + 5]),
+                         pack_bf16x2(w[8 * cc + 6], w[8 * cc + 7]));
+        ROW[(hh * 3 + 0) * 64 + i] = rsum;
       } else {
-        const float dA = -w[u];
-        x = (i < L && j < i) ? dA * bi * dec : 0.f;  // Ma
-        if (i < L && j < i) dba += dA * dec * m[u];
-        MA[i * 65 + j] = x;
+        ROW[(hh * 3 + 1) * 64 + i] = rsum;
+        ROW[(hh * 3 + 2) * 64 + i] = dba;
+        if (hh == (quad & 1)) {  // dX_i . v_i sits in this column half
+          float x[32];
+          tmem_ld32(tl + kTcB + 64 + 32 * hh, x);
+          tmem_wait_ld();
+          float d = 0.f;
+#pragma unroll
+          for (int u = 0; u < 32; ++u) d = u == lane ? x[u] : d;
+          vec(kVDXv)[i] = i < L ? d : 0.f;
+        }
       }
-      w[u] = x;
-      m[u] *= x;  // W = M o (QK or KK)
-      rsum += m[u];
+      const float cs = warp_transpose_sum32(m, lane);  // column 32 hh + lane over these 32 rows
+      red(quad, qside ? kRedColWq : kRedColWa)[32 * hh + lane] = cs;
     }
-    if (qside) {  // row i of Mq, columns 32 hh .. 32 hh + 31, as bf16
+    __syncthreads();
+    {  // Msym = Ma + Ma^T: row i = tid & 63, 16 columns per thread
+      const int i = tid & 63, q4 = tid >> 6;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc)
-        *reinterpret_cast<uint4 *>(smem + SM::kMQ + i * 128 + (((4 * hh + cc) ^ i) & 7) * 16) =
-            make_uint4(pack_bf16x2(w[8 * cc], w[8 * cc + 1]), pack_bf16x2(w[8 * cc + 2], w[8 * cc + 3]),
-                       pack_bf16x2(w[8 * cc + 4], w[8 * cc + 5]),
-                       pack_bf16x2(w[8 * cc + 6], w[8 * cc + 7]));
-      ROW[(hh * 3 + 0) * 64 + i] = rsum;
-    } else {
-      ROW[(hh * 3 + 1) * 64 + i] = rsum;
-      ROW[(hh * 3 + 2) * 64 + i] = dba;
-      if (hh == (quad & 1)) {  // dX_i . v_i sits in this column half
-        float x[32];
-        tmem_ld32(tl + kTcB + 64 + 32 * hh, x);
-        tmem_wait_ld();
-        float d = 0.f;
+      for (int cc = 2 * q4; cc < 2 * q4 + 2; ++cc) {
+        float x[8];
 #pragma unroll
-        for (int u = 0; u < 32; ++u) d = u == lane ? x[u] : d;
-        vec(kVDXv)[i] = i < L ? d : 0.f;
+        for (int u = 0; u < 8; ++u) {
+          const int j = 8 * cc + u;
+          x[u] = MA[i * 65 + j] + MA[j * 65 + i];
+        }
+        *reinterpret_cast<uint4 *>(smem + SM::kMS + i * 128 + ((cc ^ i) & 7) * 16) =
+            make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
+                       pack_bf16x2(x[6], x[7]));
       }
     }
-    const float cs = warp_transpose_sum32(m, lane);  // column 32 hh + lane over these 32 rows
-    red(quad, qside ? kRedColWq : kRedColWa)[32 * hh + lane] = cs;
-  }
-  __syncthreads();
-  {  // Msym = Ma + Ma^T: row i = tid & 63, 16 columns per thread
-    const int i = tid & 63, q4 = tid >> 6;
-#pragma unroll
-    for (int cc = 2 * q4; cc < 2 * q4 + 2; ++cc) {
-      float x[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = 8 * cc + u;
-        x[u] = MA[i * 65 + j] + MA[j * 65 + i];
-      }
-      *reinterpret_cast<uint4 *>(smem + SM::kMS + i * 128 + ((cc ^ i) & 7) * 16) =
-          make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
-                     pack_bf16x2(x[6], x[7]));
-    }
-  }
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 
-  // ---- MMA batch 3: (f) K^T Mq^T; (g) Q^T Mq, (h) + K^T Msym ----
-  if (tid == 0) {
-    const uint32_t id_f = umma_idesc_bf16(128, 64, true, false);
-    const uint32_t id_g = umma_idesc_bf16(128, 64, true, true);
-    const uint64_t dk16 = umma_desc_sw128(s_base, 16, 1024);
-    const uint64_t dmn16k = umma_desc_sw128(s_base, 16384, 1024);
-    const uint64_t dmn8k = umma_desc_sw128(s_base, 8192, 1024);
+    // ---- MMA batch 3: (f) K^T Mq^T; (g) Q^T Mq, (h) + K^T Msym ----
+    if (tid == 0) {
+      const uint32_t id_f = umma_idesc_bf16(128, 64, true, false);
+      const uint32_t id_g = umma_idesc_bf16(128, 64, true, true);
+      const uint64_t dk16 = umma_desc_sw128(s_base, 16, 1024);
+      const uint64_t dmn16k = umma_desc_sw128(s_base, 16384, 1024);
+      const uint64_t dmn8k = umma_desc_sw128(s_base, 8192, 1024);
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {  // K = 64 tokens
-      const uint64_t kt = umma_desc_advance(dmn16k, SM::kQK + 8192 + ks * 2048);
-      const uint64_t qt = umma_desc_advance(dmn16k, SM::kQK + ks * 2048);
-      umma_bf16(tmem + kTcF, kt, umma_desc_advance(dk16, SM::kMQ + ks * 32), id_f, ks > 0);
-      umma_bf16(tmem + kTcGH, qt, umma_desc_advance(dmn8k, SM::kMQ + ks * 2048), id_g, ks > 0);
+      for (int ks = 0; ks < 4; ++ks) {  // K = 64 tokens
+        const uint64_t kt = umma_desc_advance(dmn16k, SM::kQK + 8192 + ks * 2048);
+        const uint64_t qt = umma_desc_advance(dmn16k, SM::kQK + ks * 2048);
+        umma_bf16(tmem + kTcF, kt, umma_desc_advance(dk16, SM::kMQ + ks * 32), id_f, ks > 0);
+        umma_bf16(tmem + kTcGH, qt, umma_desc_advance(dmn8k, SM::kMQ + ks * 2048), id_g, ks > 0);
+      }
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + kTcGH, umma_desc_advance(dmn16k, SM::kQK + 8192 + ks * 2048),
+                  umma_desc_advance(dk16, SM::kMS + ks * 32), id_f, 1);
+      umma_commit(bar_m3);
     }
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks)
-      umma_bf16(tmem + kTcGH, umma_desc_advance(dmn16k, SM::kQK + 8192 + ks * 2048),
-                umma_desc_advance(dk16, SM::kMS + ks * 32), id_f, 1);
-    umma_commit(bar_m3);
-  }
 
-  // ---- per-token dot products with q and k: thread = k (TMEM lane), tokens 32 hh.. ----
-  wait_phase(bar_m2, 0, broken);
-  tc_fence_after();
-  const int kk = 32 * quad + lane;  // k index of this thread's TMEM lane
-  const uint8_t *qtile = smem + SM::kQK + (kk >> 6) * 16384;
-  const uint8_t *ktile = qtile + 8192;
+    // ---- per-token dot products with q and k: thread = k (TMEM lane), tokens 32 hh.. ----
+    wait_phase(bar_m2, par, broken);
+    tc_fence_after();
+    // batch 2 is done: S_0, dS_C, [dO;dX] and [delta;V] are no longer read,
+    // so the next pair's copies go there now and land while this pair runs
+    if (have_n) {
+      if (tid == 0) issue_rest(pn / kHQK, hv_n, en.z);
+      fetch_gates(en, hv_n);
+    }
+    {
+      const uint8_t *qtile = smem + SM::kQK + (kk >> 6) * 16384;
+      const uint8_t *ktile = qtile + 8192;
 #pragma unroll 1
-  for (int f = 0; f < 3; ++f) {
-    const uint32_t col = f == 0 ? kTcP1 : (f == 1 ? kTcP2 : kTcP3);
-    const uint8_t *tile = f == 0 ? qtile : ktile;
-    float x[32];
-    tmem_ld32(tl + col + 32 * hh, x);
-    tmem_wait_ld();
+      for (int f = 0; f < 3; ++f) {
+        const uint32_t col = f == 0 ? kTcP1 : (f == 1 ? kTcP2 : kTcP3);
+        const uint8_t *tile = f == 0 ? qtile : ktile;
+        float x[32];
+        tmem_ld32(tl + col + 32 * hh, x);
+        tmem_wait_ld();
 #pragma unroll
-    for (int u = 0; u < 32; ++u) x[u] *= tile_at(tile, 32 * hh + u, kk & 63);
-    red(quad, f)[32 * hh + lane] = warp_transpose_sum32(x, lane);
-  }
+        for (int u = 0; u < 32; ++u) x[u] *= tile_at(tile, 32 * hh + u, kk & 63);
+        red(quad, f)[32 * hh + lane] = warp_transpose_sum32(x, lane);
+      }
+    }
 
-  // ---- dq, dk ----
-  wait_phase(bar_m3, 0, broken);
-  tc_fence_after();
-  {
-    const float *EG = vec(kVEG), *BT = vec(kVBT), *ED = vec(kVED);
-    float p[32], f[32], p3[32];
-    tmem_ld32(tl + kTcP1 + 32 * hh, p);
-    tmem_ld32(tl + kTcF + 32 * hh, f);
-    tmem_wait_ld();
+    // ---- dq, dk ----
+    // The two v-heads of q/k head hqk (this cluster's two CTAs) both add to
+    // its dq and dk rows: rank 0 writes the dq rows and rank 1 the dk rows,
+    // each adding the partner's contribution, which arrives through
+    // distributed shared memory in the retired Mq / Msym / Ma area ([64 t]
+    // [128 k] fp32).  One fp32 sum of two terms per element: the result does
+    // not depend on which CTA got there first, and no zeroing pass or
+    // read-modify-write of dq / dk in DRAM is needed.
+    wait_phase(bar_m3, par, broken);
+    tc_fence_after();
+    {
+      const float *EG = vec(kVEG), *BT = vec(kVBT), *ED = vec(kVED);
+      float vq[32], vk[32];
+      {
+        float pp[32], f[32];
+        tmem_ld32(tl + kTcP1 + 32 * hh, pp);
+        tmem_ld32(tl + kTcF + 32 * hh, f);
+        tmem_wait_ld();
 #pragma unroll
-    for (int u = 0; u < 32; ++u) {
-      const int t = 32 * hh + u;
-      if (t < L) atomicAdd(dq + ((t0 + t) * kHQK + hqk) * kD + kk, scale * EG[t] * p[u] + f[u]);
-    }
-    tmem_ld32(tl + kTcP2 + 32 * hh, p);
-    tmem_ld32(tl + kTcGH + 32 * hh, f);
-    tmem_ld32(tl + kTcP3 + 32 * hh, p3);
-    tmem_wait_ld();
+        for (int u = 0; u < 32; ++u) vq[u] = scale * EG[32 * hh + u] * pp[u] + f[u];
+      }
+      {
+        float pp[32], f[32], p3[32];
+        tmem_ld32(tl + kTcP2 + 32 * hh, pp);
+        tmem_ld32(tl + kTcGH + 32 * hh, f);
+        tmem_ld32(tl + kTcP3 + 32 * hh, p3);
+        tmem_wait_ld();
 #pragma unroll
-    for (int u = 0; u < 32; ++u) {
-      const int t = 32 * hh + u;
-      if (t < L)
-        atomicAdd(dk + ((t0 + t) * kHQK + hqk) * kD + kk,
-                  f[u] - BT[t] * EG[t] * p[u] + ED[t] * p3[u]);
+        for (int u = 0; u < 32; ++u) {
+          const int t = 32 * hh + u;
+          vk[u] = f[u] - BT[t] * EG[t] * pp[u] + ED[t] * p3[u];
+        }
+      }
+      // both CTAs are past batch 3, the Msym pass and the dot products: the
+      // exchange area is free in both, and this CTA's Q/K tiles are retired
+      cluster_arrive();
+      cluster_wait();
+      if (have_n && tid == 0) issue_qk(pn % kHQK, en.z);
+      const uint32_t rx = dsmem_map(s_base + SM::kMQ, static_cast<uint32_t>(crank ^ 1));
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const uint32_t o = static_cast<uint32_t>(((32 * hh + u) * kD + kk) * 4);
+        dsmem_st_f32(rx + o, crank ? vq[u] : vk[u]);
+      }
+      cluster_arrive();
+      cluster_wait();  // the partner's values have landed
+      const float *X = reinterpret_cast<const float *>(smem + SM::kMQ);
+      float *dst = crank ? dk : dq;
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int t = 32 * hh + u;
+        if (t < L)
+          dst[((t0 + t) * kHQK + hqk) * kD + kk] = (crank ? vk[u] : vq[u]) + X[t * kD + kk];
+      }
     }
+
+    // ---- gate gradients (tokens t = tid < 64, two warps) ----
+    float dG = 0.f, dB = 0.f, ez = 0.f;
+    if (tid < 64) {
+      const int t = tid;
+      float rho = 0.f, xi = 0.f, zeta = 0.f;
+      for (int q = 0; q < 4; ++q) {
+        rho += red(q, kRedRho)[t];
+        xi += red(q, kRedXi)[t];
+        zeta += red(q, kRedZeta)[t];
+      }
+      const float colwq = red(0, kRedColWq)[t] + red(1, kRedColWq)[t];
+      const float colwa = red(2, kRedColWa)[t] + red(3, kRedColWa)[t];
+      const float rowwq = ROW[0 * 64 + t] + ROW[3 * 64 + t];
+      const float rowwa = ROW[1 * 64 + t] + ROW[4 * 64 + t];
+      const float dba = ROW[2 * 64 + t] + ROW[5 * 64 + t];
+      const float eg = vec(kVEG)[t], bt = vec(kVBT)[t], ed = vec(kVED)[t];
+      if (t < L) {
+        dB = vec(kVDXv)[t] - eg * xi + dba;
+        dG = scale * eg * rho + rowwq - colwq + rowwa - colwa - bt * eg * xi - ed * zeta;
+        ez = ed * zeta;  // the chunk-end state depends on G_C through every token
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ez += __shfl_xor_sync(0xffffffffu, ez, o);
+      if (lane == 0) SC[12 + warp] = ez;
+    }
+    __syncthreads();
+    if (tid < 64) {
+      const int t = tid;
+      if (t == L - 1) {
+        float sds = 0.f;  // <dS_C, S_0>, eight warp partials in a fixed order
+        for (int w8 = 0; w8 < 8; ++w8) sds += SC[4 + w8];
+        dG += SC[0] * sds + SC[12] + SC[13];
+      }
+      // dg_t = sum_{s >= t} dG_s: suffix scan within each warp, then warp 1's total into warp 0
+      float x = dG;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_down_sync(0xffffffffu, x, o);
+        if (lane + o < 32) x += y;
+      }
+      if (t == 32) SC[14] = x;  // total of tokens 32..63
+      vec(kVDG)[t] = x;
+    }
+    __syncthreads();
+    if (tid < L) {
+      const int t = tid;
+      const float dg = vec(kVDG)[t] + (t < 32 ? SC[14] : 0.f);
+      const int64_t idx = (t0 + t) * kHV + hv;
+      const float x = bf16_to_f32(a[idx]) + dt_bias[hv];
+      const float ea = expf(A_log[hv]);
+      const float sig = 1.0f / (1.0f + expf(-x));  // d softplus / dx
+      const float gt = -ea * softplus_stable(x);
+      const float bt = vec(kVBT)[t];
+      da[idx] = -dg * ea * sig;
+      db[idx] = dB * bt * (1.0f - bt);
+      dgg_ws[idx] = dg * gt;
+    }
+    // the next pair overwrites the gate vectors, the partial sums and TMEM
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    p = pn;
+    e = en;
+    have = have_n;
+    par ^= 1u;
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTcCols);
-  }
-
-  // ---- gate gradients (tokens t = tid < 64, two warps) ----
-  float dG = 0.f, dB = 0.f, ez = 0.f;
-  if (tid < 64) {
-    const int t = tid;
-    float rho = 0.f, xi = 0.f, zeta = 0.f;
-    for (int q = 0; q < 4; ++q) {
-      rho += red(q, kRedRho)[t];
-      xi += red(q, kRedXi)[t];
-      zeta += red(q, kRedZeta)[t];
-    }
-    const float colwq = red(0, kRedColWq)[t] + red(1, kRedColWq)[t];
-    const float colwa = red(2, kRedColWa)[t] + red(3, kRedColWa)[t];
-    const float rowwq = ROW[0 * 64 + t] + ROW[3 * 64 + t];
-    const float rowwa = ROW[1 * 64 + t] + ROW[4 * 64 + t];
-    const float dba = ROW[2 * 64 + t] + ROW[5 * 64 + t];
-    const float eg = vec(kVEG)[t], bt = vec(kVBT)[t], ed = vec(kVED)[t];
-    if (t < L) {
-      dB = vec(kVDXv)[t] - eg * xi + dba;
-      dG = scale * eg * rho + rowwq - colwq + rowwa - colwa - bt * eg * xi - ed * zeta;
-      ez = ed * zeta;  // the chunk-end state depends on G_C through every token
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ez += __shfl_xor_sync(0xffffffffu, ez, o);
-    if (lane == 0) SC[12 + warp] = ez;
-  }
-  __syncthreads();
-  if (tid < 64) {
-    const int t = tid;
-    if (t == L - 1) {
-      float sds = 0.f;  // <dS_C, S_0>, eight warp partials in a fixed order
-      for (int w = 0; w < 8; ++w) sds += SC[4 + w];
-      dG += SC[0] * sds + SC[12] + SC[13];
-    }
-    // dg_t = sum_{s >= t} dG_s: suffix scan within each warp, then warp 1's total into warp 0
-    float x = dG;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_down_sync(0xffffffffu, x, o);
-      if (lane + o < 32) x += y;
-    }
-    if (t == 32) SC[14] = x;  // total of tokens 32..63
-    vec(kVDG)[t] = x;
-  }
-  __syncthreads();
-  if (tid < L) {
-    const int t = tid;
-    const float dg = vec(kVDG)[t] + (t < 32 ? SC[14] : 0.f);
-    const int64_t idx = (t0 + t) * kHV + hv;
-    const float x = bf16_to_f32(a[idx]) + dt_bias[hv];
-    const float ea = expf(A_log[hv]);
-    const float sig = 1.0f / (1.0f + expf(-x));  // d softplus / dx
-    const float gt = -ea * softplus_stable(x);
-    const float bt = vec(kVBT)[t];
-    da[idx] = -dg * ea * sig;
-    db[idx] = dB * bt * (1.0f - bt);
-    dgg_ws[idx] = dg * gt;
   }
 }
 
@@ -942,6 +1034,27 @@ gdn_prefill_bwd_reduce_kernel(const float *__restrict__ red, float *__restrict__
 // ---------------------------------------------------------------------------
 int prefill_bwd_kernel_launches() { return 7; }
 
+// Clusters of the chunk kernel that are resident at once on this device (one
+// CTA per SM, two SMs of a GPC per cluster), queried once per device.
+static cudaError_t bwd_chunk_clusters(cudaLaunchConfig_t cfg, int *out) {
+  static int cache[64];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) {
+    *out = cache[dev];
+    return cudaSuccess;
+  }
+  cfg.gridDim = dim3(2);
+  int n = 0;
+  err = cudaOccupancyMaxActiveClusters(&n, gdn_prefill_bwd_chunk_kernel, &cfg);
+  if (err != cudaSuccess) return err;
+  if (n < 1) return cudaErrorInvalidConfiguration;
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  *out = n;
+  return cudaSuccess;
+}
+
 cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, const float *state,
                                const float *A_log, const void *a, const float *dt_bias,
                                const void *b, const int64_t *cu_seqlens, int64_t N, int64_t T,
@@ -979,12 +1092,6 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
       return cudaErrorInvalidValue;
   }
   cudaError_t err;
-  if (T > 0) {
-    err = cudaMemsetAsync(dq, 0, static_cast<size_t>(T) * kHQK * kD * sizeof(float), stream);
-    if (err != cudaSuccess) return err;
-    err = cudaMemsetAsync(dk, 0, static_cast<size_t>(T) * kHQK * kD * sizeof(float), stream);
-    if (err != cudaSuccess) return err;
-  }
 
   // recompute: tables, gates and [P Ainv ; Ainv], then the scan saving S_0 and delta
   gdn_prefill_meta_kernel<<<1, kMetaThreads, 0, stream>>>(
@@ -1029,17 +1136,31 @@ cudaError_t launch_prefill_bwd(const void *q, const void *k, const void *v, cons
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
 
-  // chunk-parallel gradients
+  // chunk-parallel gradients: persistent clusters of two CTAs, as many as fit
   if (f.nt_max > 0 && T > 0) {
     const CUtensorMap &tvs = tv;  // V with 128-byte swizzle, 64-wide boxes
     err = cudaFuncSetAttribute(gdn_prefill_bwd_chunk_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, BwdTcSmem::kBytes);
     if (err != cudaSuccess) return err;
-    const unsigned grid = static_cast<unsigned>(f.nt_max * kHV);
-    gdn_prefill_bwd_chunk_kernel<<<grid, kBwdTcThreads, BwdTcSmem::kBytes, stream>>>(
-        tq, tk, tdo, tvs, A_log, static_cast<const uint16_t *>(a), dt_bias, cu_seqlens, meta,
-        chunk_tab, gcum, beta, states, dsc, delta, dx, scale, dq, dk, da, db, dgg);
-    err = cudaGetLastError();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kBwdTcThreads);
+    cfg.dynamicSmemBytes = BwdTcSmem::kBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    err = bwd_chunk_clusters(cfg, &clusters);
+    if (err != cudaSuccess) return err;
+    const int npairs = static_cast<int>(f.nt_max * kHQK);
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * (clusters < npairs ? clusters : npairs)));
+    err = cudaLaunchKernelEx(&cfg, gdn_prefill_bwd_chunk_kernel, tq, tk, tdo, tvs, A_log,
+                             static_cast<const uint16_t *>(a), dt_bias, cu_seqlens, meta, chunk_tab,
+                             gcum, beta, states, dsc, delta, dx, scale, npairs, dq, dk, da, db, dgg);
     if (err != cudaSuccess) return err;
   }
   float *red = reinterpret_cast<float *>(ws + w.red);
