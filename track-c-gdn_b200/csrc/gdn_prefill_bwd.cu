@@ -466,9 +466,10 @@ struct BwdTcSmem {
   static constexpr int kVec = kMA + 64 * 65 * 4;     // per-token vectors: 16 x 64 fp32
   static constexpr int kRed = kVec + 16 * 64 * 4;    // partials [4 lane quadrants][5][64] fp32
   static constexpr int kRow = kRed + 4 * 5 * 64 * 4;  // row-sum halves [2][3][64] fp32
-  static constexpr int kBar = kRow + 2 * 3 * 64 * 4;  // 5 mbarriers: qk, rest, m1, m2, m3
-  static constexpr int kTmem = kBar + 40;
-  static constexpr int kBroken = kBar + 44;
+  // 7 mbarriers: qk, rest, m1, m2, m3, xfree, xfull
+  static constexpr int kBar = kRow + 2 * 3 * 64 * 4;
+  static constexpr int kTmem = kBar + 56;
+  static constexpr int kBroken = kBar + 60;
   static constexpr int kScal = kBar + 64;            // 16 fp32 scalars
   static constexpr int kBytes = kScal + 64 + 1024;   // + base alignment slack
 };
@@ -552,6 +553,10 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar_qk = s_base + SM::kBar, bar_rest = bar_qk + 8, bar_m1 = bar_qk + 16,
                  bar_m2 = bar_qk + 24, bar_m3 = bar_qk + 32;
+  // the dq / dk exchange: the partner arrives on xfree when its exchange area
+  // may be written; its stores into this CTA's area complete on xfull
+  const uint32_t bar_xfree = bar_qk + 40, bar_xfull = bar_qk + 48;
+  const uint32_t peer = static_cast<uint32_t>(crank ^ 1);
 
   // the copies of one pair's operands: the Q and K tiles (bar_qk); the dO and
   // V tiles and the S_0, dS_C, delta and dX images (bar_rest)
@@ -600,7 +605,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   if (warp == 0) tmem_alloc(s_base + SM::kTmem, kTcCols);
   if (tid == 0) {
     *broken = 0;
-    for (int i = 0; i < 5; ++i) mbar_init(bar_qk + 8 * i, 1);
+    for (int i = 0; i < 7; ++i) mbar_init(bar_qk + 8 * i, 1);
     mbar_init_fence();
     if (have) {
       issue_qk(p % kHQK, e.z);
@@ -611,14 +616,17 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // both CTAs' barriers are initialised before either signals the other
+  cluster_arrive();
+  cluster_wait();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + SM::kTmem);
   const int quad = warp & 3, hh = warp >> 2;
   const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
   const int kk = 32 * quad + lane;  // k index of this thread's TMEM lane (dots, dq, dk)
 
-  uint32_t par = 0;  // each of the five barriers completes once per pair
+  uint32_t par = 0;  // each of the seven barriers completes once per pair
   while (have) {
-    const int g = p / kHQK, hqk = p % kHQK, hv = 2 * hqk + crank;
+    const int hqk = p % kHQK, hv = 2 * hqk + crank;
     const int64_t t0 = e.z;
     const int L = e.w;
     GDN_DCHECK(e.x >= 0 && e.x < meta[kMetaN] && L > 0 && t0 + L <= meta[kMetaT]);
@@ -627,6 +635,8 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const int4 en = have_n ? chunk_tab[pn / kHQK] : make_int4(0, 0, 0, 0);
     const int hv_n = 2 * (pn % kHQK) + crank;
 
+    // the partner's 32 KB of dq / dk values for this pair land on xfull
+    if (tid == 0) mbar_arrive_expect_tx(bar_xfull, 32768);
     // ---- gates (inputs fetched a pair ahead) ----
     if (tid < 64) {
       const float gg = nx_g, bt = nx_b;
@@ -823,16 +833,19 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // ---- dq, dk ----
     // The two v-heads of q/k head hqk (this cluster's two CTAs) both add to
     // its dq and dk rows: rank 0 writes the dq rows and rank 1 the dk rows,
-    // each adding the partner's contribution, which arrives through
-    // distributed shared memory in the retired Mq / Msym / Ma area ([64 t]
-    // [128 k] fp32).  One fp32 sum of two terms per element: the result does
-    // not depend on which CTA got there first, and no zeroing pass or
-    // read-modify-write of dq / dk in DRAM is needed.
+    // each adding the partner's contribution, which arrives by asynchronous
+    // stores into the retired Mq / Msym / Ma area as [128 k][64 t] fp32 (the
+    // 16-byte chunk t / 4 of row k at chunk (t / 4) ^ (k & 7): conflict-free
+    // for the 16-byte accesses of consecutive k).  One fp32 sum of two terms
+    // per element: the result does not depend on which CTA got there first,
+    // and no zeroing pass or read-modify-write of dq / dk in DRAM is needed.
     wait_phase(bar_m3, par, broken);
     tc_fence_after();
+    // batch 3 and the Msym pass are done: this CTA's exchange area is free
+    if (tid == 0) mbar_arrive_cluster(dsmem_map(bar_xfree, peer));
+    float vq[32], vk[32];
     {
       const float *EG = vec(kVEG), *BT = vec(kVBT), *ED = vec(kVED);
-      float vq[32], vk[32];
       {
         float pp[32], f[32];
         tmem_ld32(tl + kTcP1 + 32 * hh, pp);
@@ -853,26 +866,18 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
           vk[u] = f[u] - BT[t] * EG[t] * pp[u] + ED[t] * p3[u];
         }
       }
-      // both CTAs are past batch 3, the Msym pass and the dot products: the
-      // exchange area is free in both, and this CTA's Q/K tiles are retired
-      cluster_arrive();
-      cluster_wait();
-      if (have_n && tid == 0) issue_qk(pn % kHQK, en.z);
-      const uint32_t rx = dsmem_map(s_base + SM::kMQ, static_cast<uint32_t>(crank ^ 1));
+    }
+    // the partner's area is free: send it the half it writes
+    wait_phase_cluster(bar_xfree, par, broken);
+    {
+      const uint32_t rx = dsmem_map(s_base + SM::kMQ, peer) + static_cast<uint32_t>(kk) * 256;
+      const uint32_t rbar = dsmem_map(bar_xfull, peer);
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const uint32_t o = static_cast<uint32_t>(((32 * hh + u) * kD + kk) * 4);
-        dsmem_st_f32(rx + o, crank ? vq[u] : vk[u]);
-      }
-      cluster_arrive();
-      cluster_wait();  // the partner's values have landed
-      const float *X = reinterpret_cast<const float *>(smem + SM::kMQ);
-      float *dst = crank ? dk : dq;
-#pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int t = 32 * hh + u;
-        if (t < L)
-          dst[((t0 + t) * kHQK + hqk) * kD + kk] = (crank ? vk[u] : vq[u]) + X[t * kD + kk];
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t chunk = static_cast<uint32_t>(8 * hh + (q ^ (kk & 7)));
+        const float4 v = crank ? make_float4(vq[4 * q], vq[4 * q + 1], vq[4 * q + 2], vq[4 * q + 3])
+                               : make_float4(vk[4 * q], vk[4 * q + 1], vk[4 * q + 2], vk[4 * q + 3]);
+        dsmem_st_async_v4(rx + chunk * 16, v, rbar);
       }
     }
 
@@ -902,6 +907,8 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       if (lane == 0) SC[12 + warp] = ez;
     }
     __syncthreads();
+    // every thread is past the dot products: the Q / K tiles are retired
+    if (have_n && tid == 0) issue_qk(pn % kHQK, en.z);
     if (tid < 64) {
       const int t = tid;
       if (t == L - 1) {
@@ -933,6 +940,22 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       db[idx] = dB * bt * (1.0f - bt);
       dgg_ws[idx] = dg * gt;
     }
+    // the partner's half has landed: add it to this CTA's own and write the rows
+    wait_phase_cluster(bar_xfull, par, broken);
+    {
+      const float *X = reinterpret_cast<const float *>(smem + SM::kMQ) + kk * 64;
+      float *dst = crank ? dk : dq;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 x = *reinterpret_cast<const float4 *>(X + 4 * (8 * hh + (q ^ (kk & 7))));
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int u = 4 * q + r, t = 32 * hh + u;
+          if (t < L) dst[((t0 + t) * kHQK + hqk) * kD + kk] = (crank ? vk[u] : vq[u]) + xs[r];
+        }
+      }
+    }
     // the next pair overwrites the gate vectors, the partial sums and TMEM
     tc_fence_before();
     __syncthreads();
@@ -942,6 +965,9 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     have = have_n;
     par ^= 1u;
   }
+  // neither CTA leaves while the other may still signal or store into it
+  cluster_arrive();
+  cluster_wait();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

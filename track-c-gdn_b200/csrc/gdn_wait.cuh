@@ -52,4 +52,28 @@ __device__ __forceinline__ bool wait_phase(uint32_t mbar, uint32_t parity, volat
   return wait_phase_slow(mbar, parity, broken);
 }
 
+// The same bounded wait, with acquire at cluster scope (phases completed by
+// the other CTA of a cluster).
+__device__ __noinline__ bool wait_phase_cluster_slow(uint32_t mbar, uint32_t parity,
+                                                     volatile int *broken) {
+  const long long t0 = clock64();
+  const long long limit = wait_limit_cycles();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_cluster(mbar, parity)) return true;
+    if (*broken) return false;
+    if (clock64() - t0 > limit) {
+      *broken = 1;
+      set_device_status(kDevStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ bool wait_phase_cluster(uint32_t mbar, uint32_t parity,
+                                                   volatile int *broken) {
+  if (mbar_try_wait_cluster(mbar, parity)) return true;
+  if (*broken) return false;
+  return wait_phase_cluster_slow(mbar, parity, broken);
+}
+
 }  // namespace gdn

@@ -278,8 +278,20 @@ __device__ __forceinline__ uint32_t dsmem_map(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ void dsmem_st_f32(uint32_t caddr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(caddr), "f"(v) : "memory");
+// Asynchronous 16-byte store into the shared memory of a CTA of the cluster
+// (`caddr`); its completion counts 16 transaction bytes on that CTA's
+// mbarrier `cmbar` (both shared::cluster addresses in the same CTA).
+__device__ __forceinline__ void dsmem_st_async_v4(uint32_t caddr, float4 v, uint32_t cmbar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+      ::"r"(caddr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(cmbar)
+      : "memory");
+}
+// Arrive (release at cluster scope) on the mbarrier at shared::cluster address
+// `caddr`, which may belong to another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr)
+               : "memory");
 }
 // Every thread of every CTA of the cluster arrives (release) / waits for all
 // of them (acquire); warp-uniform.
@@ -315,6 +327,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t saddr, uint32_t parity) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(saddr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// try_wait with acquire at cluster scope: for phases completed by another CTA
+// of the cluster (a remote arrive or remote asynchronous stores).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t saddr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(saddr), "r"(parity)
