@@ -453,6 +453,9 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // Mq and Msym come from (a) and (b) by element-wise work on the CUDA cores
 // between the two MMA batches.
 constexpr int kBwdTcThreads = 256;  // warps w and w + 4 share TMEM lanes 32 (w & 3) ..
+// The thread that issues the copies and the MMAs: lane 0 of warp 4, whose
+// share of the Mq pass (rows 0..31, columns 32..63) is structurally zero.
+constexpr int kBwdTcIssuer = 128;
 
 struct BwdTcSmem {
   static constexpr int kQK = 0;        // [Q;K]: 2 d-blocks x (64 Q rows | 64 K rows) x 128 B (TMA)
@@ -480,7 +483,7 @@ constexpr uint32_t kTcA = 0, kTcB = 64, kTcP1 = 192, kTcP2 = 256, kTcP3 = 320, k
                    kTcGH = 448, kTcCols = 512;
 // per-token vector slots and partial-sum families
 enum BwdVec : int {
-  kVG = 0, kVEG, kVBT, kVED, kVRowWq, kVRowWa, kVDbA, kVDXv, kVZeta, kVDG, kVDB
+  kVG = 0, kVEG, kVBT, kVED, kVRowWq, kVRowWa, kVDbA, kVDXv, kVZeta, kVDG, kVDB, kVEGL
 };
 enum BwdRed : int { kRedRho = 0, kRedXi, kRedZeta, kRedColWq, kRedColWa };
 
@@ -584,16 +587,20 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
   };
   // gate inputs of the next pair, loaded a pair ahead into registers (token
-  // tid < 64; zero past the chunk's end)
-  float nx_g = 0.f, nx_b = 0.f, nx_gc = 0.f;
+  // tid < 64; zero past the chunk's end): G, beta, G_C, x = a + dt_bias, A_log
+  float nx_g = 0.f, nx_b = 0.f, nx_gc = 0.f, nx_x = 0.f, nx_alog = 0.f;
   auto fetch_gates = [&](const int4 &en, int hvn) {
     if (tid < 64) {
       nx_gc = gcum_ws[(en.z + en.w - 1) * kHV + hvn];
+      nx_alog = A_log[hvn];
       nx_g = 0.f;
       nx_b = 0.f;
+      nx_x = 0.f;
       if (tid < en.w) {
-        nx_g = gcum_ws[(en.z + tid) * kHV + hvn];
-        nx_b = beta_ws[(en.z + tid) * kHV + hvn];
+        const int64_t idx = (en.z + tid) * kHV + hvn;
+        nx_g = gcum_ws[idx];
+        nx_b = beta_ws[idx];
+        nx_x = bf16_to_f32(a[idx]) + dt_bias[hvn];
       }
     }
   };
@@ -603,7 +610,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   bool have = live(p);
   int4 e = have ? chunk_tab[p / kHQK] : make_int4(0, 0, 0, 0);
   if (warp == 0) tmem_alloc(s_base + SM::kTmem, kTcCols);
-  if (tid == 0) {
+  if (tid == kBwdTcIssuer) {
     *broken = 0;
     for (int i = 0; i < 7; ++i) mbar_init(bar_qk + 8 * i, 1);
     mbar_init_fence();
@@ -636,14 +643,21 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     const int hv_n = 2 * (pn % kHQK) + crank;
 
     // the partner's 32 KB of dq / dk values for this pair land on xfull
-    if (tid == 0) mbar_arrive_expect_tx(bar_xfull, 32768);
+    if (tid == kBwdTcIssuer) mbar_arrive_expect_tx(bar_xfull, 32768);
     // ---- gates (inputs fetched a pair ahead) ----
+    // token tid's gate terms, kept for the gate gradients at the end: e^{A_log},
+    // d softplus / dx at x = a + dt_bias, and gl = -e^{A_log} softplus(x)
+    float g_ea = 0.f, g_sig = 0.f, g_gl = 0.f;
     if (tid < 64) {
       const float gg = nx_g, bt = nx_b;
+      g_ea = expf(nx_alog);
+      g_sig = 1.0f / (1.0f + expf(-nx_x));
+      g_gl = -g_ea * softplus_stable(nx_x);
       vec(kVG)[tid] = gg;
       vec(kVEG)[tid] = tid < L ? expf(gg) : 0.f;
       vec(kVBT)[tid] = bt;
       vec(kVED)[tid] = tid < L ? expf(nx_gc - gg) : 0.f;
+      vec(kVEGL)[tid] = tid < L ? expf(g_gl) : 1.f;
       if (tid == 0) SC[0] = expf(nx_gc);
     }
     __syncthreads();
@@ -653,19 +667,6 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // hold the next sequence's tokens: zero them (the images are zero there)
     wait_phase(bar_qk, par, broken);
     wait_phase(bar_rest, par, broken);
-    {  // <dS_C, S_0> (the images share one layout)
-      float sds = 0.f;
-      for (int idx = tid; idx < static_cast<int>(kStateImgBytes / 16); idx += kBwdTcThreads) {
-        float x[8], y[8];
-        unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kS0 + 16 * idx), x);
-        unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kDS + 16 * idx), y);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) sds += x[u] * y[u];
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sds += __shfl_xor_sync(0xffffffffu, sds, o);
-      if (lane == 0) SC[4 + warp] = sds;  // SC[4..11]
-    }
     if (L < kChunk) {
       const int nz = kChunk - L;
       for (int idx = tid; idx < 8 * nz * 8; idx += kBwdTcThreads) {
@@ -682,7 +683,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     tc_fence_after();
 
     // ---- MMA batch 1: (a), (b); batch 2: (c), (d), (e) ----
-    if (tid == 0) {
+    if (tid == kBwdTcIssuer) {
       const uint32_t id_kk = umma_idesc_bf16(128, 64, false, false);
       const uint32_t id_kk2 = umma_idesc_bf16(128, 128, false, false);
       const uint32_t id_mn = umma_idesc_bf16(128, 64, true, false);
@@ -709,35 +710,81 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       }
       umma_commit(bar_m2);
     }
+    // <dS_C, S_0> (the images share one layout) while batch 1 runs, on the
+    // warps other than the issuer's
+    if (warp != 4) {
+      float sds = 0.f;
+      const int r = tid < 128 ? tid : tid - 32;
+      for (int idx = r; idx < static_cast<int>(kStateImgBytes / 16); idx += kBwdTcThreads - 32) {
+        float x[8], y[8];
+        unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kS0 + 16 * idx), x);
+        unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kDS + 16 * idx), y);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sds += x[u] * y[u];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sds += __shfl_xor_sync(0xffffffffu, sds, o);
+      if (lane == 0) SC[4 + warp] = sds;  // SC[4..11]
+    } else if (lane == 0) {
+      SC[4 + warp] = 0.f;
+    }
 
     // ---- Mq, Ma and their gate terms: row i = TMEM lane, columns 32 hh.. ----
     wait_phase(bar_m1, par, broken);
     tc_fence_after();
-    {
+    if ((warp & 5) == 4) {
+      // warps 4 and 6: rows 0..31, columns 32..63 -- every j > i, so Mq, Ma,
+      // their row and column sums and dbA are zero there
+      const int i = lane;
+      if (warp == 4) {
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          *reinterpret_cast<uint4 *>(smem + SM::kMQ + i * 128 + (((4 + cc) ^ i) & 7) * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
+        ROW[(3 + 0) * 64 + i] = 0.f;
+        red(0, kRedColWq)[32 + lane] = 0.f;
+      } else {
+#pragma unroll
+        for (int u = 0; u < 32; ++u) MA[i * 65 + 32 + u] = 0.f;
+        ROW[(3 + 1) * 64 + i] = 0.f;
+        ROW[(3 + 2) * 64 + i] = 0.f;
+        red(2, kRedColWa)[32 + lane] = 0.f;
+      }
+    } else {
       const bool qside = quad < 2;  // lanes 0-63: QK, dO.delta; lanes 64-127: KK, dX.delta
       const int i = 32 * (quad & 1) + lane;
-      const float gi = vec(kVG)[i], bi = vec(kVBT)[i];
+      const float bi = vec(kVBT)[i];
       float rsum = 0.f, dba = 0.f;
       float m[32], w[32];
       tmem_ld32(tl + kTcA + 32 * hh, m);  // QK or KK
       tmem_ld32(tl + kTcB + 32 * hh, w);  // dO.delta or dX.delta
       tmem_wait_ld();
+      // e^{G_i - G_j} for the columns j <= i, right to left as a running
+      // product of the per-token decays e^{gl_j} (one exponential per row)
+      const int jt = 32 * hh + 31;
+      float dec = i > jt ? expf(vec(kVG)[i] - vec(kVG)[jt]) : 1.f;
+      const float4 *egl4 = reinterpret_cast<const float4 *>(vec(kVEGL) + 32 * hh);
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int j = 32 * hh + u;
-        const float dec = expf(gi - vec(kVG)[j]);
-        float x;
-        if (qside) {
-          x = (i < L && j <= i) ? scale * dec * w[u] : 0.f;  // Mq
-        } else {
-          const float dA = -w[u];
-          x = (i < L && j < i) ? dA * bi * dec : 0.f;  // Ma
-          if (i < L && j < i) dba += dA * dec * m[u];
-          MA[i * 65 + j] = x;
+      for (int q = 7; q >= 0; --q) {
+        const float4 e4 = egl4[q];
+        const float egl[4] = {e4.x, e4.y, e4.z, e4.w};
+#pragma unroll
+        for (int r = 3; r >= 0; --r) {
+          const int u = 4 * q + r, j = 32 * hh + u;
+          float x;
+          if (qside) {
+            x = (i < L && j <= i) ? scale * dec * w[u] : 0.f;  // Mq
+          } else {
+            const float dA = -w[u];
+            x = (i < L && j < i) ? dA * bi * dec : 0.f;  // Ma
+            if (i < L && j < i) dba += dA * dec * m[u];
+            MA[i * 65 + j] = x;
+          }
+          w[u] = x;
+          m[u] *= x;  // W = M o (QK or KK)
+          rsum += m[u];
+          if (j <= i) dec *= egl[r];  // column j - 1 next
         }
-        w[u] = x;
-        m[u] *= x;  // W = M o (QK or KK)
-        rsum += m[u];
       }
       if (qside) {  // row i of Mq, columns 32 hh .. 32 hh + 31, as bf16
 #pragma unroll
@@ -785,7 +832,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     tc_fence_after();
 
     // ---- MMA batch 3: (f) K^T Mq^T; (g) Q^T Mq, (h) + K^T Msym ----
-    if (tid == 0) {
+    if (tid == kBwdTcIssuer) {
       const uint32_t id_f = umma_idesc_bf16(128, 64, true, false);
       const uint32_t id_g = umma_idesc_bf16(128, 64, true, true);
       const uint64_t dk16 = umma_desc_sw128(s_base, 16, 1024);
@@ -811,7 +858,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // batch 2 is done: S_0, dS_C, [dO;dX] and [delta;V] are no longer read,
     // so the next pair's copies go there now and land while this pair runs
     if (have_n) {
-      if (tid == 0) issue_rest(pn / kHQK, hv_n, en.z);
+      if (tid == kBwdTcIssuer) issue_rest(pn / kHQK, hv_n, en.z);
       fetch_gates(en, hv_n);
     }
     {
@@ -842,7 +889,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     wait_phase(bar_m3, par, broken);
     tc_fence_after();
     // batch 3 and the Msym pass are done: this CTA's exchange area is free
-    if (tid == 0) mbar_arrive_cluster(dsmem_map(bar_xfree, peer));
+    if (tid == kBwdTcIssuer) mbar_arrive_cluster(dsmem_map(bar_xfree, peer));
     float vq[32], vk[32];
     {
       const float *EG = vec(kVEG), *BT = vec(kVBT), *ED = vec(kVED);
@@ -908,7 +955,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
     __syncthreads();
     // every thread is past the dot products: the Q / K tiles are retired
-    if (have_n && tid == 0) issue_qk(pn % kHQK, en.z);
+    if (have_n && tid == kBwdTcIssuer) issue_qk(pn % kHQK, en.z);
     if (tid < 64) {
       const int t = tid;
       if (t == L - 1) {
@@ -931,14 +978,10 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const int t = tid;
       const float dg = vec(kVDG)[t] + (t < 32 ? SC[14] : 0.f);
       const int64_t idx = (t0 + t) * kHV + hv;
-      const float x = bf16_to_f32(a[idx]) + dt_bias[hv];
-      const float ea = expf(A_log[hv]);
-      const float sig = 1.0f / (1.0f + expf(-x));  // d softplus / dx
-      const float gt = -ea * softplus_stable(x);
       const float bt = vec(kVBT)[t];
-      da[idx] = -dg * ea * sig;
+      da[idx] = -dg * g_ea * g_sig;
       db[idx] = dB * bt * (1.0f - bt);
-      dgg_ws[idx] = dg * gt;
+      dgg_ws[idx] = dg * g_gl;
     }
     // the partner's half has landed: add it to this CTA's own and write the rows
     wait_phase_cluster(bar_xfull, par, broken);
