@@ -708,25 +708,14 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
         umma_bf16(tmem + kTcP3, umma_desc_advance(dmn16k, SM::kDS + ks * 2048),
                   umma_desc_advance(dk16, SM::kDV + off), id_mn, ks > 0);
       }
+      // S_0^T dS_C into the F / GH columns (free until batch 3): its trace is
+      // <dS_C, S_0>
+      const uint32_t id_tr = umma_idesc_bf16(128, 128, true, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem + kTcF, umma_desc_advance(dmn16k, SM::kS0 + ks * 2048),
+                  umma_desc_advance(dmn16k, SM::kDS + ks * 2048), id_tr, ks > 0);
       umma_commit(bar_m2);
-    }
-    // <dS_C, S_0> (the images share one layout) while batch 1 runs, on the
-    // warps other than the issuer's
-    if (warp != 4) {
-      float sds = 0.f;
-      const int r = tid < 128 ? tid : tid - 32;
-      for (int idx = r; idx < static_cast<int>(kStateImgBytes / 16); idx += kBwdTcThreads - 32) {
-        float x[8], y[8];
-        unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kS0 + 16 * idx), x);
-        unpack8(*reinterpret_cast<const uint4 *>(smem + SM::kDS + 16 * idx), y);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) sds += x[u] * y[u];
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sds += __shfl_xor_sync(0xffffffffu, sds, o);
-      if (lane == 0) SC[4 + warp] = sds;  // SC[4..11]
-    } else if (lane == 0) {
-      SC[4 + warp] = 0.f;
     }
 
     // ---- Mq, Ma and their gate terms: row i = TMEM lane, columns 32 hh.. ----
@@ -810,6 +799,22 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const float cs = warp_transpose_sum32(m, lane);  // column 32 hh + lane over these 32 rows
       red(quad, qside ? kRedColWq : kRedColWa)[32 * hh + lane] = cs;
     }
+    // <dS_C, S_0>: the diagonal of S_0^T dS_C, lanes 32 quad .. of warp 4 + quad
+    // (batch 3 overwrites these columns after the next barrier)
+    if (hh == 1) {
+      wait_phase(bar_m2, par, broken);
+      tc_fence_after();
+      float x[32];
+      tmem_ld32(tl + kTcF + 32 * quad, x);
+      tmem_wait_ld();
+      float d = 0.f;
+#pragma unroll
+      for (int u = 0; u < 32; ++u) d = u == lane ? x[u] : d;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      if (lane == 0) SC[4 + quad] = d;  // SC[4..7]
+    }
+    tc_fence_before();
     __syncthreads();
     {  // Msym = Ma + Ma^T: row i = tid & 63, 16 columns per thread
       const int i = tid & 63, q4 = tid >> 6;
@@ -959,8 +964,8 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     if (tid < 64) {
       const int t = tid;
       if (t == L - 1) {
-        float sds = 0.f;  // <dS_C, S_0>, eight warp partials in a fixed order
-        for (int w8 = 0; w8 < 8; ++w8) sds += SC[4 + w8];
+        float sds = 0.f;  // <dS_C, S_0>, four warp partials in a fixed order
+        for (int w4 = 0; w4 < 4; ++w4) sds += SC[4 + w4];
         dG += SC[0] * sds + SC[12] + SC[13];
       }
       // dg_t = sum_{s >= t} dG_s: suffix scan within each warp, then warp 1's total into warp 0
