@@ -120,6 +120,21 @@ def test_autograd_wrapper_matches_direct_backward(gdn):
         assert torch.equal(leaf.grad, g[name].to(leaf.dtype).view_as(leaf)), name
 
 
+def test_backward_is_deterministic_with_many_pairs_per_cluster(gdn):
+    """The chunk-gradient kernel is persistent: each cluster of two CTAs walks
+    many (chunk, q/k head) pairs, fetching the next pair's operands while the
+    current one runs, and the two CTAs exchange their dq / dk halves.  On an
+    input with far more pairs than clusters, repeated calls must agree bit for
+    bit on every gradient (a missing barrier between two passes of one pair
+    shows up here as a few differing chunks)."""
+    args, d_out, d_final = _case(4242, [4096, 3000, 2500, 1800, 700, 64, 1, 5000], True, True)
+    runs = [gdn.prefill.backward(*args, None, d_out.cuda(), d_final.cuda()) for _ in range(4)]
+    for g in runs[1:]:
+        for name in NAMES:
+            if runs[0][name] is not None:
+                assert torch.equal(runs[0][name], g[name]), name
+
+
 def test_backward_reports_bad_seqlens(gdn):
     args, d_out, _ = _case(9, [64, 64], False, False)
     q, k, v, state, A_log, a, dt, b, cu = args

@@ -449,7 +449,8 @@ gdn_prefill_bwd_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
 // Every input arrives by TMA (Q, K, dO, V tiles) or bulk copy (the S_0,
 // dS_C, delta and dX images the recompute and the reverse scan wrote): the
 // images and the dO / V tiles as soon as batch 2 is done with the previous
-// pair's, the Q / K tiles once batch 3 and the dot products are.
+// pair's, the Q / K tiles once batch 3 and the dot products are, dS_C once the
+// dq / dk exchange that borrows its buffer is consumed.
 // Mq and Msym come from (a) and (b) by element-wise work on the CUDA cores
 // between the two MMA batches.
 constexpr int kBwdTcThreads = 256;  // warps w and w + 4 share TMEM lanes 32 (w & 3) ..
@@ -469,11 +470,11 @@ struct BwdTcSmem {
   static constexpr int kVec = kMA + 64 * 65 * 4;     // per-token vectors: 16 x 64 fp32
   static constexpr int kRed = kVec + 16 * 64 * 4;    // partials [4 lane quadrants][5][64] fp32
   static constexpr int kRow = kRed + 4 * 5 * 64 * 4;  // row-sum halves [2][3][64] fp32
-  // 7 mbarriers: qk, rest, m1, m2, m3, xfree, xfull
+  // 8 mbarriers: qk, rest, m1, m2, m3, xfree, xfull, ds
   static constexpr int kBar = kRow + 2 * 3 * 64 * 4;
-  static constexpr int kTmem = kBar + 56;
-  static constexpr int kBroken = kBar + 60;
-  static constexpr int kScal = kBar + 64;            // 16 fp32 scalars
+  static constexpr int kTmem = kBar + 64;
+  static constexpr int kBroken = kBar + 68;
+  static constexpr int kScal = kBar + 96;            // 16 fp32 scalars
   static constexpr int kBytes = kScal + 64 + 1024;   // + base alignment slack
 };
 static_assert(BwdTcSmem::kMA + 64 * 65 * 4 <= BwdTcSmem::kVec, "layout");
@@ -557,12 +558,14 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const uint32_t bar_qk = s_base + SM::kBar, bar_rest = bar_qk + 8, bar_m1 = bar_qk + 16,
                  bar_m2 = bar_qk + 24, bar_m3 = bar_qk + 32;
   // the dq / dk exchange: the partner arrives on xfree when its exchange area
-  // may be written; its stores into this CTA's area complete on xfull
-  const uint32_t bar_xfree = bar_qk + 40, bar_xfull = bar_qk + 48;
+  // may be written; its stores into this CTA's area complete on xfull.  The
+  // area is the dS_C image, whose copy for the next pair (bar_ds) is issued
+  // once the exchange is consumed.
+  const uint32_t bar_xfree = bar_qk + 40, bar_xfull = bar_qk + 48, bar_ds = bar_qk + 56;
   const uint32_t peer = static_cast<uint32_t>(crank ^ 1);
 
   // the copies of one pair's operands: the Q and K tiles (bar_qk); the dO and
-  // V tiles and the S_0, dS_C, delta and dX images (bar_rest)
+  // V tiles and the S_0, delta and dX images (bar_rest); the dS_C image (bar_ds)
   auto issue_qk = [&](int hqk, int64_t t0) {
     mbar_arrive_expect_tx(bar_qk, 32768);
     for (int blk = 0; blk < 2; ++blk) {
@@ -574,10 +577,9 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   auto issue_rest = [&](int g, int hv, int64_t t0) {
     const int64_t soff = (static_cast<int64_t>(g) * kHV + hv) * kStateImgBytes;
     const int64_t toff = (static_cast<int64_t>(g) * kHV + hv) * kTokImgBytes;
-    mbar_arrive_expect_tx(bar_rest, 32768 + 2 * static_cast<uint32_t>(kStateImgBytes) +
+    mbar_arrive_expect_tx(bar_rest, 32768 + static_cast<uint32_t>(kStateImgBytes) +
                                         2 * static_cast<uint32_t>(kTokImgBytes));
     bulk_load(s_base + SM::kS0, states_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_rest);
-    bulk_load(s_base + SM::kDS, dsc_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_rest);
     for (int blk = 0; blk < 2; ++blk) {
       const int y = static_cast<int>(t0);
       tma_load_2d(s_base + SM::kOX + blk * 16384, &tmap_do, hv * kD + 64 * blk, y, bar_rest);
@@ -585,6 +587,11 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       bulk_load(s_base + SM::kOX + blk * 16384 + 8192, dx_ws + toff + blk * 8192, 8192, bar_rest);
       bulk_load(s_base + SM::kDV + blk * 16384, delta_ws + toff + blk * 8192, 8192, bar_rest);
     }
+  };
+  auto issue_ds = [&](int g, int hv) {
+    const int64_t soff = (static_cast<int64_t>(g) * kHV + hv) * kStateImgBytes;
+    mbar_arrive_expect_tx(bar_ds, static_cast<uint32_t>(kStateImgBytes));
+    bulk_load(s_base + SM::kDS, dsc_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_ds);
   };
   // gate inputs of the next pair, loaded a pair ahead into registers (token
   // tid < 64; zero past the chunk's end): G, beta, G_C, x = a + dt_bias, A_log
@@ -612,11 +619,12 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   if (warp == 0) tmem_alloc(s_base + SM::kTmem, kTcCols);
   if (tid == kBwdTcIssuer) {
     *broken = 0;
-    for (int i = 0; i < 7; ++i) mbar_init(bar_qk + 8 * i, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(bar_qk + 8 * i, 1);
     mbar_init_fence();
     if (have) {
       issue_qk(p % kHQK, e.z);
       issue_rest(p / kHQK, 2 * (p % kHQK) + crank, e.z);
+      issue_ds(p / kHQK, 2 * (p % kHQK) + crank);
     }
   }
   if (have) fetch_gates(e, 2 * (p % kHQK) + crank);
@@ -631,7 +639,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
   const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
   const int kk = 32 * quad + lane;  // k index of this thread's TMEM lane (dots, dq, dk)
 
-  uint32_t par = 0;  // each of the seven barriers completes once per pair
+  uint32_t par = 0;  // each of the eight barriers completes once per pair
   while (have) {
     const int hqk = p % kHQK, hv = 2 * hqk + crank;
     const int64_t t0 = e.z;
@@ -705,6 +713,12 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
         const uint64_t s0 = umma_desc_advance(dmn16k, SM::kS0 + ks * 2048);
         umma_bf16(tmem + kTcP1, s0, umma_desc_advance(dk16, SM::kOX + off), id_mn, ks > 0);
         umma_bf16(tmem + kTcP2, s0, umma_desc_advance(dk16, SM::kOX + 8192 + off), id_mn, ks > 0);
+      }
+      wait_phase(bar_ds, par, broken);  // dS_C (issued after the previous pair's exchange)
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
         umma_bf16(tmem + kTcP3, umma_desc_advance(dmn16k, SM::kDS + ks * 2048),
                   umma_desc_advance(dk16, SM::kDV + off), id_mn, ks > 0);
       }
@@ -745,6 +759,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const float bi = vec(kVBT)[i];
       float rsum = 0.f, dba = 0.f;
       float m[32], w[32];
+      __syncwarp();
       tmem_ld32(tl + kTcA + 32 * hh, m);  // QK or KK
       tmem_ld32(tl + kTcB + 32 * hh, w);  // dO.delta or dX.delta
       tmem_wait_ld();
@@ -804,6 +819,9 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     if (hh == 1) {
       wait_phase(bar_m2, par, broken);
       tc_fence_after();
+      // batch 2 is done with dS_C: this CTA's exchange area is free
+      if (tid == kBwdTcIssuer) mbar_arrive_cluster(dsmem_map(bar_xfree, peer));
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the one-lane branches
       float x[32];
       tmem_ld32(tl + kTcF + 32 * quad, x);
       tmem_wait_ld();
@@ -866,6 +884,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       if (tid == kBwdTcIssuer) issue_rest(pn / kHQK, hv_n, en.z);
       fetch_gates(en, hv_n);
     }
+    __syncwarp();
     {
       const uint8_t *qtile = smem + SM::kQK + (kk >> 6) * 16384;
       const uint8_t *ktile = qtile + 8192;
@@ -886,15 +905,14 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // The two v-heads of q/k head hqk (this cluster's two CTAs) both add to
     // its dq and dk rows: rank 0 writes the dq rows and rank 1 the dk rows,
     // each adding the partner's contribution, which arrives by asynchronous
-    // stores into the retired Mq / Msym / Ma area as [128 k][64 t] fp32 (the
+    // stores into the retired dS_C image as [128 k][64 t] fp32 (the
     // 16-byte chunk t / 4 of row k at chunk (t / 4) ^ (k & 7): conflict-free
     // for the 16-byte accesses of consecutive k).  One fp32 sum of two terms
     // per element: the result does not depend on which CTA got there first,
     // and no zeroing pass or read-modify-write of dq / dk in DRAM is needed.
     wait_phase(bar_m3, par, broken);
     tc_fence_after();
-    // batch 3 and the Msym pass are done: this CTA's exchange area is free
-    if (tid == kBwdTcIssuer) mbar_arrive_cluster(dsmem_map(bar_xfree, peer));
+    __syncwarp();
     float vq[32], vk[32];
     {
       const float *EG = vec(kVEG), *BT = vec(kVBT), *ED = vec(kVED);
@@ -922,7 +940,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // the partner's area is free: send it the half it writes
     wait_phase_cluster(bar_xfree, par, broken);
     {
-      const uint32_t rx = dsmem_map(s_base + SM::kMQ, peer) + static_cast<uint32_t>(kk) * 256;
+      const uint32_t rx = dsmem_map(s_base + SM::kDS, peer) + static_cast<uint32_t>(kk) * 256;
       const uint32_t rbar = dsmem_map(bar_xfull, peer);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
@@ -934,6 +952,8 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
 
     // ---- gate gradients (tokens t = tid < 64, two warps) ----
+    // every warp's dot-product partials (red) are written
+    __syncthreads();
     float dG = 0.f, dB = 0.f, ez = 0.f;
     if (tid < 64) {
       const int t = tid;
@@ -991,7 +1011,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // the partner's half has landed: add it to this CTA's own and write the rows
     wait_phase_cluster(bar_xfull, par, broken);
     {
-      const float *X = reinterpret_cast<const float *>(smem + SM::kMQ) + kk * 64;
+      const float *X = reinterpret_cast<const float *>(smem + SM::kDS) + kk * 64;
       float *dst = crank ? dk : dq;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
@@ -1008,6 +1028,8 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // the exchange is consumed: the next pair's dS_C
+    if (have_n && tid == kBwdTcIssuer) issue_ds(pn / kHQK, hv_n);
     p = pn;
     e = en;
     have = have_n;
