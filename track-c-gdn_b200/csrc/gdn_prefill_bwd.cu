@@ -574,9 +574,11 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       tma_load_2d(s_base + SM::kQK + blk * 16384 + 8192, &tmap_k, hqk * kD + 64 * blk, y, bar_qk);
     }
   };
-  auto issue_rest = [&](int g, int hv, int64_t t0) {
+  // (bar_rest's copies in two halves, which two threads may issue: the barrier
+  // cannot complete before the first half's expect_tx arrival, whichever half's
+  // bytes land first)
+  auto issue_rest_a = [&](int g, int hv, int64_t t0) {  // expect_tx, S_0, dO and V tiles
     const int64_t soff = (static_cast<int64_t>(g) * kHV + hv) * kStateImgBytes;
-    const int64_t toff = (static_cast<int64_t>(g) * kHV + hv) * kTokImgBytes;
     mbar_arrive_expect_tx(bar_rest, 32768 + static_cast<uint32_t>(kStateImgBytes) +
                                         2 * static_cast<uint32_t>(kTokImgBytes));
     bulk_load(s_base + SM::kS0, states_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_rest);
@@ -584,6 +586,11 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       const int y = static_cast<int>(t0);
       tma_load_2d(s_base + SM::kOX + blk * 16384, &tmap_do, hv * kD + 64 * blk, y, bar_rest);
       tma_load_2d(s_base + SM::kDV + blk * 16384 + 8192, &tmap_v, hv * kD + 64 * blk, y, bar_rest);
+    }
+  };
+  auto issue_rest_b = [&](int g, int hv) {  // the dX and delta images
+    const int64_t toff = (static_cast<int64_t>(g) * kHV + hv) * kTokImgBytes;
+    for (int blk = 0; blk < 2; ++blk) {
       bulk_load(s_base + SM::kOX + blk * 16384 + 8192, dx_ws + toff + blk * 8192, 8192, bar_rest);
       bulk_load(s_base + SM::kDV + blk * 16384, delta_ws + toff + blk * 8192, 8192, bar_rest);
     }
@@ -594,20 +601,25 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     bulk_load(s_base + SM::kDS, dsc_ws + soff, static_cast<uint32_t>(kStateImgBytes), bar_ds);
   };
   // gate inputs of the next pair, loaded a pair ahead into registers (token
-  // tid < 64; zero past the chunk's end): G, beta, G_C, x = a + dt_bias, A_log
-  float nx_g = 0.f, nx_b = 0.f, nx_gc = 0.f, nx_x = 0.f, nx_alog = 0.f;
+  // tid < 64; zero past the chunk's end): G, beta, G_C, a (raw bf16), dt_bias,
+  // A_log -- only loaded here, used at the next pair's start, so that no
+  // arithmetic waits on the loads now
+  float nx_g = 0.f, nx_b = 0.f, nx_gc = 0.f, nx_dtb = 0.f, nx_alog = 0.f;
+  uint16_t nx_a = 0;
   auto fetch_gates = [&](const int4 &en, int hvn) {
     if (tid < 64) {
       nx_gc = gcum_ws[(en.z + en.w - 1) * kHV + hvn];
       nx_alog = A_log[hvn];
       nx_g = 0.f;
       nx_b = 0.f;
-      nx_x = 0.f;
+      nx_a = 0;
+      nx_dtb = 0.f;
       if (tid < en.w) {
         const int64_t idx = (en.z + tid) * kHV + hvn;
         nx_g = gcum_ws[idx];
         nx_b = beta_ws[idx];
-        nx_x = bf16_to_f32(a[idx]) + dt_bias[hvn];
+        nx_a = a[idx];
+        nx_dtb = dt_bias[hvn];
       }
     }
   };
@@ -623,7 +635,8 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     mbar_init_fence();
     if (have) {
       issue_qk(p % kHQK, e.z);
-      issue_rest(p / kHQK, 2 * (p % kHQK) + crank, e.z);
+      issue_rest_a(p / kHQK, 2 * (p % kHQK) + crank, e.z);
+      issue_rest_b(p / kHQK, 2 * (p % kHQK) + crank);
       issue_ds(p / kHQK, 2 * (p % kHQK) + crank);
     }
   }
@@ -658,9 +671,10 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     float g_ea = 0.f, g_sig = 0.f, g_gl = 0.f;
     if (tid < 64) {
       const float gg = nx_g, bt = nx_b;
+      const float x = bf16_to_f32(nx_a) + nx_dtb;  // a + dt_bias (0 past the end)
       g_ea = expf(nx_alog);
-      g_sig = 1.0f / (1.0f + expf(-nx_x));
-      g_gl = -g_ea * softplus_stable(nx_x);
+      g_sig = 1.0f / (1.0f + expf(-x));
+      g_gl = -g_ea * softplus_stable(x);
       vec(kVG)[tid] = gg;
       vec(kVEG)[tid] = tid < L ? expf(gg) : 0.f;
       vec(kVBT)[tid] = bt;
@@ -878,10 +892,13 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // ---- per-token dot products with q and k: thread = k (TMEM lane), tokens 32 hh.. ----
     wait_phase(bar_m2, par, broken);
     tc_fence_after();
-    // batch 2 is done: S_0, dS_C, [dO;dX] and [delta;V] are no longer read,
-    // so the next pair's copies go there now and land while this pair runs
+    // batch 2 is done: S_0, [dO;dX] and [delta;V] are no longer read, so the
+    // next pair's copies go there now and land while this pair runs (issued
+    // by lane 0 of warps 6 and 7, not by the MMA issuer's warp, which has the
+    // batch 3 MMAs to issue)
     if (have_n) {
-      if (tid == kBwdTcIssuer) issue_rest(pn / kHQK, hv_n, en.z);
+      if (tid == 192) issue_rest_a(pn / kHQK, hv_n, en.z);
+      if (tid == 224) issue_rest_b(pn / kHQK, hv_n);
       fetch_gates(en, hv_n);
     }
     __syncwarp();
