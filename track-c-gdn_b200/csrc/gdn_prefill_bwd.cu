@@ -969,11 +969,15 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
 
     // ---- gate gradients (tokens t = tid < 64, two warps) ----
-    // every warp's dot-product partials (red) are written
+    // every warp's dot-product partials (red) are written, and every thread is
+    // past the dot products: the Q / K tiles are retired
     __syncthreads();
-    float dG = 0.f, dB = 0.f, ez = 0.f;
-    if (tid < 64) {
+    if (have_n && tid == kBwdTcIssuer) issue_qk(pn % kHQK, en.z);
+    // warps 0 and 1 only, synchronised by a named barrier of their 64 threads,
+    // while the other warps go on to their dq / dk rows
+    if (warp < 2) {
       const int t = tid;
+      float dG = 0.f, dB = 0.f, ez = 0.f;
       float rho = 0.f, xi = 0.f, zeta = 0.f;
       for (int q = 0; q < 4; ++q) {
         rho += red(q, kRedRho)[t];
@@ -994,12 +998,7 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ez += __shfl_xor_sync(0xffffffffu, ez, o);
       if (lane == 0) SC[12 + warp] = ez;
-    }
-    __syncthreads();
-    // every thread is past the dot products: the Q / K tiles are retired
-    if (have_n && tid == kBwdTcIssuer) issue_qk(pn % kHQK, en.z);
-    if (tid < 64) {
-      const int t = tid;
+      asm volatile("bar.sync 1, 64;" ::: "memory");
       if (t == L - 1) {
         float sds = 0.f;  // <dS_C, S_0>, four warp partials in a fixed order
         for (int w4 = 0; w4 < 4; ++w4) sds += SC[4 + w4];
@@ -1014,16 +1013,14 @@ gdn_prefill_bwd_chunk_kernel(const __grid_constant__ CUtensorMap tmap_q,
       }
       if (t == 32) SC[14] = x;  // total of tokens 32..63
       vec(kVDG)[t] = x;
-    }
-    __syncthreads();
-    if (tid < L) {
-      const int t = tid;
-      const float dg = vec(kVDG)[t] + (t < 32 ? SC[14] : 0.f);
-      const int64_t idx = (t0 + t) * kHV + hv;
-      const float bt = vec(kVBT)[t];
-      da[idx] = -dg * g_ea * g_sig;
-      db[idx] = dB * bt * (1.0f - bt);
-      dgg_ws[idx] = dg * g_gl;
+      asm volatile("bar.sync 1, 64;" ::: "memory");
+      if (t < L) {
+        const float dg = vec(kVDG)[t] + (t < 32 ? SC[14] : 0.f);
+        const int64_t idx = (t0 + t) * kHV + hv;
+        da[idx] = -dg * g_ea * g_sig;
+        db[idx] = dB * bt * (1.0f - bt);
+        dgg_ws[idx] = dg * g_gl;
+      }
     }
     // the partner's half has landed: add it to this CTA's own and write the rows
     wait_phase_cluster(bar_xfull, par, broken);
