@@ -1002,9 +1002,10 @@ struct ScanSmemT {
   // [Q.db ; K.db] are the 128 N rows of MMA 1's B operand for d-block db.
   static constexpr int kQK0 = 0;
   static constexpr int kQK1 = 32768;
-  // [P ; Ainv] image: the forward's compact 10 KiB, the backward's full 16 KiB
+  // [P ; Ainv] image: the forward's compact 10 KiB; the backward's recompute
+  // (no outputs) only the Ainv half of its [PA ; Ainv] image, 8 KiB
   static constexpr int kM2 = 65536;
-  static constexpr int kM2Size = kSave ? 16384 : 10240;
+  static constexpr int kM2Size = kSave ? 8192 : 10240;
   // V tile: 2 v-blocks x 64 t rows x 128 B, 128-byte swizzle (the MN-major
   // A operand of the V MMA)
   static constexpr int kV = kM2 + kM2Size;
@@ -1167,13 +1168,17 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
     tma_load_2d(s_base + SM::kV, &tmap_v, hv * kD, y, bar_v);
     tma_load_2d(s_base + SM::kV + 8192, &tmap_v, hv * kD + 64, y, bar_v);
   };
-  // the backward's recompute reads the full [PA ; Ainv] image, the forward
-  // the compact [P ; Ainv] one
-  constexpr uint32_t kImgBytes = static_cast<uint32_t>(kSave ? kM2Bytes : kImgFwdBytes);
+  // the forward reads the compact [P ; Ainv] image; the backward's recompute,
+  // which forms no outputs, only the Ainv half (its second 8 KiB) of the
+  // [PA ; Ainv] image that the reverse scan reads whole
+  constexpr uint32_t kImgStride = static_cast<uint32_t>(kSave ? kM2Bytes : kImgFwdBytes);
+  constexpr uint32_t kImgOff = kSave ? 8192u : 0u;
+  constexpr uint32_t kImgLoad = kSave ? 8192u : static_cast<uint32_t>(kImgFwdBytes);
   auto issue_m2 = [&](int c) {
-    mbar_arrive_expect_tx(bar_m2, kImgBytes);
-    bulk_load(s_base + SM::kM2, m2_ws + (static_cast<int64_t>(gbase + c) * kHV + hv) * kImgBytes,
-              kImgBytes, bar_m2);
+    mbar_arrive_expect_tx(bar_m2, kImgLoad);
+    bulk_load(s_base + SM::kM2,
+              m2_ws + (static_cast<int64_t>(gbase + c) * kHV + hv) * kImgStride + kImgOff,
+              kImgLoad, bar_m2);
   };
   // Gates of chunk c for token gt = tid - 64 (threads 64..127, warps 2 and 3:
   // thread 0, which issues the MMAs and copies, has no part in them): fetched
@@ -1480,7 +1485,7 @@ gdn_prefill_scan_kernel(const __grid_constant__ CUtensorMap tmap_q,
         wait_phase(bar_m2, ph_m2, broken);
         tc_fence_after();
         if constexpr (kSave) {
-          const uint64_t da = umma_desc_sw128(m2buf + 8192, 16, 1024);
+          const uint64_t da = umma_desc_sw128(m2buf, 16, 1024);  // Ainv (swizzled, 1024-aligned)
   #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             umma_bf16_ts(tmem + SM::kColVn, tmem + SM::kColX + 32 * (ks >> 1) + 8 * (ks & 1),
