@@ -267,7 +267,10 @@ constexpr int kMtpRowsPerWarp = 8;
 constexpr int kMtpRowsPerCta = kDecWarps * kMtpRowsPerWarp;  // 64
 constexpr int kMtpCtasPerHead = kD / kMtpRowsPerCta;         // 2
 
-template <bool kBf16State>
+// kInter: the per-token states are written (`inter` non-null); the
+// instantiation without them keeps that pointer and its addressing out of the
+// token loop's registers.
+template <bool kBf16State, bool kInter>
 __global__ void __launch_bounds__(kDecWarps * 32, 4)
 gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
                       const uint16_t *__restrict__ v,
@@ -355,7 +358,7 @@ gdn_decode_mtp_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict
     for (int i = 0; i < R; ++i) {
       const float delta = beta * (vv[i] - old[i]);
       o[i] = update_dot(s[i], delta, kxy, kzw, qxy, qzw);
-      if (inter != nullptr)
+      if constexpr (kInter)
         IO::store(inter + ((tok * kHV + hv) * kD + row0 + i) * kD, lane, to_float4(s[i]));
       // a bf16 state carries its rounded value into the next token, as T
       // separate steps would (the output above used the unrounded update)
@@ -381,7 +384,9 @@ cudaError_t launch_decode_mtp(const void *q, const void *k, const void *v, const
   if (batch == 0) return cudaSuccess;
   const int64_t blocks = batch * kHV * kMtpCtasPerHead;
   const size_t smem = static_cast<size_t>(num_tokens) * (80 * sizeof(uint2) + 2 * sizeof(float));
-  gdn_decode_mtp_kernel<false><<<static_cast<unsigned>(blocks), kDecWarps * 32, smem, stream>>>(
+  auto kernel = inter != nullptr ? gdn_decode_mtp_kernel<false, true>
+                                 : gdn_decode_mtp_kernel<false, false>;
+  kernel<<<static_cast<unsigned>(blocks), kDecWarps * 32, smem, stream>>>(
       static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
       static_cast<const uint16_t *>(v), state, A_log, static_cast<const uint16_t *>(a), dt_bias,
       static_cast<const uint16_t *>(b), scale, num_tokens, static_cast<uint16_t *>(out),
@@ -409,7 +414,7 @@ cudaError_t launch_decode_bf16_state(const void *q, const void *k, const void *v
   }
   const int64_t blocks = batch * kHV * kMtpCtasPerHead;
   const size_t smem = static_cast<size_t>(num_tokens) * (80 * sizeof(uint2) + 2 * sizeof(float));
-  gdn_decode_mtp_kernel<true><<<static_cast<unsigned>(blocks), kDecWarps * 32, smem, stream>>>(
+  gdn_decode_mtp_kernel<true, false><<<static_cast<unsigned>(blocks), kDecWarps * 32, smem, stream>>>(
       static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
       static_cast<const uint16_t *>(v), st, A_log, static_cast<const uint16_t *>(a), dt_bias,
       static_cast<const uint16_t *>(b), scale, num_tokens, static_cast<uint16_t *>(out), st,
