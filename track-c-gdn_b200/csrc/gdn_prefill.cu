@@ -596,38 +596,20 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
   }
 
-  // Gates for v-heads 2*hqk + j (j = tid / 64), token t = tid % 64, while the
-  // tile is in flight.
-  {
-    const int j = tid >> 6, t = tid & 63, hv = 2 * hqk + j;
-    const bool valid = t < L;
-    float gl = 0.f, bt = 0.f;
-    if (valid) {
-      const int64_t idx = (t0 + t) * kHV + hv;
-      gl = -expf(A_log[hv]) * softplus_stable(bf16_to_f32(a[idx]) + dt_bias[hv]);
-      bt = 1.0f / (1.0f + expf(-bf16_to_f32(b[idx])));
-    }
-    float x = gl;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) wt[warp] = x;
-    __syncthreads();
-    if (warp & 1) x += wt[warp - 1];
-    Gs[j * 64 + t] = x;
-    Bs[j * 64 + t] = bt;
-    // per-token decay e^{gl_t} (1 past the end), stored one slot down so that
-    // gnext[c] = e^{gl_{c+1}}: the factor that extends a row's running decay
-    // product from column c+1 to column c
-    Gn[j * 64 + (t == 0 ? 63 : t - 1)] = t == 0 ? 1.f : expf(gl);
-    if (valid) {
-      const int64_t idx = (t0 + t) * kHV + hv;
-      gcum_ws[idx] = x;
-      beta_ws[idx] = bt;
-    }
+  // Gate inputs of token t = tid % 64 for v-head 2 hqk + tid / 64 (zero past
+  // the chunk's end): loaded now, turned into the gates while MMA 1 runs.
+  const int gj = tid >> 6, gt = tid & 63, ghv = 2 * hqk + gj;
+  const bool gvalid = gt < L;
+  uint16_t g_a = 0, g_b = 0;
+  const float g_alog = A_log[ghv], g_dtb = dt_bias[ghv];
+  if (gvalid) {
+    const int64_t idx = (t0 + gt) * kHV + ghv;
+    g_a = a[idx];
+    g_b = b[idx];
   }
+  // thread 0's mbarrier initialisation (and *broken = 0) before any thread
+  // polls the barrier
+  __syncthreads();
 
   wait_phase(bar_tma, 0, broken);
   if (L < kChunk) {
@@ -655,6 +637,39 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     }
     umma_commit(bar);
   }
+  // Gates for v-heads 2*hqk + j (j = tid / 64), token t = tid % 64, while the
+  // MMA runs.
+  {
+    const int j = gj, t = gt;
+    const bool valid = gvalid;
+    float gl = 0.f, bt = 0.f;
+    if (valid) {
+      gl = -expf(g_alog) * softplus_stable(bf16_to_f32(g_a) + g_dtb);
+      bt = 1.0f / (1.0f + expf(-bf16_to_f32(g_b)));
+    }
+    float x = gl;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wt[warp] = x;
+    __syncthreads();
+    if (warp & 1) x += wt[warp - 1];
+    Gs[j * 64 + t] = x;
+    Bs[j * 64 + t] = bt;
+    // per-token decay e^{gl_t} (1 past the end), stored one slot down so that
+    // gnext[c] = e^{gl_{c+1}}: the factor that extends a row's running decay
+    // product from column c+1 to column c
+    Gn[j * 64 + (t == 0 ? 63 : t - 1)] = t == 0 ? 1.f : expf(gl);
+    if (valid) {
+      const int64_t idx = (t0 + t) * kHV + ghv;
+      gcum_ws[idx] = x;
+      beta_ws[idx] = bt;
+    }
+  }
+  // the gates (Gs, Bs, Gn) are read by the A/P rows after the barrier below
+  __syncthreads();
   wait_phase(bar, 0, broken);
   tc_fence_after();
 
