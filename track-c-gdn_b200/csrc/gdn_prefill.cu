@@ -889,14 +889,17 @@ gdn_prefill_prep_kernel(const __grid_constant__ CUtensorMap tmap_q,
     // (128-byte-swizzled rows in shared memory) -> the compact image's second
     // matrix, one 16-byte piece per iteration, consecutive in global memory
     uint8_t *img0 = m2_ws + (static_cast<size_t>(gchunk) * kHV + 2 * hqk) * kImgFwdBytes + kTriBytes;
-    constexpr int kPieces = static_cast<int>(kTriBytes / 16);  // 320 per matrix
-    for (int idx = tid; idx < 2 * kPieces; idx += kPrepThreads) {
-      const int j = idx >= kPieces, q = idx - j * kPieces;
-      const int ks = q < 128 ? 0 : q < 224 ? 1 : q < 288 ? 2 : 3;
-      const int qb = q - static_cast<int>(tri_step_off(ks) >> 4);
-      const int t = 16 * ks + (qb >> 4) * 8 + (qb & 7), cc = 2 * ks + ((qb >> 3) & 1);
-      reinterpret_cast<uint4 *>(img0 + j * kImgFwdBytes)[q] =
-          *reinterpret_cast<const uint4 *>(ai + j * 8192 + sw128(t, cc));
+    // K-step by K-step (compile-time bounds): step ks holds rows 16 ks .. 63,
+    // (64 - 16 ks) x 2 pieces per matrix
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const int n = (64 - 16 * ks) * 2, base = static_cast<int>(tri_step_off(ks) >> 4);
+      for (int idx = tid; idx < 2 * n; idx += kPrepThreads) {
+        const int j = idx >= n, qb = idx - j * n;
+        const int t = 16 * ks + (qb >> 4) * 8 + (qb & 7), cc = 2 * ks + ((qb >> 3) & 1);
+        reinterpret_cast<uint4 *>(img0 + j * kImgFwdBytes)[base + qb] =
+            *reinterpret_cast<const uint4 *>(ai + j * 8192 + sw128(t, cc));
+      }
     }
     tc_fence_before();
     __syncthreads();
